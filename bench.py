@@ -1,0 +1,367 @@
+"""EM-iteration throughput benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+A step is one full soft-EM iteration (prepare, fused E+M statistics,
+allreduce when N > 1, finalize) over the configuration's whole synthetic
+dataset, which is resident in HBM and sharded by rows across the ranks
+(strong scaling: the total N is the configuration's N at every GPU count).
+Default workload: configs[1] of BASELINE.json -- diagonal GMM, bf16 X with fp32
+accumulation, N = 50,000,000, D = 64, K = 512.
+
+``value``  samples/s per EM iteration, device-timed (CUDA events on the compute
+           stream, barrier + synchronize on both sides, max over ranks).
+``e2e``    the same metric through the public streamed API: X in pinned host
+           memory, every step copies its rows host->device (double-buffered
+           copy stream overlapping the kernels) and reads the fitted
+           parameters and lower bound back to the host.
+``roofline`` the dominant kernel launch (gmmxx_em_accumulate) against the
+           measured bf16 tensor peak, algorithmic FLOPs only.
+``cpu_baseline`` the numpy oracle port of the reference's torch path on the
+           host cores, on a bounded row sample, rank 0 at N = 1.
+
+``--impl reference`` times that CPU port alone (the reference's own
+implementation is PyTorch code that cannot travel to the GPU host).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+
+def algorithmic_flops(cov: str, n: int, d: int, k: int) -> float:
+    """Per-iteration algorithmic FLOPs of the E-step logit contraction plus the
+    M-step statistics contraction (expanded-distance form, one pass each)."""
+    if cov == "diag":
+        return 2.0 * n * k * (2 * d) + 2.0 * n * k * (2 * d + 1)
+    if cov == "spherical":
+        return 2.0 * n * k * d + 2.0 * n * k * (d + 2)
+    if cov == "tied":
+        return 2.0 * n * k * d + 2.0 * n * d * d + 2.0 * n * k * (d + 1)
+    q = d * (d + 1) // 2
+    return 2.0 * n * k * (d + q) + 2.0 * n * k * (1 + d + q)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16": p["bf16_tflops"], "bf16_sus": p["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sus": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(cfg, mix, init, rows: int, iters: int = 1):
+    """The oracle (numpy port of the reference torch path) on a bounded sample."""
+    import torch
+
+    import oracle
+    from gmmxx_b200 import synthetic
+
+    x = synthetic.sample_rows(cfg, mix, rows, torch.device("cpu"), seed=12345).float().numpy()
+    means, cov, w = init
+    t0 = time.perf_counter()
+    oracle.fit(cfg.cov_type, x, cfg.K, iters, 0.0, means, cov, w, compute_labels=False)
+    dt = time.perf_counter() - t0
+    return {"value": rows * cfg.B * iters / dt, "unit": "samples/s", "cores": os.cpu_count(),
+            "kind": "port", "sample": f"{cfg.B}x{rows} rows of config {cfg.index}, {iters} EM iteration(s), "
+                                      f"numpy float32 on {os.cpu_count()} host threads, {dt:.2f} s"}
+
+
+def run_reference(args, cfg):
+    """--impl reference: the CPU port timed per step on bounded samples."""
+    from gmmxx_b200 import synthetic
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    mix = synthetic.mixture_params(cfg)
+    init = synthetic.initial_params(cfg, mix)
+    rows = args.ref_rows
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(cfg, mix, init, rows)
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(cfg, mix, init, rows)["value"])
+    v = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": "EM samples/s per iteration", "value": v, "unit": "samples/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * rows * cfg.B / v,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(cfg, args),
+        "cpu_baseline": {"value": v, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{cfg.B}x{rows} rows per step, 1 EM iteration, numpy float32"},
+        "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(cfg, args):
+    names = {0: "configs[0] spherical", 1: "configs[1] diag", 2: "configs[2] tied", 3: "configs[3] full",
+             4: "configs[4] spherical large-K"}
+    return {"workload": f"{names[cfg.index]} GMM EM iteration", "covariance_type": cfg.cov_type,
+            "x_dtype": str(cfg.dtype).replace("torch.", ""), "B": cfg.B, "N": cfg.N, "D": cfg.D, "K": cfg.K,
+            "parallelism": f"dp{args.gpus} (rows sharded, stats allreduce)",
+            "l2": "inputs larger than L2 (126 MB); no flush needed"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=0, help="override total N (smaller runs)")
+    ap.add_argument("--ref-rows", type=int, default=200_000)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from gmmxx_b200 import synthetic
+
+    cfg = synthetic.CONFIGS[args.config]
+    if args.n:
+        cfg = synthetic.Config(cfg.index, cfg.cov_type, cfg.dtype, cfg.B, args.n, cfg.D, cfg.K, cfg.iters)
+    if args.impl == "reference":
+        run_reference(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from gmmxx_b200 import _native as nat
+    from gmmxx_b200 import engine, large_n
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    comm = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        comm = engine.Comm()
+    nat.load()
+
+    mix = synthetic.mixture_params(cfg)
+    init_means, init_cov, init_w = synthetic.initial_params(cfg, mix)
+    n_local = cfg.N // world + (1 if rank < cfg.N % world else 0)
+    x = synthetic.sample_rows(cfg, mix, n_local, dev, seed=1000 + rank)
+    torch.cuda.synchronize()
+
+    means, cov, weights, _ = engine.initial_parameters(
+        cfg.cov_type, x, cfg.K, torch.from_numpy(init_means), torch.from_numpy(init_cov),
+        torch.from_numpy(init_w), 1e-6)
+    ops = engine.CudaOps(cfg.cov_type, x, cfg.K)
+    B, D, K = cfg.B, cfg.D, cfg.K
+    stats = torch.zeros((B, K, ops.stat_width), dtype=torch.float32, device=dev)
+    ll = torch.zeros((1,), dtype=torch.float64, device=dev)
+    lb = torch.zeros((1,), dtype=torch.float32, device=dev)
+    xx = None
+    if cfg.cov_type == "tied":
+        xx = torch.zeros((B, D, D), dtype=torch.float32, device=dev)
+        ops.xx_total(xx)
+        if comm:
+            comm.allreduce_(xx)
+    stream = torch.cuda.current_stream(dev)
+    ev_acc = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+
+    def step(i=None):
+        ops.prepare(means, cov, weights, 1e-6, 1e-8)
+        stats.zero_()
+        ll.zero_()
+        if i is not None:
+            ev_acc[i][0].record(stream)
+        ops.accumulate(stats, ll)
+        if i is not None:
+            ev_acc[i][1].record(stream)
+        if comm:
+            comm.allreduce_(stats)
+            comm.allreduce_(ll)
+        ops.finalize(cfg.N, stats, ll, xx, 1e-6, 1e-8, means, cov, weights, lb)
+
+    for _ in range(args.warmup):
+        step()
+    sampler = ClockSampler(local)
+    if comm:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if comm:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    acc_ms = sum(a.elapsed_time(b) for a, b in ev_acc) / args.steps
+    ms_t = torch.tensor([ms, acc_ms], dtype=torch.float64, device=dev)
+    if comm:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, acc_ms = float(ms_t[0]), float(ms_t[1])
+    ops.check_status()
+    value = cfg.N * cfg.B / (ms / 1e3)
+
+    # --- end to end through the streamed public API (host-resident X) -------
+    e2e = None
+    if not args.no_e2e and cfg.B == 1:
+        x_host = torch.empty((1, n_local, D), dtype=cfg.dtype, pin_memory=True)
+        x_host.copy_(x)
+        del x, ops
+        torch.cuda.empty_cache()
+        chunk = 1 << 22
+        streamer = large_n.ChunkStreamer(x_host, chunk, dev)
+        m2, c2, w2, _ = engine.initial_parameters(cfg.cov_type, streamer.bufs[0][:, :1], cfg.K,
+                                                  torch.from_numpy(init_means), torch.from_numpy(init_cov),
+                                                  torch.from_numpy(init_w), 1e-6)
+        ops2 = engine.CudaOps(cfg.cov_type, streamer.bufs[0], cfg.K)
+        host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (m2, c2, w2, lb)]
+
+        def e2e_step():
+            ops2.prepare(m2, c2, w2, 1e-6, 1e-8)
+            stats.zero_()
+            ll.zero_()
+            for xc, _ in streamer.chunks():
+                nat.call("gmmxx_em_accumulate", ops2.covc, ops2.xdt, xc.data_ptr(), 1, xc.shape[1], D, K,
+                         ops2.ws.data_ptr(), ops2.ws.numel(), stats.data_ptr(), ll.data_ptr(), ops2.stream)
+            if comm:
+                comm.allreduce_(stats)
+                comm.allreduce_(ll)
+            ops2.finalize(cfg.N, stats, ll, xx, 1e-6, 1e-8, m2, c2, w2, lb)
+            for h, t in zip(host_out, (m2, c2, w2, lb)):
+                h.copy_(t, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        if comm:
+            dist.barrier()
+        torch.cuda.synchronize()
+        streamer.h2d_bytes = 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if comm:
+            dist.barrier()
+        ems = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+        if comm:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": cfg.N * cfg.B / (float(ems[0]) / 1e3), "unit": "samples/s",
+               "h2d_bytes_per_step": streamer.h2d_bytes // args.steps,
+               "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in host_out),
+               "path": "gmmxx_b200.large_n streamed host-resident X (pinned, 4M-row double buffer)"}
+
+    if rank == 0:
+        peaks = load_peaks()
+        flops = algorithmic_flops(cfg.cov_type, n_local * cfg.B, D, K)
+        achieved = flops / (acc_ms / 1e3) / 1e12
+        long_run = ms * args.steps > 1000.0
+        peak = peaks["bf16_sus"] if long_run else peaks["bf16"]
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tpath):
+            with open(tpath) as f:
+                tr = json.load(f).get(f"config{cfg.index}")
+            if tr:
+                traffic = tr["bytes_per_row"] * n_local * cfg.B
+        line = {
+            "metric": "EM samples/s per iteration", "value": value, "unit": "samples/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(cfg, args),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "gmmxx_em_accumulate (rows_kernel + mstep_kernel)",
+                         "peak_source": f"{peaks['source']} bf16 {'sustained' if long_run else 'burst'}",
+                         "algorithmic_flops_per_launch": flops, "launch_ms": acc_ms,
+                         "hbm_frac": (n_local * cfg.B * D * torch.empty((), dtype=cfg.dtype).element_size()) /
+                                     (acc_ms / 1e3) / 1e9 / peaks["hbm_gbs"]},
+            "clocks": clocks,
+            "gpu_launches": args.steps * (5 + (2 if cfg.cov_type in ("tied", "full") else 0)),
+            "e2e": e2e,
+        }
+        if world == 1 and not args.no_cpu:
+            try:
+                line["cpu_baseline"] = cpu_baseline(cfg, mix, (init_means, init_cov, init_w), args.ref_rows)
+            except Exception as exc:  # report, never fake
+                line["cpu_baseline"] = {"error": repr(exc)}
+        print(json.dumps(line), flush=True)
+    if comm:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

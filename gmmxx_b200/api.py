@@ -1,0 +1,186 @@
+"""Functional API with the reference's signatures, served by the CUDA engine.
+
+``batch_gmm_{Spherical,Diagonal,Tied,Full}`` keep the argument names, order,
+defaults and return value ``(labels, means, covariances, weights, info)`` of
+the reference (gmmxx/torch_fallback.py:3339-3513).  Arguments that only steer
+the reference's Triton / chunking heuristics (``chunk_size_N``,
+``chunk_size_K``, ``kmeans_*``, ``use_triton``) are accepted and validated but
+do not change the result: the engine streams rows and components itself.
+``approx_top_k`` (approximate top-k EM) is not part of this engine and raises.
+
+Inference functions mirror the reference's ``*_torch_native_chunked``
+functions (torch_fallback.py:780-1345) without the torch-specific suffix.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import engine
+
+
+def _validate(x, n_components, max_iters, chunk_size_N, chunk_size_K, min_weight, approx_top_k):
+    if not torch.is_tensor(x) or x.ndim != 3:
+        raise ValueError("x must have shape (B, N, D)")
+    if n_components <= 0:
+        raise ValueError("n_components must be positive")
+    if x.shape[1] == 0:
+        raise ValueError("x must contain at least one sample")
+    if max_iters <= 0:
+        raise ValueError("max_iters must be positive")
+    if chunk_size_N <= 0 or chunk_size_K <= 0:
+        raise ValueError("chunk_size_N and chunk_size_K must be positive")
+    if min_weight <= 0.0:
+        raise ValueError("min_weight must be positive")
+    if approx_top_k is not None and int(approx_top_k) < int(n_components):
+        raise NotImplementedError("approximate top-k EM is not implemented by the gmmxx_b200 engine")
+
+
+def _fit(cov_type, x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
+         init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k):
+    _validate(x, n_components, max_iters, chunk_size_N, chunk_size_K, min_weight, approx_top_k)
+    return engine.em_fit(
+        cov_type, x, n_components, max_iters=max_iters, tol=tol, init_means=init_means,
+        init_variances=init_variances, init_weights=init_weights, init_params=init_params,
+        reg_covar=reg_covar, min_weight=min_weight, compute_labels=compute_labels, verbose=verbose)
+
+
+def batch_gmm_Spherical(
+    x: torch.Tensor,
+    n_components: int,
+    max_iters: int = 100,
+    tol: float = 1e-4,
+    init_means: Optional[torch.Tensor] = None,
+    init_variances: Optional[torch.Tensor] = None,
+    init_weights: Optional[torch.Tensor] = None,
+    verbose: bool = False,
+    *,
+    init_params: str = "kmeans",
+    reg_covar: float = 1e-6,
+    chunk_size_N: int = 32768,
+    chunk_size_K: int = 1024,
+    kmeans_init_iters: int = 10,
+    kmeans_init_tol: float = 1e-4,
+    use_triton: bool = True,
+    min_weight: float = 1e-8,
+    compute_labels: bool = True,
+    approx_top_k: Optional[int] = None,
+):
+    """Spherical soft EM (reference: torch_fallback.py:3339-3380, loop 1897-2397)."""
+    return _fit("spherical", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+
+
+def batch_gmm_Diagonal(
+    x: torch.Tensor,
+    n_components: int,
+    max_iters: int = 100,
+    tol: float = 1e-4,
+    init_means: Optional[torch.Tensor] = None,
+    init_variances: Optional[torch.Tensor] = None,
+    init_weights: Optional[torch.Tensor] = None,
+    verbose: bool = False,
+    *,
+    init_params: str = "kmeans",
+    reg_covar: float = 1e-6,
+    chunk_size_N: int = 32768,
+    chunk_size_K: int = 1024,
+    kmeans_init_iters: int = 10,
+    kmeans_init_tol: float = 1e-4,
+    use_triton: bool = True,
+    min_weight: float = 1e-8,
+    compute_labels: bool = True,
+    approx_top_k: Optional[int] = None,
+):
+    """Diagonal soft EM (reference: torch_fallback.py:3383-3424, loop 2401-2728)."""
+    return _fit("diag", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+
+
+def batch_gmm_Full(
+    x: torch.Tensor,
+    n_components: int,
+    max_iters: int = 100,
+    tol: float = 1e-4,
+    init_means: Optional[torch.Tensor] = None,
+    init_variances: Optional[torch.Tensor] = None,
+    init_weights: Optional[torch.Tensor] = None,
+    verbose: bool = False,
+    *,
+    init_params: str = "kmeans",
+    reg_covar: float = 1e-6,
+    chunk_size_N: int = 32768,
+    chunk_size_K: int = 1024,
+    kmeans_init_iters: int = 10,
+    kmeans_init_tol: float = 1e-4,
+    use_triton: bool = True,
+    min_weight: float = 1e-8,
+    compute_labels: bool = True,
+    approx_top_k: Optional[int] = None,
+):
+    """Full-covariance soft EM (reference: torch_fallback.py:3427-3468, loop 2732-3244)."""
+    return _fit("full", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+
+
+def batch_gmm_Tied(
+    x: torch.Tensor,
+    n_components: int,
+    max_iters: int = 100,
+    tol: float = 1e-4,
+    init_means: Optional[torch.Tensor] = None,
+    init_variances: Optional[torch.Tensor] = None,
+    init_weights: Optional[torch.Tensor] = None,
+    verbose: bool = False,
+    *,
+    init_params: str = "kmeans",
+    reg_covar: float = 1e-6,
+    chunk_size_N: int = 32768,
+    chunk_size_K: int = 1024,
+    kmeans_init_iters: int = 10,
+    kmeans_init_tol: float = 1e-4,
+    use_triton: bool = True,
+    min_weight: float = 1e-8,
+    compute_labels: bool = True,
+    approx_top_k: Optional[int] = None,
+):
+    """Tied-covariance soft EM (reference: torch_fallback.py:3471-3512, loop 2732-3244)."""
+    return _fit("tied", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+
+
+batch_gmm_spherical = batch_gmm_Spherical
+batch_gmm_diagonal = batch_gmm_Diagonal
+batch_gmm_diag = batch_gmm_Diagonal
+batch_gmm_full = batch_gmm_Full
+batch_gmm_tied = batch_gmm_Tied
+
+
+# --- inference (torch_fallback.py:780-1345) ----------------------------------
+
+
+def _inf(fn, cov_type):
+    def run(x, means, covariances, weights, *, chunk_size_N: int = 32768, chunk_size_K: int = 1024):
+        if chunk_size_N <= 0 or chunk_size_K <= 0:
+            raise ValueError("chunk_size_N and chunk_size_K must be positive")
+        return fn(cov_type, x, means, covariances, weights)
+
+    run.__name__ = f"{cov_type}_{fn.__name__}"
+    run.__doc__ = f"{fn.__doc__} ({cov_type} covariance)"
+    return run
+
+
+spherical_assign = _inf(engine.assign, "spherical")
+spherical_score_samples = _inf(engine.score_samples, "spherical")
+spherical_predict_proba = _inf(engine.predict_proba, "spherical")
+diagonal_assign = _inf(engine.assign, "diag")
+diagonal_score_samples = _inf(engine.score_samples, "diag")
+diagonal_predict_proba = _inf(engine.predict_proba, "diag")
+tied_assign = _inf(engine.assign, "tied")
+tied_score_samples = _inf(engine.score_samples, "tied")
+tied_predict_proba = _inf(engine.predict_proba, "tied")
+full_assign = _inf(engine.assign, "full")
+full_score_samples = _inf(engine.score_samples, "full")
+full_predict_proba = _inf(engine.predict_proba, "full")

@@ -1,0 +1,262 @@
+// capi.cu -- the extern "C" boundary (include/gmmxx_b200.h): argument
+// validation, workspace carving, kernel orchestration and error reporting.
+//
+// Error convention (mirrors the reference's TORCH_CHECK -> RuntimeError,
+// gmmxx/csrc/canary/canary.cu:28-46): every entry point returns a status code;
+// the message of the last failure on the calling host thread is kept in a
+// thread-local buffer exposed by gmmxx_last_error().
+#include "gmm_common.cuh"
+
+#include <stdarg.h>
+#include <stdio.h>
+
+namespace gmmxx {
+
+static thread_local char g_err[1024] = {0};
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return GMMXX_OK;
+}
+
+int launch_prepare(int cov, int64_t B, int64_t D, int64_t K, float* means, float* covp, float* weights,
+                   float reg, float mw, int prologue, const Layout& L, char* ws, cudaStream_t st);
+int launch_finalize(int cov, int64_t B, int64_t D, int64_t K, int64_t n_total, const float* stats,
+                    const double* ll, const float* xx, float reg, float mw, float* means, float* covp,
+                    float* weights, float* lb_out, cudaStream_t st);
+int launch_canary(const int32_t* in, int32_t* out, int64_t n, int32_t offset, cudaStream_t st);
+int launch_xx_total(const void* x, int dt, int64_t B, int64_t N, int D, float* xx, cudaStream_t st);
+
+}  // namespace gmmxx
+
+#include "rows_api.cuh"
+
+using namespace gmmxx;
+
+namespace {
+
+int check_shape(int cov, int dt, int64_t B, int64_t N, int64_t D, int64_t K) {
+  if (cov < GMMXX_SPHERICAL || cov > GMMXX_FULL) return set_error(GMMXX_ERR_INVALID, "unknown covariance type %d", cov);
+  if (dt < GMMXX_FLOAT32 || dt > GMMXX_FLOAT16) return set_error(GMMXX_ERR_INVALID, "unknown x dtype %d", dt);
+  if (B <= 0 || N < 0 || D <= 0 || K <= 0)
+    return set_error(GMMXX_ERR_INVALID, "bad sizes B=%lld N=%lld D=%lld K=%lld", (long long)B, (long long)N,
+                     (long long)D, (long long)K);
+  const int64_t maxd = (cov == GMMXX_FULL) ? kMaxDFull : kMaxD;
+  if (D > maxd)
+    return set_error(GMMXX_ERR_UNSUPPORTED, "D=%lld exceeds the engine window (D <= %lld for this covariance type)",
+                     (long long)D, (long long)maxd);
+  if (K > (1 << 24)) return set_error(GMMXX_ERR_UNSUPPORTED, "K=%lld too large", (long long)K);
+  if (B > 65535) return set_error(GMMXX_ERR_UNSUPPORTED, "B=%lld too large (max 65535)", (long long)B);
+  return GMMXX_OK;
+}
+
+int check_ws(const void* ws, size_t bytes, const Layout& L) {
+  if (ws == nullptr) return set_error(GMMXX_ERR_INVALID, "workspace is NULL");
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return set_error(GMMXX_ERR_INVALID, "workspace must be 256-byte aligned");
+  if ((int64_t)bytes < L.total)
+    return set_error(GMMXX_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %lld bytes required", bytes,
+                     (long long)L.total);
+  return GMMXX_OK;
+}
+
+#define GMMXX_REQUIRE(p, name) \
+  if ((p) == nullptr) return set_error(GMMXX_ERR_INVALID, "%s is NULL", name)
+
+RowArgs make_rows(int cov, int dt, const void* x, int64_t B, int64_t N, int64_t D, int64_t K, const Layout& L,
+                  char* ws) {
+  RowArgs a{};
+  a.x = x;
+  a.dt = dt;
+  a.N = N;
+  a.D = (int)D;
+  a.K = (int)K;
+  a.FE = L.FE;
+  a.Kp = L.Kp;
+  a.cc = reinterpret_cast<const CompConst*>(ws + L.cc);
+  a.wt = reinterpret_cast<const float*>(ws + L.wt);
+  a.prec = reinterpret_cast<const float*>(ws + L.prec);
+  a.FM = stat_width(cov, (int)D);
+  return a;
+}
+
+int infer_common(int cov, int dt, const void* x, int64_t B, int64_t N, int64_t D, int64_t K, const float* means,
+                 const float* covp, const float* weights, void* ws, size_t wsb, cudaStream_t st, Layout* L) {
+  if (int rc = check_shape(cov, dt, B, N, D, K)) return rc;
+  GMMXX_REQUIRE(means, "means");
+  GMMXX_REQUIRE(covp, "cov");
+  GMMXX_REQUIRE(weights, "weights");
+  if (N > 0) GMMXX_REQUIRE(x, "x");
+  *L = make_layout(cov, B, N, D, K);
+  if (int rc = check_ws(ws, wsb, *L)) return rc;
+  // prologue off: parameters are read, never written
+  return launch_prepare(cov, B, D, K, const_cast<float*>(means), const_cast<float*>(covp),
+                        const_cast<float*>(weights), 0.f, 0.f, 0, *L, static_cast<char*>(ws), st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int gmmxx_abi_version(void) { return GMMXX_ABI_VERSION; }
+
+const char* gmmxx_last_error(void) { return g_err; }
+
+int gmmxx_canary_add_offset(const int32_t* in, int32_t* out, int64_t n, int32_t offset, void* stream) {
+  if (n < 0) return set_error(GMMXX_ERR_INVALID, "n < 0");
+  if (n > 0) {
+    GMMXX_REQUIRE(in, "in");
+    GMMXX_REQUIRE(out, "out");
+  }
+  return launch_canary(in, out, n, offset, static_cast<cudaStream_t>(stream));
+}
+
+int64_t gmmxx_stat_width(int cov_type, int64_t D) {
+  if (cov_type < GMMXX_SPHERICAL || cov_type > GMMXX_FULL || D <= 0) return -1;
+  return stat_width(cov_type, (int)D);
+}
+
+size_t gmmxx_workspace_bytes(int cov_type, int64_t B, int64_t N, int64_t D, int64_t K) {
+  if (cov_type < GMMXX_SPHERICAL || cov_type > GMMXX_FULL || B <= 0 || N < 0 || D <= 0 || K <= 0) return 0;
+  return (size_t)make_layout(cov_type, B, N, D, K).total;
+}
+
+int gmmxx_workspace_status(void* workspace, int* status_out, void* stream) {
+  GMMXX_REQUIRE(workspace, "workspace");
+  GMMXX_REQUIRE(status_out, "status_out");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, workspace, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, sizeof(int), st);
+  if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "workspace status read: %s", cudaGetErrorString(e));
+  *status_out = (host & (1 << GMMXX_ERR_NOT_PD)) ? GMMXX_ERR_NOT_PD : GMMXX_OK;
+  return GMMXX_OK;
+}
+
+int gmmxx_em_prepare(int cov_type, int64_t B, int64_t D, int64_t K, float* means, float* cov, float* weights,
+                     float reg_covar, float min_weight, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_shape(cov_type, GMMXX_FLOAT32, B, 0, D, K)) return rc;
+  GMMXX_REQUIRE(means, "means");
+  GMMXX_REQUIRE(cov, "cov");
+  GMMXX_REQUIRE(weights, "weights");
+  if (!(min_weight > 0.f)) return set_error(GMMXX_ERR_INVALID, "min_weight must be positive");
+  if (!(reg_covar >= 0.f)) return set_error(GMMXX_ERR_INVALID, "reg_covar must be non-negative");
+  const Layout L = make_layout(cov_type, B, 0, D, K);
+  if (int rc = check_ws(workspace, workspace_bytes, L)) return rc;
+  return launch_prepare(cov_type, B, D, K, means, cov, weights, reg_covar, min_weight, 1, L,
+                        static_cast<char*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,
+                        void* workspace, size_t workspace_bytes, float* stats, double* log_likelihood,
+                        void* stream) {
+  if (int rc = check_shape(cov_type, x_dtype, B, N, D, K)) return rc;
+  GMMXX_REQUIRE(stats, "stats");
+  GMMXX_REQUIRE(log_likelihood, "log_likelihood");
+  if (N > 0) GMMXX_REQUIRE(x, "x");
+  const Layout L = make_layout(cov_type, B, N, D, K);
+  if (int rc = check_ws(workspace, workspace_bytes, L)) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
+  a.lse_out = reinterpret_cast<float*>(ws + L.lse);
+  a.ll = log_likelihood;
+  if (int rc = launch_rows(cov_type, MODE_LSE, a, (int)B, st)) return rc;
+  a.lse_in = a.lse_out;
+  a.stats = stats;
+  return launch_mstep(cov_type, a, (int)B, st);
+}
+
+int gmmxx_em_finalize(int cov_type, int64_t B, int64_t D, int64_t K, int64_t n_total, const float* stats,
+                      const double* log_likelihood, const float* xx_total, float reg_covar, float min_weight,
+                      float* means, float* cov, float* weights, float* lower_bound_out, void* stream) {
+  if (int rc = check_shape(cov_type, GMMXX_FLOAT32, B, 0, D, K)) return rc;
+  GMMXX_REQUIRE(stats, "stats");
+  GMMXX_REQUIRE(log_likelihood, "log_likelihood");
+  GMMXX_REQUIRE(means, "means");
+  GMMXX_REQUIRE(cov, "cov");
+  GMMXX_REQUIRE(weights, "weights");
+  if (cov_type == GMMXX_TIED) GMMXX_REQUIRE(xx_total, "xx_total");
+  if (n_total <= 0) return set_error(GMMXX_ERR_INVALID, "n_total must be positive");
+  if (!(min_weight > 0.f)) return set_error(GMMXX_ERR_INVALID, "min_weight must be positive");
+  return launch_finalize(cov_type, B, D, K, n_total, stats, log_likelihood, xx_total, reg_covar, min_weight, means,
+                         cov, weights, lower_bound_out, static_cast<cudaStream_t>(stream));
+}
+
+int gmmxx_xx_total(int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, float* xx_out, void* stream) {
+  if (int rc = check_shape(GMMXX_TIED, x_dtype, B, N, D, 1)) return rc;
+  GMMXX_REQUIRE(xx_out, "xx_out");
+  if (N > 0) GMMXX_REQUIRE(x, "x");
+  return launch_xx_total(x, x_dtype, B, N, (int)D, xx_out, static_cast<cudaStream_t>(stream));
+}
+
+int gmmxx_assign(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,
+                 const float* means, const float* cov, const float* weights, int64_t* labels_out, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Layout L;
+  if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
+    return rc;
+  if (N > 0) GMMXX_REQUIRE(labels_out, "labels_out");
+  RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, static_cast<char*>(workspace));
+  a.labels = labels_out;
+  return launch_rows(cov_type, MODE_ARGMAX, a, (int)B, st);
+}
+
+int gmmxx_logsumexp(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,
+                    const float* means, const float* cov, const float* weights, float* lse_out, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Layout L;
+  if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
+    return rc;
+  if (N > 0) GMMXX_REQUIRE(lse_out, "lse_out");
+  RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, static_cast<char*>(workspace));
+  a.lse_out = lse_out;
+  return launch_rows(cov_type, MODE_LSE, a, (int)B, st);
+}
+
+int gmmxx_resp(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,
+               const float* means, const float* cov, const float* weights, const float* log_norm, float* resp_out,
+               void* workspace, size_t workspace_bytes, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Layout L;
+  if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
+    return rc;
+  if (N > 0) {
+    GMMXX_REQUIRE(log_norm, "log_norm");
+    GMMXX_REQUIRE(resp_out, "resp_out");
+  }
+  RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, static_cast<char*>(workspace));
+  a.lse_in = log_norm;
+  a.out = resp_out;
+  return launch_rows(cov_type, MODE_RESP, a, (int)B, st);
+}
+
+int gmmxx_predict_proba(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,
+                        const float* means, const float* cov, const float* weights, float* proba_out,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Layout L;
+  if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
+    return rc;
+  if (N > 0) GMMXX_REQUIRE(proba_out, "proba_out");
+  char* ws = static_cast<char*>(workspace);
+  RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
+  a.lse_out = reinterpret_cast<float*>(ws + L.lse);
+  if (int rc = launch_rows(cov_type, MODE_LSE, a, (int)B, st)) return rc;
+  a.lse_in = a.lse_out;
+  a.out = proba_out;
+  return launch_rows(cov_type, MODE_RESP, a, (int)B, st);
+}
+
+}  // extern "C"

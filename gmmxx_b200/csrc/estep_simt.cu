@@ -1,0 +1,539 @@
+// estep_simt.cu -- SIMT fp32 E-step / M-step statistics kernels (all four
+// covariance types, any x dtype).
+//
+// These are the engine's exact-fp32 kernels: the logits, the streaming
+// per-row logsumexp, responsibilities and the sufficient statistics are all
+// computed in fp32 on the CUDA cores, in the same expanded-distance form as the
+// reference's torch path (gmmxx/torch_fallback.py:337-465, 468-596,
+// 2255-2291).  Tile: 64 rows x 64 components per CTA, 256 threads with 4x4
+// register micro-tiles; features and component weights are staged through
+// shared memory in chunks of 32.
+//
+//   rows_kernel   one pass over all K per row tile: logsumexp (+ sum for the
+//                 log-likelihood), argmax (labels) or exp(logit - lse)
+//                 (responsibilities / predict_proba).
+//   mstep_kernel  grid (row blocks, K tiles, B): recomputes the logits of its
+//                 64-component slice, r = exp(logit - lse), and accumulates
+//                 sum_n r_nk psi(x_n) in registers over many row tiles; one
+//                 atomic flush per CTA.  (N, K) is never materialised.
+#include "rows_api.cuh"
+
+#include <float.h>
+
+#include <algorithm>
+
+namespace gmmxx {
+
+
+
+template <int COV>
+__device__ __forceinline__ float feat_e(const float* xr, int f, int D, const uint16_t* pairs) {
+  if (COV == GMMXX_SPHERICAL || COV == GMMXX_TIED) return xr[f];
+  if (COV == GMMXX_DIAG) return f < D ? xr[f] * xr[f] : xr[f - D];
+  if (f < D) return xr[f];
+  const uint16_t p = pairs[f - D];
+  return xr[p & 0xff] * xr[p >> 8];
+}
+
+template <int COV>
+__device__ __forceinline__ float feat_m(const float* xr, float q, int f, int D, int FM, const uint16_t* pairs) {
+  if (f >= FM) return 0.f;
+  if (f == 0) return 1.f;
+  if (f <= D) return xr[f - 1];
+  const int g = f - 1 - D;
+  if (COV == GMMXX_SPHERICAL) return q;
+  if (COV == GMMXX_DIAG) return xr[g] * xr[g];
+  if (COV == GMMXX_FULL) {
+    const uint16_t p = pairs[g];
+    return xr[p & 0xff] * xr[p >> 8];
+  }
+  return 0.f;
+}
+
+// Shared-memory carve-up common to both kernels.
+struct Smem {
+  float* xs;        // [kBN][D+1]
+  float* q;         // [kBN]
+  float* phic;      // [kFC][kBN]
+  float* wc;        // [kFC][kBK]
+  float* prec;      // [D][D] (tied)
+  uint16_t* pairs;  // [D(D+1)/2] (full)
+  float* R;         // [kBN][kBK]      (mstep)
+  float* phim;      // [kBN][64]       (mstep)
+};
+
+__host__ __device__ inline int64_t smem_bytes(int cov, int D, bool mstep) {
+  int64_t b = 0;
+  b += (int64_t)kBN * (D + 1) * 4;
+  b += kBN * 4;
+  b += kFC * kBN * 4 + kFC * kBK * 4;
+  if (cov == GMMXX_TIED) b += (int64_t)D * D * 4;
+  if (mstep) b += kBN * kBK * 4 + kBN * 64 * 4;
+  if (cov == GMMXX_FULL) b += round_up((int64_t)D * (D + 1) / 2 * 2, 16);
+  return b;
+}
+
+template <int COV>
+__device__ __forceinline__ Smem carve(char* base, int D, bool mstep) {
+  Smem s;
+  float* p = reinterpret_cast<float*>(base);
+  s.phic = p; p += kFC * kBN;
+  s.wc = p; p += kFC * kBK;
+  s.R = nullptr; s.phim = nullptr;
+  if (mstep) { s.R = p; p += kBN * kBK; s.phim = p; p += kBN * 64; }
+  s.q = p; p += kBN;
+  s.prec = nullptr;
+  if (COV == GMMXX_TIED) { s.prec = p; p += D * D; }
+  s.xs = p; p += kBN * (D + 1);
+  s.pairs = reinterpret_cast<uint16_t*>(p);
+  return s;
+}
+
+// Stage one row tile of x (fp32 in smem, zero beyond N) and its q_n.
+template <int COV>
+__device__ __forceinline__ void load_rows(const RowArgs& a, const Smem& s, int b, int64_t row0) {
+  const int D = a.D, xst = D + 1;
+  const int64_t base = ((int64_t)b * a.N + row0) * D;
+  const int64_t nrows = min((int64_t)kBN, a.N - row0);
+  for (int e = threadIdx.x; e < kBN * D; e += kThreads) {
+    const int r = e / D, d = e - r * D;
+    s.xs[r * xst + d] = (r < nrows) ? load_x(a.x, base + e, a.dt) : 0.f;
+  }
+  __syncthreads();
+  if (COV == GMMXX_SPHERICAL) {
+    // |x|^2 (torch_fallback.py:1992, x_sq_all)
+    if (threadIdx.x < kBN) {
+      const float* xr = s.xs + threadIdx.x * xst;
+      float acc = 0.f;
+      for (int d = 0; d < D; ++d) acc = fmaf(xr[d], xr[d], acc);
+      s.q[threadIdx.x] = acc;
+    }
+  } else if (COV == GMMXX_TIED) {
+    // x^T P x (torch_fallback.py:452): 4 threads per row
+    const int r = threadIdx.x >> 2, part = threadIdx.x & 3;
+    const float* xr = s.xs + r * xst;
+    float acc = 0.f;
+    for (int d = part; d < D; d += 4) {
+      const float* pr = s.prec + d * D;
+      float t = 0.f;
+      for (int e = 0; e < D; ++e) t = fmaf(pr[e], xr[e], t);
+      acc = fmaf(xr[d], t, acc);
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (part == 0) s.q[r] = acc;
+  } else {
+    if (threadIdx.x < kBN) s.q[threadIdx.x] = 0.f;
+  }
+  __syncthreads();
+}
+
+// 64x64 dot products of the row tile's features with one component tile.
+template <int COV>
+__device__ __forceinline__ void tile_dots(const RowArgs& a, const Smem& s, int b, int kt, float acc[4][4]) {
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int D = a.D, xst = D + 1, FE = a.FE;
+  const float* wtb = a.wt + (int64_t)b * FE * a.Kp + (int64_t)kt * kBK;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int f0 = 0; f0 < FE; f0 += kFC) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < kFC * kBN; e += kThreads) {
+      const int r = e & (kBN - 1), f = e / kBN;
+      s.phic[e] = (f0 + f < FE) ? feat_e<COV>(s.xs + r * xst, f0 + f, D, s.pairs) : 0.f;
+    }
+    for (int e = threadIdx.x; e < kFC * kBK; e += kThreads) {
+      const int k = e & (kBK - 1), f = e / kBK;
+      s.wc[e] = (f0 + f < FE) ? __ldg(wtb + (int64_t)(f0 + f) * a.Kp + k) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int f = 0; f < kFC; ++f) {
+      const float4 xv = *reinterpret_cast<const float4*>(s.phic + f * kBN + ty * 4);
+      const float4 wv = *reinterpret_cast<const float4*>(s.wc + f * kBK + tx * 4);
+      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+      const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
+    }
+  }
+}
+
+// acc -> logits in place (invalid components -> -inf).
+__device__ __forceinline__ void to_logits(const RowArgs& a, const Smem& s, int b, int kt, float acc[4][4]) {
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = kt * kBK + tx * 4 + j;
+    if (k < a.K) {
+      const CompConst c = a.cc[(int64_t)b * a.K + k];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float dist = s.q[ty * 4 + i] + acc[i][j] + c.mpm;
+        dist = fmaxf(dist, 0.f);
+        acc[i][j] = c.lw - 0.5f * (c.s * dist + c.ln);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i][j] = -INFINITY;
+    }
+  }
+}
+
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) { m = m2; s = s2; return; }
+  const float nm = fmaxf(m, m2);
+  s = s * expf(m - nm) + s2 * expf(m2 - nm);
+  m = nm;
+}
+
+template <int COV, int MODE>
+__global__ void __launch_bounds__(kThreads) rows_kernel(RowArgs a) {
+  extern __shared__ __align__(16) char smem_raw[];
+  const Smem s = carve<COV>(smem_raw, a.D, false);
+  const int b = blockIdx.y;
+  const int64_t row0 = (int64_t)blockIdx.x * kBN;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  if (COV == GMMXX_TIED) {
+    const float* pb = a.prec + (int64_t)b * a.D * a.D;
+    for (int e = threadIdx.x; e < a.D * a.D; e += kThreads) s.prec[e] = pb[e];
+  }
+  if (COV == GMMXX_FULL) {
+    for (int i = threadIdx.x; i < a.D; i += kThreads) {
+      int p = i * a.D - i * (i - 1) / 2;  // index of (i, i) in the packed i<=j order
+      for (int j = i; j < a.D; ++j) s.pairs[p++] = (uint16_t)(i | (j << 8));
+    }
+  }
+  __syncthreads();
+  load_rows<COV>(a, s, b, row0);
+
+  float run_m[4], run_s[4], lse_row[4];
+  float best_v[4];
+  int best_k[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    run_m[i] = -INFINITY; run_s[i] = 0.f; best_v[i] = -INFINITY; best_k[i] = 0;
+    const int64_t row = row0 + ty * 4 + i;
+    lse_row[i] = (MODE == MODE_RESP && row < a.N) ? a.lse_in[(int64_t)b * a.N + row] : 0.f;
+  }
+  const int ktiles = (int)(a.Kp / kBK);
+  float acc[4][4];
+  for (int kt = 0; kt < ktiles; ++kt) {
+    tile_dots<COV>(a, s, b, kt, acc);
+    to_logits(a, s, b, kt, acc);
+    if (MODE == MODE_LSE) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float m = fmaxf(fmaxf(acc[i][0], acc[i][1]), fmaxf(acc[i][2], acc[i][3]));
+        float sm = 0.f;
+        if (m != -INFINITY) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) sm += expf(acc[i][j] - m);
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+          const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+          const float s2 = __shfl_xor_sync(0xffffffffu, sm, o);
+          lse_merge(m, sm, m2, s2);
+        }
+        lse_merge(run_m[i], run_s[i], m, sm);
+      }
+    } else if (MODE == MODE_ARGMAX) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float v = best_v[i];
+        int kk = best_k[i];
+        float tv = -INFINITY;
+        int tk = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (acc[i][j] > tv) { tv = acc[i][j]; tk = kt * kBK + tx * 4 + j; }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+          const float v2 = __shfl_xor_sync(0xffffffffu, tv, o);
+          const int k2 = __shfl_xor_sync(0xffffffffu, tk, o);
+          if (v2 > tv || (v2 == tv && k2 < tk)) { tv = v2; tk = k2; }
+        }
+        if (tv > v) { v = tv; kk = tk; }  // later tiles replace only on strictly larger
+        best_v[i] = v; best_k[i] = kk;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t row = row0 + ty * 4 + i;
+        if (row >= a.N) continue;
+        float* orow = a.out + ((int64_t)b * a.N + row) * a.K;
+        const int k0 = kt * kBK + tx * 4;
+        float p[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[j] = expf(acc[i][j] - lse_row[i]);
+        if ((a.K & 3) == 0 && k0 + 3 < a.K) {
+          *reinterpret_cast<float4*>(orow + k0) = make_float4(p[0], p[1], p[2], p[3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (k0 + j < a.K) orow[k0 + j] = p[j];
+        }
+      }
+    }
+  }
+
+  if (MODE == MODE_LSE) {
+    double part = 0.0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = row0 + ty * 4 + i;
+      const float l = run_m[i] + logf(run_s[i]);
+      if (row < a.N && tx == 0) {
+        a.lse_out[(int64_t)b * a.N + row] = l;
+        part += (double)l;
+      }
+    }
+    if (a.ll != nullptr) {
+      __shared__ double red[kThreads / 32];
+      const double tot = block_sum<double>(part, red);
+      if (threadIdx.x == 0) atomicAdd(a.ll, tot);
+    }
+  } else if (MODE == MODE_ARGMAX) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = row0 + ty * 4 + i;
+      if (row < a.N && tx == 0) a.labels[(int64_t)b * a.N + row] = best_k[i];
+    }
+  }
+}
+
+template <int COV, int NCH>
+__global__ void __launch_bounds__(kThreads) mstep_kernel(RowArgs a) {
+  extern __shared__ __align__(16) char smem_raw[];
+  const Smem s = carve<COV>(smem_raw, a.D, true);
+  const int b = blockIdx.z, kt = blockIdx.y;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int kg = threadIdx.x >> 4, fg = threadIdx.x & 15;
+  const int D = a.D, xst = D + 1;
+  if (COV == GMMXX_TIED) {
+    const float* pb = a.prec + (int64_t)b * D * D;
+    for (int e = threadIdx.x; e < D * D; e += kThreads) s.prec[e] = pb[e];
+  }
+  if (COV == GMMXX_FULL) {
+    for (int i = threadIdx.x; i < D; i += kThreads) {
+      int p = i * D - i * (i - 1) / 2;
+      for (int j = i; j < D; ++j) s.pairs[p++] = (uint16_t)(i | (j << 8));
+    }
+  }
+  float macc[NCH][4][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) macc[c][i][j] = 0.f;
+
+  const int64_t rstart = (int64_t)blockIdx.x * a.rows_per_cta;
+  const int64_t rend = min(rstart + a.rows_per_cta, a.N);
+  const float* lse_b = a.lse_in + (int64_t)b * a.N;
+  float acc[4][4];
+  for (int64_t row0 = rstart; row0 < rend; row0 += kBN) {
+    __syncthreads();
+    load_rows<COV>(a, s, b, row0);
+    tile_dots<COV>(a, s, b, kt, acc);
+    to_logits(a, s, b, kt, acc);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = row0 + ty * 4 + i;
+      const bool ok = row < rend;
+      const float l = ok ? lse_b[row] : 0.f;
+      float r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = ok ? expf(acc[i][j] - l) : 0.f;  // -inf -> 0
+      *reinterpret_cast<float4*>(s.R + (ty * 4 + i) * kBK + tx * 4) = make_float4(r[0], r[1], r[2], r[3]);
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      __syncthreads();
+      for (int e = threadIdx.x; e < kBN * 64; e += kThreads) {
+        const int r = e >> 6, f = e & 63;
+        s.phim[e] = feat_m<COV>(s.xs + r * xst, s.q[r], c * 64 + f, D, a.FM, s.pairs);
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int r = 0; r < kBN; ++r) {
+        const float4 rv = *reinterpret_cast<const float4*>(s.R + r * kBK + kg * 4);
+        const float4 pv = *reinterpret_cast<const float4*>(s.phim + r * 64 + fg * 4);
+        const float ra[4] = {rv.x, rv.y, rv.z, rv.w};
+        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) macc[c][i][j] = fmaf(ra[i], pa[j], macc[c][i][j]);
+      }
+    }
+  }
+  // one flush per CTA
+  float* st = a.stats + (int64_t)b * a.K * a.FM;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = kt * kBK + kg * 4 + i;
+      if (k >= a.K) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int f = c * 64 + fg * 4 + j;
+        if (f < a.FM) atomicAdd(st + (int64_t)k * a.FM + f, macc[c][i][j]);
+      }
+    }
+}
+
+// xx (B, D, D) += sum_n x_n x_n^T  (tied covariance; torch_fallback.py:2856-2862)
+__global__ void __launch_bounds__(kThreads) xx_total_kernel(const void* x, int dt, int64_t N, int D,
+                                                            int64_t rows_per_cta, float* xx) {
+  extern __shared__ __align__(16) char smem_raw[];
+  float* xs = reinterpret_cast<float*>(smem_raw);  // [kBN][D+1]
+  const int b = blockIdx.y;
+  const int xst = D + 1;
+  const int64_t rstart = (int64_t)blockIdx.x * rows_per_cta;
+  const int64_t rend = min(rstart + rows_per_cta, N);
+  constexpr int kPer = (kMaxD * kMaxD) / kThreads;  // 64
+  float acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
+  for (int64_t row0 = rstart; row0 < rend; row0 += kBN) {
+    __syncthreads();
+    const int64_t nrows = min((int64_t)kBN, rend - row0);
+    const int64_t base = ((int64_t)b * N + row0) * D;
+    for (int e = threadIdx.x; e < kBN * D; e += kThreads) {
+      const int r = e / D, d = e - r * D;
+      xs[r * xst + d] = (r < nrows) ? load_x(x, base + e, dt) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = threadIdx.x + i * kThreads;
+      if (e < D * D) {
+        const int di = e / D, de = e - di * D;
+        float t = acc[i];
+        for (int r = 0; r < kBN; ++r) t = fmaf(xs[r * xst + di], xs[r * xst + de], t);
+        acc[i] = t;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x + i * kThreads;
+    if (e < D * D) atomicAdd(xx + (int64_t)b * D * D + e, acc[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host launchers
+// ---------------------------------------------------------------------------
+
+static int sm_count() {
+  static int cached = 0;
+  if (cached == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&cached, cudaDevAttrMultiProcessorCount, dev);
+    if (cached <= 0) cached = 148;
+  }
+  return cached;
+}
+
+template <typename KernelT>
+static int prep_smem(KernelT k, int64_t bytes) {
+  if (bytes > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  return GMMXX_OK;
+}
+
+template <int COV, int MODE>
+static int launch_rows_t(const RowArgs& a, int B, cudaStream_t st) {
+  const int64_t sm = smem_bytes(COV, a.D, false);
+  auto k = rows_kernel<COV, MODE>;
+  if (int rc = prep_smem(k, sm)) return rc;
+  dim3 grid((unsigned)ceil_div(a.N, kBN), (unsigned)B);
+  k<<<grid, kThreads, sm, st>>>(a);
+  return check_launch("rows_kernel");
+}
+
+int launch_rows(int cov, int mode, const RowArgs& a, int B, cudaStream_t st) {
+  if (a.N == 0) return GMMXX_OK;
+#define GMMXX_ROWS_CASE(C)                                                    \
+  case C:                                                                     \
+    if (mode == MODE_LSE) return launch_rows_t<C, MODE_LSE>(a, B, st);        \
+    if (mode == MODE_ARGMAX) return launch_rows_t<C, MODE_ARGMAX>(a, B, st);  \
+    return launch_rows_t<C, MODE_RESP>(a, B, st);
+  switch (cov) {
+    GMMXX_ROWS_CASE(GMMXX_SPHERICAL)
+    GMMXX_ROWS_CASE(GMMXX_DIAG)
+    GMMXX_ROWS_CASE(GMMXX_TIED)
+    GMMXX_ROWS_CASE(GMMXX_FULL)
+  }
+#undef GMMXX_ROWS_CASE
+  return set_error(GMMXX_ERR_INVALID, "bad covariance type %d", cov);
+}
+
+template <int COV, int NCH>
+static int launch_mstep_t(RowArgs a, int B, cudaStream_t st) {
+  const int64_t sm = smem_bytes(COV, a.D, true);
+  auto k = mstep_kernel<COV, NCH>;
+  if (int rc = prep_smem(k, sm)) return rc;
+  const int ktiles = (int)(a.Kp / kBK);
+  const int64_t tiles = ceil_div(a.N, kBN);
+  const int64_t target = (int64_t)sm_count() * 4;
+  int64_t nblk = ceil_div(target, (int64_t)ktiles * B);
+  nblk = std::max<int64_t>(1, std::min<int64_t>(nblk, tiles));
+  a.rows_per_cta = ceil_div(tiles, nblk) * kBN;
+  nblk = ceil_div(a.N, a.rows_per_cta);
+  dim3 grid((unsigned)nblk, (unsigned)ktiles, (unsigned)B);
+  k<<<grid, kThreads, sm, st>>>(a);
+  return check_launch("mstep_kernel");
+}
+
+template <int COV>
+static int launch_mstep_c(const RowArgs& a, int B, cudaStream_t st) {
+  const int nch = (int)ceil_div(a.FM, 64);
+  switch (nch) {
+    case 1: return launch_mstep_t<COV, 1>(a, B, st);
+    case 2: return launch_mstep_t<COV, 2>(a, B, st);
+    case 3: return launch_mstep_t<COV, 3>(a, B, st);
+    case 4: return launch_mstep_t<COV, 4>(a, B, st);
+    case 5: return launch_mstep_t<COV, 5>(a, B, st);
+    case 6: return launch_mstep_t<COV, 6>(a, B, st);
+  }
+  return set_error(GMMXX_ERR_UNSUPPORTED, "statistics width %d exceeds the SIMT window", a.FM);
+}
+
+int launch_mstep(int cov, const RowArgs& a, int B, cudaStream_t st) {
+  if (a.N == 0) return GMMXX_OK;
+  switch (cov) {
+    case GMMXX_SPHERICAL: return launch_mstep_c<GMMXX_SPHERICAL>(a, B, st);
+    case GMMXX_DIAG: return launch_mstep_c<GMMXX_DIAG>(a, B, st);
+    case GMMXX_TIED: return launch_mstep_c<GMMXX_TIED>(a, B, st);
+    case GMMXX_FULL: return launch_mstep_c<GMMXX_FULL>(a, B, st);
+  }
+  return set_error(GMMXX_ERR_INVALID, "bad covariance type %d", cov);
+}
+
+int launch_xx_total(const void* x, int dt, int64_t B, int64_t N, int D, float* xx, cudaStream_t st) {
+  if (N == 0) return GMMXX_OK;
+  const int64_t sm = (int64_t)kBN * (D + 1) * 4;
+  if (int rc = prep_smem(xx_total_kernel, sm)) return rc;
+  const int64_t tiles = ceil_div(N, kBN);
+  int64_t nblk = std::max<int64_t>(1, std::min<int64_t>(ceil_div((int64_t)sm_count() * 2, B), tiles));
+  const int64_t rpc = ceil_div(tiles, nblk) * kBN;
+  nblk = ceil_div(N, rpc);
+  dim3 grid((unsigned)nblk, (unsigned)B);
+  xx_total_kernel<<<grid, kThreads, sm, st>>>(x, dt, N, D, rpc, xx);
+  return check_launch("xx_total_kernel");
+}
+
+}  // namespace gmmxx

@@ -1,0 +1,146 @@
+// gmm_common.cuh -- shared definitions of the B200 GMM EM engine.
+//
+// The engine writes every covariance type as one "feature" contraction:
+//
+//   dist[n,k]  = q_n + sum_f phi_f(x_n) * W[f,k] + mpm_k          (clamped >= 0)
+//   logit[n,k] = lw_k - 0.5 * (s_k * dist[n,k] + ln_k)
+//
+// which is the reference's expanded-distance logit
+// (gmmxx/torch_fallback.py:337-465) with the loop-invariant terms folded into
+// a per-iteration "component table":
+//
+//   type       phi (E-step features)          W[f,k]                         q_n        s_k
+//   spherical  x_d                            -2 mu_kd                       |x|^2      1/var_k
+//   diag       [x_d^2, x_d]                   [1/var_kd, -2 mu_kd/var_kd]    0          1
+//   tied       x_d                            -2 (P mu_k)_d                  x^T P x    1
+//   full       [x_d, x_i x_j (i<=j)]          [-2 (P_k mu_k)_d, P_ij+P_ji]   0          1
+//
+// The M-step statistics of one row are r_nk * psi(x_n) with
+//   psi = [1, x, |x|^2] (spherical) | [1, x, x^2] (diag) | [1, x] (tied) |
+//         [1, x, x_i x_j (i<=j)] (full);
+// their sum over n is the (B, K, F) stats buffer of the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/gmmxx_b200.h"
+
+namespace gmmxx {
+
+constexpr float kLog2Pi = 1.8378770664093453f;  // log(2*pi)
+
+// Tile shape of the SIMT kernels: 64 rows x 64 components, 256 threads,
+// 4x4 register micro-tiles.
+constexpr int kBN = 64;
+constexpr int kBK = 64;
+constexpr int kThreads = 256;
+constexpr int kFC = 32;  // feature chunk staged in shared memory
+
+// SIMT windows (shapes outside return GMMXX_ERR_UNSUPPORTED).
+constexpr int kMaxD = 128;      // spherical / diag / tied
+constexpr int kMaxDFull = 26;   // full: stat width 1 + D + D(D+1)/2 <= 384
+constexpr int kMaxStatChunks = 6;
+
+__host__ __device__ inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+__host__ __device__ inline int feat_width(int cov, int D) {
+  switch (cov) {
+    case GMMXX_SPHERICAL: return D;
+    case GMMXX_DIAG: return 2 * D;
+    case GMMXX_TIED: return D;
+    default: return D + D * (D + 1) / 2;
+  }
+}
+
+__host__ __device__ inline int stat_width(int cov, int D) {
+  switch (cov) {
+    case GMMXX_SPHERICAL: return D + 2;
+    case GMMXX_DIAG: return 2 * D + 1;
+    case GMMXX_TIED: return D + 1;
+    default: return 1 + D + D * (D + 1) / 2;
+  }
+}
+
+// Per-component constants of the logit epilogue.
+struct __align__(16) CompConst {
+  float lw;   // log weight
+  float s;    // distance scale (1/var for spherical, else 1)
+  float ln;   // log-normaliser (D log 2pi + log det)
+  float mpm;  // mu^T P mu (or |mu|^2 for spherical)
+};
+
+// Workspace layout (all offsets 256-byte aligned).
+struct Layout {
+  int64_t status;   // int[4]: [0] sticky status, [1] Cholesky jitter level
+  int64_t cc;       // CompConst[B][K]
+  int64_t wt;       // float[B][FE][Kp]  (feature-major component weights)
+  int64_t prec;     // float[B][D][D] (tied) or float[B][K][D][D] (full)
+  int64_t lse;      // float[B][max(N, K)] (per-row lse; per-matrix log det while preparing)
+  int64_t total;
+  int64_t Kp;
+  int FE;
+};
+
+inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
+  Layout L;
+  auto al = [](int64_t v) { return round_up(v, 256); };
+  L.Kp = round_up(K, kBK);
+  L.FE = feat_width(cov, (int)D);
+  int64_t off = 0;
+  L.status = off; off += al(16);
+  L.cc = off; off += al(B * K * (int64_t)sizeof(CompConst));
+  L.wt = off; off += al(B * L.FE * L.Kp * 4);
+  L.prec = off;
+  if (cov == GMMXX_TIED) off += al(B * D * D * 4);
+  else if (cov == GMMXX_FULL) off += al(B * K * D * D * 4);
+  L.lse = off; off += al(B * (N > K ? N : K) * 4);
+  L.total = off;
+  return L;
+}
+
+// --- dtype-generic loads -----------------------------------------------------
+
+__device__ __forceinline__ float load_x(const void* p, int64_t i, int dt) {
+  if (dt == GMMXX_FLOAT32) return static_cast<const float*>(p)[i];
+  if (dt == GMMXX_BFLOAT16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum; every thread gets the result.  `red` needs blockDim/32 slots.
+template <typename V>
+__device__ V block_sum(V v, V* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  V t = 0;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  __syncthreads();
+  return t;
+}
+
+}  // namespace gmmxx
+
+// --- host-side error plumbing (defined in capi.cu) ---------------------------
+namespace gmmxx {
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+}  // namespace gmmxx

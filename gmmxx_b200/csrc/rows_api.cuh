@@ -1,0 +1,33 @@
+// rows_api.cuh -- argument block and launchers of the row-tile kernels
+// (estep_simt.cu), shared with the C ABI layer.
+#pragma once
+
+#include "gmm_common.cuh"
+
+namespace gmmxx {
+
+struct RowArgs {
+  const void* x;
+  int dt;
+  int64_t N;
+  int D, K, FE;
+  int64_t Kp;
+  const CompConst* cc;  // [B][K]
+  const float* wt;      // [B][FE][Kp]
+  const float* prec;    // tied precision [B][D][D]
+  const float* lse_in;  // [B][N]
+  float* lse_out;       // [B][N]
+  double* ll;           // log-likelihood accumulator (may be null)
+  int64_t* labels;      // [B][N]
+  float* out;           // [B][N][K]
+  float* stats;         // [B][K][FM]
+  int FM;
+  int64_t rows_per_cta;
+};
+
+enum { MODE_LSE = 0, MODE_ARGMAX = 1, MODE_RESP = 2 };
+
+int launch_rows(int cov, int mode, const RowArgs& a, int B, cudaStream_t st);
+int launch_mstep(int cov, const RowArgs& a, int B, cudaStream_t st);
+
+}  // namespace gmmxx

@@ -1,0 +1,180 @@
+/*
+ * gmmxx_b200.h -- C ABI of the B200 (sm_100a) GMM EM engine.
+ *
+ * Plain C: pointers, sizes and a CUDA stream passed as `void*` (a
+ * cudaStream_t; NULL means the legacy default stream).  No framework types
+ * cross this boundary.  Every device pointer must be on the device that is
+ * current when the call is made; every call is asynchronous on `stream`
+ * unless stated otherwise.
+ *
+ * Return value: GMMXX_OK (0) or a gmmxx_status error code; a readable
+ * message for the last failing call on this host thread is available from
+ * gmmxx_last_error().
+ *
+ * Layouts (row-major, contiguous):
+ *   x          (B, N, D)      float32 / bfloat16 / float16 (x_dtype)
+ *   means      (B, K, D)      float32
+ *   cov        spherical (B, K) variances | diag (B, K, D) variances |
+ *              tied (B, D, D) covariance  | full (B, K, D, D) covariances
+ *   weights    (B, K)         float32 mixing weights
+ *   stats      (B, K, F)      float32 sufficient statistics, F from
+ *              gmmxx_stat_width(): [n_k, sum r*x (D), second-order block]
+ *              second-order block: spherical sum r*|x|^2 (1), diag sum r*x^2
+ *              (D), tied none, full sum r*x_i*x_j for i<=j (D(D+1)/2).
+ *
+ * Reference interfaces these entry points replace (OpsiClear/GMMXX, paths
+ * inside that project):
+ *   gmmxx/csrc/bindings.cpp:16-191   the nanobind `gmmxx._C` module
+ *   gmmxx/_cuda.py:328-1416          the Python wrappers around it
+ *   gmmxx/torch_fallback.py:1897-3244 the soft-EM loops whose semantics the
+ *                                     engine reproduces (parity target)
+ */
+#ifndef GMMXX_B200_H
+#define GMMXX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GMMXX_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define GMMXX_API __attribute__((visibility("default")))
+#else
+#define GMMXX_API
+#endif
+
+enum gmmxx_cov_type {
+  GMMXX_SPHERICAL = 0,
+  GMMXX_DIAG = 1,
+  GMMXX_TIED = 2,
+  GMMXX_FULL = 3
+};
+
+enum gmmxx_dtype {
+  GMMXX_FLOAT32 = 0,
+  GMMXX_BFLOAT16 = 1,
+  GMMXX_FLOAT16 = 2
+};
+
+enum gmmxx_status {
+  GMMXX_OK = 0,
+  GMMXX_ERR_INVALID = 1,      /* bad argument (shape, pointer, enum)          */
+  GMMXX_ERR_UNSUPPORTED = 2,  /* shape outside the compiled kernel windows    */
+  GMMXX_ERR_CUDA = 3,         /* CUDA runtime / launch error                  */
+  GMMXX_ERR_NOT_PD = 4,       /* covariance not positive definite (device)    */
+  GMMXX_ERR_WORKSPACE = 5     /* workspace too small                          */
+};
+
+/* ---- library / lifecycle ------------------------------------------------ */
+
+/* ABI version of the loaded library (GMMXX_ABI_VERSION). */
+GMMXX_API int gmmxx_abi_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+GMMXX_API const char* gmmxx_last_error(void);
+
+/* Smoke kernel: out[i] = in[i] + offset for n int32 values.
+ * Replaces: gmmxx/csrc/canary/canary.cu:8-48 (canary_add_offset). */
+GMMXX_API int gmmxx_canary_add_offset(const int32_t* in, int32_t* out, int64_t n, int32_t offset, void* stream);
+
+/* Width F of one (b, k) row of the sufficient-statistics buffer. */
+GMMXX_API int64_t gmmxx_stat_width(int cov_type, int64_t D);
+
+/* Bytes of device scratch a call needs for these sizes.  One workspace may be
+ * reused by successive calls on the same stream. */
+GMMXX_API size_t gmmxx_workspace_bytes(int cov_type, int64_t B, int64_t N, int64_t D, int64_t K);
+
+/* Reads (and clears) the sticky device status word kept in `workspace`
+ * (GMMXX_OK or GMMXX_ERR_NOT_PD).  Synchronises `stream`. */
+GMMXX_API int gmmxx_workspace_status(void* workspace, int* status_out, void* stream);
+
+/* ---- one soft-EM iteration, in the three steps a sharded driver needs ---- */
+
+/* Per-iteration prologue + component table.
+ * In place: spherical/diag variances clamped to >= reg_covar; weights clamped
+ * to >= min_weight and renormalised (torch_fallback.py:2062-2064, 2486-2488,
+ * 2866-2867).  Then the loop-invariant logit terms (log-weights, precisions
+ * via batch Cholesky with the reference's jitter ladder, log-determinants,
+ * precision-weighted means) are written into `workspace`.
+ * Replaces: gmmxx/csrc/estep/prepare_spherical.cu:19-90 and the torch
+ * prologue of the reference loops. */
+GMMXX_API int gmmxx_em_prepare(int cov_type, int64_t B, int64_t D, int64_t K,
+                     float* means, float* cov, float* weights,
+                     float reg_covar, float min_weight,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* E-step + M-step statistics over this shard's rows: adds sum_n r_nk * phi(x_n)
+ * into `stats` (B, K, F) and sum_n lse_n into `*log_likelihood`; both are
+ * accumulated into (callers zero them per iteration).  Uses the table written
+ * by gmmxx_em_prepare.  Never materialises the (N, K) responsibilities.
+ * Replaces: gmmxx/csrc/fused/spherical_fused.cu:31-187 (fused_safe_kernel),
+ * gmmxx/_cuda.py:415-682 (soft_update_spherical) and the E/M chunk loops of
+ * torch_fallback.py:2097-2291, 2508-2651, 2912-3139. */
+GMMXX_API int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x,
+                        int64_t B, int64_t N, int64_t D, int64_t K,
+                        void* workspace, size_t workspace_bytes,
+                        float* stats, double* log_likelihood, void* stream);
+
+/* M-step finalize from reduced statistics (torch_fallback.py:2293-2305,
+ * 2654-2666, 3141-3167): new means / covariances / weights written in place,
+ * empty components (n_k <= min_weight) keep their old means (and, except
+ * tied, covariances).  `n_total` is the per-problem sample count N summed
+ * over shards.  `xx_total` (B, D, D) = sum_n x_n x_n^T is required for tied
+ * and ignored otherwise.  `lower_bound_out` (may be NULL) receives
+ * (*log_likelihood) / (B * n_total).
+ * Replaces: gmmxx/csrc/mstep/finalize_spherical.cu:141-223,
+ * gmmxx/csrc/mstep/finalize_diag.cu:6-44, gmmxx/_cuda.py:1204-1238
+ * (tied_finalize) and gmmxx/_cuda.py:1355-1416 (full_finalize). */
+GMMXX_API int gmmxx_em_finalize(int cov_type, int64_t B, int64_t D, int64_t K, int64_t n_total,
+                      const float* stats, const double* log_likelihood,
+                      const float* xx_total, float reg_covar, float min_weight,
+                      float* means, float* cov, float* weights,
+                      float* lower_bound_out, void* stream);
+
+/* xx_out (B, D, D) += sum_n x_n x_n^T (tied covariance, once per fit;
+ * torch_fallback.py:2856-2862). */
+GMMXX_API int gmmxx_xx_total(int x_dtype, const void* x, int64_t B, int64_t N, int64_t D,
+                   float* xx_out, void* stream);
+
+/* ---- inference on fixed parameters ---------------------------------------
+ * Parameters are used as given (no clamp/renormalisation), like the
+ * reference's *_torch_native_chunked inference functions. */
+
+/* labels (B, N) int64: argmax_k logit, first maximal component wins
+ * (torch_fallback.py:780-965). Replaces _C.spherical_assign / diag_assign. */
+GMMXX_API int gmmxx_assign(int cov_type, int x_dtype, const void* x,
+                 int64_t B, int64_t N, int64_t D, int64_t K,
+                 const float* means, const float* cov, const float* weights,
+                 int64_t* labels_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* lse (B, N) float32 = log sum_k exp(logit) (torch_fallback.py:983-1130).
+ * Replaces _C.spherical_logsumexp / diag_logsumexp. */
+GMMXX_API int gmmxx_logsumexp(int cov_type, int x_dtype, const void* x,
+                    int64_t B, int64_t N, int64_t D, int64_t K,
+                    const float* means, const float* cov, const float* weights,
+                    float* lse_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* resp (B, N, K) float32 = exp(logit - log_norm) for a caller-supplied
+ * log_norm (B, N).  Replaces _C.spherical_resp / diag_resp. */
+GMMXX_API int gmmxx_resp(int cov_type, int x_dtype, const void* x,
+               int64_t B, int64_t N, int64_t D, int64_t K,
+               const float* means, const float* cov, const float* weights,
+               const float* log_norm, float* resp_out,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* predict_proba (B, N, K) float32 = exp(logit - lse) in one call
+ * (torch_fallback.py:1133-1345). */
+GMMXX_API int gmmxx_predict_proba(int cov_type, int x_dtype, const void* x,
+                        int64_t B, int64_t N, int64_t D, int64_t K,
+                        const float* means, const float* cov, const float* weights,
+                        float* proba_out, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* GMMXX_B200_H */

@@ -1,0 +1,82 @@
+"""The C ABI library loads on a CPU-only host and exports every symbol the
+header declares; host-only entry points answer without a GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from gmmxx_b200 import _native, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gmmxx_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"GMMXX_API\s+[\w\s\*]+?\b(gmmxx_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(_native.LIB_PATH):
+        build.build()
+    return _native.load()
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "gmmxx_em_accumulate" in syms and "gmmxx_assign" in syms
+    assert len(syms) >= 14
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_binding_covers_the_header(lib):
+    assert sorted(_native.exported_symbols()) == declared_symbols()
+
+
+def test_abi_version(lib):
+    assert lib.gmmxx_abi_version() == 1
+
+
+def test_stat_width_matches_layout(lib):
+    d = 16
+    assert _native.stat_width(_native.SPHERICAL, d) == d + 2
+    assert _native.stat_width(_native.DIAG, d) == 2 * d + 1
+    assert _native.stat_width(_native.TIED, d) == d + 1
+    assert _native.stat_width(_native.FULL, d) == 1 + d + d * (d + 1) // 2
+    assert lib.gmmxx_stat_width(9, 4) == -1
+
+
+def test_workspace_bytes_monotone(lib):
+    a = _native.workspace_bytes(_native.DIAG, 1, 1000, 64, 512)
+    b = _native.workspace_bytes(_native.DIAG, 1, 2000, 64, 512)
+    assert 0 < a < b
+    assert a % 256 == 0
+    assert _native.workspace_bytes(7, 1, 10, 4, 4) == 0
+
+
+def test_invalid_arguments_rejected_without_gpu(lib):
+    # validation runs before any CUDA call
+    rc = lib.gmmxx_em_prepare(9, 1, 4, 4, None, None, None, 1e-6, 1e-8, None, 0, None)
+    assert rc == _native.ERR_INVALID
+    assert b"covariance" in lib.gmmxx_last_error()
+    rc = lib.gmmxx_assign(_native.DIAG, _native.FLOAT32, None, 1, 10, 4096, 3, None, None, None, None, None, 0, None)
+    assert rc == _native.ERR_UNSUPPORTED
+    with pytest.raises(_native.UnsupportedShape):
+        _native.call("gmmxx_assign", _native.FULL, _native.FLOAT32, None, 1, 10, 64, 3, None, None, None, None,
+                     None, 0, None)
+
+
+def test_workspace_too_small_is_reported(lib):
+    buf = ctypes.create_string_buffer(1024 + 256)
+    addr = (ctypes.addressof(buf) + 255) // 256 * 256
+    m = ctypes.c_float(0.0)
+    rc = lib.gmmxx_em_prepare(_native.DIAG, 1, 4, 3, ctypes.addressof(m), ctypes.addressof(m), ctypes.addressof(m),
+                              1e-6, 1e-8, addr, 16, None)
+    assert rc == _native.ERR_WORKSPACE

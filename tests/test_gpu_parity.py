@@ -1,0 +1,191 @@
+"""GPU parity: the CUDA engine against the reference's golden vectors and the
+numpy oracle (all four covariance types, fp32 / bf16 / fp16 inputs, edge
+shapes).  Tolerances are the north-star contract: fp32 parameters within
+1e-4 relative (atol 1e-4), mean log-likelihood within 1e-4 relative (1e-3 for
+bf16 inputs), labels >= 99.9 % identical."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden_cases, load_golden
+
+pytestmark = pytest.mark.gpu
+
+PARAM_TOL = dict(rtol=1e-4, atol=1e-4)
+
+
+def _fit(cov, x, k, iters, init_means, init_var, init_w, reg=1e-6):
+    from gmmxx_b200 import engine
+
+    return engine.em_fit(cov, x, k, max_iters=iters, tol=0.0, init_means=init_means, init_variances=init_var,
+                         init_weights=init_w, reg_covar=reg)
+
+
+def test_canary(cuda_device):
+    from gmmxx_b200 import engine
+
+    x = torch.arange(1000, dtype=torch.int32, device=cuda_device)
+    assert torch.equal(engine.canary_add_offset(x, 7).cpu(), (x + 7).cpu())
+
+
+@pytest.mark.parametrize("case", golden_cases())
+def test_fit_matches_reference_golden(cuda_device, case):
+    g = load_golden(case)
+    cov = str(g["cov_type"])
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    labels, means, c, w, info = _fit(cov, t(g["x"]), int(g["n_components"]), int(g["iters"]), t(g["init_means"]),
+                                     t(g["init_var"]), t(g["init_weights"]), float(g["reg_covar"]))
+    np.testing.assert_allclose(means.cpu().numpy(), g["means"], **PARAM_TOL)
+    np.testing.assert_allclose(c.cpu().numpy(), g["cov"], **PARAM_TOL)
+    np.testing.assert_allclose(w.cpu().numpy(), g["weights"], **PARAM_TOL)
+    ref_lb = g["lower_bound_history"]
+    assert len(info["lower_bound_history"]) == len(ref_lb)
+    np.testing.assert_allclose(np.array(info["lower_bound_history"]), ref_lb, rtol=1e-4, atol=1e-5)
+    assert (labels.cpu().numpy() == g["labels"]).mean() >= 0.999
+
+
+@pytest.mark.parametrize("case", golden_cases())
+def test_inference_matches_reference_golden(cuda_device, case):
+    from gmmxx_b200 import engine
+
+    g = load_golden(case)
+    cov = str(g["cov_type"])
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    args = (cov, t(g["x"]), t(g["means"]), t(g["cov"]), t(g["weights"]))
+    assert (engine.assign(*args).cpu().numpy() == g["assign"]).mean() >= 0.999
+    np.testing.assert_allclose(engine.score_samples(*args).cpu().numpy(), g["score_samples"], rtol=1e-5, atol=2e-4)
+    np.testing.assert_allclose(engine.predict_proba(*args).cpu().numpy(), g["predict_proba"], rtol=1e-4, atol=2e-5)
+    lse = engine.score_samples(*args)
+    r = engine.resp(*args, lse)
+    np.testing.assert_allclose(r.cpu().numpy(), g["predict_proba"], rtol=1e-4, atol=2e-5)
+
+
+def _mixture(seed, b, n, d, k, spread=6.0):
+    rng = np.random.default_rng(seed)
+    centers = rng.uniform(-spread, spread, size=(b, k, d)).astype(np.float32)
+    sig = rng.uniform(0.5, 1.5, size=(b, k)).astype(np.float32)
+    comp = rng.integers(0, k, size=(b, n))
+    x = np.take_along_axis(centers, comp[..., None], 1) + np.take_along_axis(sig, comp, 1)[..., None] * \
+        rng.standard_normal((b, n, d)).astype(np.float32)
+    init = np.stack([x[i, rng.choice(n, k, replace=False)] for i in range(b)]).astype(np.float32)
+    return x.astype(np.float32), init
+
+
+def _init_cov(cov, x, k):
+    return {"spherical": oracle.global_spherical_variance, "diag": oracle.global_diag_variance,
+            "full": oracle.global_full_covariance}[cov](x, k, 1e-6) if cov != "tied" else \
+        oracle.global_tied_covariance(x, 1e-6)
+
+
+@pytest.mark.parametrize("cov,b,n,d,k", [
+    ("spherical", 2, 3000, 16, 70),     # K spans two component tiles
+    ("spherical", 1, 777, 128, 5),      # D at the window edge, ragged N
+    ("diag", 2, 2500, 24, 65),
+    ("diag", 1, 1000, 128, 3),
+    ("tied", 2, 2000, 12, 9),
+    ("tied", 1, 1500, 64, 20),
+    ("full", 3, 1200, 6, 4),
+    ("full", 1, 2000, 16, 32),          # config-3 problem shape (small N)
+    ("full", 1, 800, 26, 3),            # full window edge
+])
+def test_fit_matches_oracle(cuda_device, cov, b, n, d, k):
+    x, init = _mixture(11 + d + k, b, n, d, k)
+    icov = _init_cov(cov, x, k)
+    w = np.full((b, k), 1.0 / k, np.float32)
+    ref = oracle.fit(cov, x, k, 4, 0.0, init, icov, w)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    labels, means, c, wt, info = _fit(cov, t(x), k, 4, t(init), t(icov), t(w))
+    np.testing.assert_allclose(means.cpu().numpy(), ref[1], **PARAM_TOL)
+    np.testing.assert_allclose(c.cpu().numpy(), ref[2], **PARAM_TOL)
+    np.testing.assert_allclose(wt.cpu().numpy(), ref[3], **PARAM_TOL)
+    assert abs(info["lower_bound"] - ref[4]["lower_bound"]) <= 1e-4 * abs(ref[4]["lower_bound"])
+    assert (labels.cpu().numpy() == ref[0]).mean() >= 0.999
+
+
+@pytest.mark.parametrize("cov", ["spherical", "diag", "tied", "full"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_half_inputs_match_upcast(cuda_device, cov, dtype):
+    """bf16 / fp16 X is read as stored and computed in fp32: identical to the
+    reference's upcast of the same values (interface.py:426-433)."""
+    d = 16 if cov != "full" else 6
+    x, init = _mixture(5, 1, 2000, d, 6, spread=4.0)
+    xh = torch.from_numpy(x).to(dtype)
+    xf = xh.float().numpy()
+    icov = _init_cov(cov, xf, 6)
+    w = np.full((1, 6), 1 / 6, np.float32)
+    ref = oracle.fit(cov, xf, 6, 3, 0.0, init, icov, w)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    labels, means, c, wt, info = _fit(cov, xh.to(cuda_device), 6, 3, t(init), t(icov), t(w))
+    np.testing.assert_allclose(means.cpu().numpy(), ref[1], **PARAM_TOL)
+    np.testing.assert_allclose(c.cpu().numpy(), ref[2], **PARAM_TOL)
+    assert abs(info["lower_bound"] - ref[4]["lower_bound"]) <= 1e-3 * abs(ref[4]["lower_bound"])
+
+
+def test_edge_shapes(cuda_device):
+    from gmmxx_b200 import engine
+
+    # N = 1, K = 1, D = 1
+    x = torch.tensor([[[2.5]]], device=cuda_device)
+    labels, means, c, w, info = engine.em_fit("spherical", x, 1, max_iters=2, tol=0.0,
+                                              init_means=torch.tensor([[[0.0]]]), reg_covar=1e-6)
+    assert float(means[0, 0, 0]) == pytest.approx(2.5)
+    assert float(c[0, 0]) == pytest.approx(1e-6)
+    assert int(labels[0, 0]) == 0
+    # more components than samples: empty components keep their parameters
+    x = torch.randn(1, 3, 2, device=cuda_device)
+    init = torch.cat([x[:, :3], torch.full((1, 2, 2), 50.0, device=cuda_device)], 1)
+    labels, means, c, w, info = engine.em_fit("diag", x, 5, max_iters=3, tol=0.0, init_means=init)
+    assert torch.allclose(means[0, 3:], torch.full((2, 2), 50.0, device=cuda_device))
+
+
+def test_empty_input_rejected(cuda_device):
+    import gmmxx_b200
+
+    with pytest.raises(ValueError):
+        gmmxx_b200.batch_gmm_Diagonal(torch.empty(1, 0, 4, device=cuda_device), 3)
+
+
+def test_estimator_end_to_end(cuda_device):
+    from gmmxx_b200 import GMMXX
+
+    x, _ = _mixture(3, 1, 4000, 8, 5)
+    xt = torch.from_numpy(x[0]).to(cuda_device)
+    for cov in ("spherical", "diag", "tied", "full"):
+        g = GMMXX(k=5, niter=10, covariance_type=cov, backend="cuda", seed=1).fit(xt)
+        assert g.means_.shape == (5, 8)
+        assert g.labels_.shape == (4000,)
+        p = g.predict_proba(xt)
+        assert torch.allclose(p.sum(-1), torch.ones(4000, device=cuda_device), atol=1e-4)
+        assert torch.equal(g.predict(xt), p.argmax(-1)) or (g.predict(xt) == p.argmax(-1)).float().mean() > 0.999
+        s = g.score_samples(xt)
+        assert s.shape == (4000,)
+        assert np.isfinite(g.bic(xt)) and np.isfinite(g.aic(xt))
+        assert g.score(xt) == pytest.approx(float(s.mean()))
+
+
+def test_streamed_fit_matches_resident_fit(cuda_device):
+    from gmmxx_b200 import engine, large_n
+
+    x, init = _mixture(9, 1, 10000, 12, 7)
+    icov = oracle.global_diag_variance(x, 7, 1e-6)
+    w = np.full((1, 7), 1 / 7, np.float32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    a = engine.em_fit("diag", t(x).to(cuda_device), 7, max_iters=5, tol=0.0, init_means=t(init),
+                      init_variances=t(icov), init_weights=t(w))
+    b = large_n.em_fit_streamed("diag", t(x), 7, device=cuda_device, chunk_rows=1500, max_iters=5, tol=0.0,
+                                init_means=t(init), init_variances=t(icov), init_weights=t(w))
+    for u, v in zip(a[1:4], b[1:4]):
+        np.testing.assert_allclose(u.cpu().numpy(), v.cpu().numpy(), rtol=1e-5, atol=1e-5)
+    assert torch.equal(a[0], b[0])
+
+
+def test_repeat_runs_agree(cuda_device):
+    """Determinism harness: two runs differ by no more than atomic-order noise."""
+    x, init = _mixture(21, 1, 20000, 32, 40)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    r1 = _fit("spherical", t(x), 40, 5, t(init), None, None)
+    r2 = _fit("spherical", t(x), 40, 5, t(init), None, None)
+    np.testing.assert_allclose(r1[1].cpu().numpy(), r2[1].cpu().numpy(), rtol=1e-5, atol=1e-5)
+    assert (r1[0] == r2[0]).float().mean().item() >= 0.999
