@@ -29,6 +29,7 @@ ERR_UNSUPPORTED = 2
 ERR_CUDA = 3
 ERR_NOT_PD = 4
 ERR_WORKSPACE = 5
+ERR_TIMEOUT = 6
 
 # Windows of the compiled kernels (mirrors gmm_common.cuh).
 MAX_D = 128

@@ -138,7 +138,8 @@ int gmmxx_workspace_status(void* workspace, int* status_out, void* stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, sizeof(int), st);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "workspace status read: %s", cudaGetErrorString(e));
-  *status_out = (host & (1 << GMMXX_ERR_NOT_PD)) ? GMMXX_ERR_NOT_PD : GMMXX_OK;
+  *status_out = (host & (1 << GMMXX_ERR_TIMEOUT)) ? GMMXX_ERR_TIMEOUT
+                : (host & (1 << GMMXX_ERR_NOT_PD)) ? GMMXX_ERR_NOT_PD : GMMXX_OK;
   return GMMXX_OK;
 }
 

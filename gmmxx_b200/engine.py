@@ -74,7 +74,8 @@ class Workspace:
     def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
         buf = self._buf.get(device)
         if buf is None or buf.numel() < nbytes:
-            buf = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            # zero-filled: the first word is the C ABI's sticky status word
+            buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
             self._buf[device] = buf
         return buf
 
@@ -226,6 +227,8 @@ class CudaOps:
     def check_status(self) -> None:
         status = ctypes_int()
         nat.call("gmmxx_workspace_status", self.ws.data_ptr(), status.ref(), self.stream)
+        if status.value == nat.ERR_TIMEOUT:
+            raise nat.GmmxxError(status.value, "a bounded device-side wait expired in the EM kernel")
         if status.value != nat.OK:
             raise nat.GmmxxError(status.value, "covariance not positive definite after the jitter ladder")
 

@@ -66,7 +66,8 @@ enum gmmxx_status {
   GMMXX_ERR_UNSUPPORTED = 2,  /* shape outside the compiled kernel windows    */
   GMMXX_ERR_CUDA = 3,         /* CUDA runtime / launch error                  */
   GMMXX_ERR_NOT_PD = 4,       /* covariance not positive definite (device)    */
-  GMMXX_ERR_WORKSPACE = 5     /* workspace too small                          */
+  GMMXX_ERR_WORKSPACE = 5,    /* workspace too small                          */
+  GMMXX_ERR_TIMEOUT = 6       /* a bounded device-side wait expired (device)  */
 };
 
 /* ---- library / lifecycle ------------------------------------------------ */
@@ -85,11 +86,13 @@ GMMXX_API int gmmxx_canary_add_offset(const int32_t* in, int32_t* out, int64_t n
 GMMXX_API int64_t gmmxx_stat_width(int cov_type, int64_t D);
 
 /* Bytes of device scratch a call needs for these sizes.  One workspace may be
- * reused by successive calls on the same stream. */
+ * reused by successive calls on the same stream.  A new workspace must start
+ * zero-filled (its first word is the sticky status word read by
+ * gmmxx_workspace_status). */
 GMMXX_API size_t gmmxx_workspace_bytes(int cov_type, int64_t B, int64_t N, int64_t D, int64_t K);
 
 /* Reads (and clears) the sticky device status word kept in `workspace`
- * (GMMXX_OK or GMMXX_ERR_NOT_PD).  Synchronises `stream`. */
+ * (GMMXX_OK, GMMXX_ERR_NOT_PD or GMMXX_ERR_TIMEOUT).  Synchronises `stream`. */
 GMMXX_API int gmmxx_workspace_status(void* workspace, int* status_out, void* stream);
 
 /* ---- one soft-EM iteration, in the three steps a sharded driver needs ---- */
