@@ -39,6 +39,10 @@ int launch_xx_total(const void* x, int dt, int64_t B, int64_t N, int D, float* x
 }  // namespace gmmxx
 
 #include "rows_api.cuh"
+#include "tc_api.cuh"
+
+#include <stdlib.h>
+#include <string.h>
 
 using namespace gmmxx;
 
@@ -66,6 +70,18 @@ int check_ws(const void* ws, size_t bytes, const Layout& L) {
     return set_error(GMMXX_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %lld bytes required", bytes,
                      (long long)L.total);
   return GMMXX_OK;
+}
+
+// Kernel selection (GMMXX_B200_KERNEL): "auto" (default) uses the
+// tensor-core kernel where the shape allows it and the CUDA-core kernels
+// otherwise; "simt" always uses the exact-fp32 CUDA-core kernels; "tc"
+// requires the tensor-core kernel and fails if it cannot run.
+int kernel_mode() {
+  const char* e = getenv("GMMXX_B200_KERNEL");
+  if (e == nullptr) return 0;
+  if (strcmp(e, "simt") == 0) return 1;
+  if (strcmp(e, "tc") == 0) return 2;
+  return 0;
 }
 
 #define GMMXX_REQUIRE(p, name) \
@@ -168,6 +184,32 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
   if (int rc = check_ws(workspace, workspace_bytes, L)) return rc;
   char* ws = static_cast<char*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int mode = kernel_mode();
+  const bool tc_ok = L.tc_cluster > 0 && x_dtype == GMMXX_BFLOAT16;
+  if (mode == 2 && !tc_ok)
+    return set_error(GMMXX_ERR_UNSUPPORTED, "tensor-core kernel required but the shape / dtype is outside its window");
+  if (tc_ok && mode != 1) {
+    tc::TcLaunch t{};
+    t.x = x;
+    t.N = N;
+    t.D = (int)D;
+    t.K = (int)K;
+    t.Kp_table = L.Kp;
+    t.Kp_part = (int64_t)L.tc_cluster * 128;
+    t.F = stat_width(cov_type, (int)D);
+    t.cluster_size = L.tc_cluster;
+    t.wt = reinterpret_cast<const float*>(ws + L.wt);
+    t.cc = reinterpret_cast<const CompConst*>(ws + L.cc);
+    t.params = ws + L.tc_params;
+    t.consts = reinterpret_cast<float*>(ws + L.tc_consts);
+    t.part = reinterpret_cast<float*>(ws + L.tc_part);
+    t.part_ll = reinterpret_cast<double*>(ws + L.tc_part_ll);
+    t.status = reinterpret_cast<int*>(ws + L.status);
+    t.stats = stats;
+    t.ll = log_likelihood;
+    const int rc = tc::launch_em_tc(cov_type, t, st);
+    if (rc != GMMXX_ERR_UNSUPPORTED || mode == 2) return rc;  // else: no co-resident cluster -> CUDA-core kernels
+  }
   RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
   a.lse_out = reinterpret_cast<float*>(ws + L.lse);
   a.ll = log_likelihood;

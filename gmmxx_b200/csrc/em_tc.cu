@@ -1,0 +1,621 @@
+// em_tc.cu -- fused soft-EM statistics kernel on the 5th-generation tensor
+// cores (tcgen05 + TMEM + TMA), for bf16 X with diagonal (D = 64, K <= 512)
+// or spherical (D = 64 / 128, K <= 1024) covariance, B == 1.
+//
+// One thread-block cluster of C = ceil(K / 128) CTAs works on the same
+// 128-row tile of X at a time; CTA `rank` owns components
+// [128 rank, 128 rank + 128) whose split-bf16 logit weights stay resident in
+// its shared memory for the whole launch.  Per row tile:
+//
+//   TMA          X tile (bf16, 128-byte swizzle) -> shared memory
+//   prep warps   exact x^2 = s_hi + s_lo (two bf16, diag) / |x|^2 (spherical)
+//   MMA warp     E-step  S[128 rows, 128 comps] (TMEM, fp32) = features . W^T
+//   softmax WG   logits from S, row max / exp / partial sum -> DSMEM exchange
+//                of (max, sum) with the cluster peers -> r = exp(l - lse),
+//                split r = r_hi + r_lo (two bf16) into shared memory
+//   MMA warp     M-step  stats[128 comps, F] (TMEM, fp32) += R^T . [x | x^2 | 1]
+//
+// so the (N, K) responsibilities never leave the SM and X is read from HBM
+// once per iteration.  Precision: X is exact in bf16; x^2 is split exactly
+// into two bf16 terms; the logit weights into three bf16 terms (24
+// significant bits, fp32-equivalent); r into two (16 bits).  Products are exact
+// and accumulate in fp32, so logits match the fp32 expanded-distance form.
+// Statistics leave the kernel once per cluster as partials that a second
+// kernel reduces in a fixed order (run-to-run deterministic).
+//
+// Reference semantics: gmmxx/torch_fallback.py:2097-2291 (spherical E/M
+// chunk loop) and 2508-2651 (diag), expanded-distance logits 337-397.
+#include "gmm_common.cuh"
+#include "tc_ptx.cuh"
+#include "tc_api.cuh"
+
+#include <math.h>
+
+#include <algorithm>
+
+namespace gmmxx {
+namespace tc {
+
+using namespace ptx;
+
+constexpr int kBM = 128;          // rows per tile (UMMA M of the E-step)
+constexpr int kKC = 128;          // components per CTA
+constexpr int kNS = 3;            // bf16 terms of the split component weights (24 significant bits)
+constexpr int kThreads = 256;     // 8 warps
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kDmCol = 256;  // M-step accumulator columns [256, 256 + FDM)
+constexpr int kBlock = 16384;     // one [128][64] bf16 swizzled block
+constexpr int kAuxBytes = 4096;   // [16][128] K-major aux operand (1, |x|^2 hi / lo)
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+enum Warp { kWarpTma = 0, kWarpMma = 1, kWarpPrep0 = 2, kWarpSoftmax0 = 4 };
+
+// Shared-memory carve-up (byte offsets from a 1024-aligned base).
+//   diag      : weights (a_j, v_j) | stages{X, SH} x2 | SL (single) | aux (constant)
+//   spherical : weights (a_j)      | stages{X, aux} x2
+//   then R (two 64-component MN groups), constants, q, exchange slots, barriers.
+template <int COV, int DB>
+struct Cfg {
+  static constexpr int D = 64 * DB;
+  static constexpr bool kDiag = (COV == GMMXX_DIAG);
+  static constexpr int kParamBlocks = kDiag ? 2 * kNS * DB : kNS * DB;
+  static constexpr int kParams = 0;
+  static constexpr int kStage0 = kParams + kParamBlocks * kBlock;
+  static constexpr int kStageBytes = kDiag ? 2 * DB * kBlock : DB * kBlock + kAuxBytes;
+  static constexpr int kSL = kStage0 + 2 * kStageBytes;               // diag only
+  static constexpr int kAuxConst = kSL + (kDiag ? DB * kBlock : 0);   // diag only
+  static constexpr int kR = kAuxConst + (kDiag ? kAuxBytes : 0);
+  static constexpr int kConsts = kR + 2 * kBlock;  // mpm[128], h[128], c2[128]
+  static constexpr int kQ = kConsts + 3 * 128 * 4; // q[2][128] (spherical)
+  static constexpr int kXch = kQ + (kDiag ? 0 : 2 * 128 * 4);
+  __host__ __device__ static constexpr int xch_bytes(int C) { return 2 * C * 128 * 8; }
+  __host__ __device__ static constexpr int bars(int C) { return kXch + xch_bytes(C); }
+  __host__ __device__ static constexpr int total(int C) { return bars(C) + 256 + 1024; }
+  // feature blocks of stage s (byte offsets)
+  __host__ __device__ static constexpr int x_blk(int s, int db) { return kStage0 + s * kStageBytes + db * kBlock; }
+  __host__ __device__ static constexpr int sh_blk(int s, int db) { return kStage0 + s * kStageBytes + (DB + db) * kBlock; }
+  __host__ __device__ static constexpr int sl_blk(int db) { return kSL + db * kBlock; }
+  __host__ __device__ static constexpr int aux(int s) {
+    return kDiag ? kAuxConst : kStage0 + s * kStageBytes + DB * kBlock;
+  }
+  // weight blocks: a_j (x coefficient), v_j (x^2 coefficient, diag)
+  __host__ __device__ static constexpr int a_blk(int j, int db) { return kParams + (j * DB + db) * kBlock; }
+  __host__ __device__ static constexpr int v_blk(int j, int db) { return kParams + ((kNS + j) * DB + db) * kBlock; }
+  // M-step accumulator columns: [x (D) | x^2 (D, diag) | aux (16)]
+  static constexpr int kAuxCol = kDiag ? 2 * D : D;
+  static constexpr int kFdm = kAuxCol + 16;
+};
+
+struct Bars {
+  uint64_t params;
+  uint64_t xfull[2];   // TMA: X tile landed
+  uint64_t fmain[2];   // prep: SH (diag) / |x|^2 (spherical) ready
+  uint64_t fl;         // prep: SL ready (diag)
+  uint64_t slfree;     // MMA: M-step high part done reading SL (diag)
+  uint64_t fempty[2];  // MMA: stage free for the next TMA
+  uint64_t sfull[2];   // MMA: S tile complete
+  uint64_t sfree[2];   // softmax: S tile consumed
+  uint64_t rfull;      // softmax: R part written
+  uint64_t rfree;      // MMA: R part consumed
+  uint64_t xch[2];     // cluster exchange of (row max, row sum)
+  uint64_t mdone;      // MMA: all MMAs issued and complete
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void set_abort(Bars* b, int* status) {
+  b->abort = 1;
+  atomicOr(status, 1 << GMMXX_ERR_TIMEOUT);
+}
+
+template <int COV, int DB>
+__global__ void __launch_bounds__(kThreads, 1)
+    em_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
+  using C = Cfg<COV, DB>;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nclus = a.cluster_size;
+  Bars* bars = reinterpret_cast<Bars*>(sm + C::bars(nclus));
+  float* c_mpm = reinterpret_cast<float*>(sm + C::kConsts);
+  float* c_h = c_mpm + 128;
+  float* c_c2 = c_h + 128;
+  float* qbuf = reinterpret_cast<float*>(sm + C::kQ);
+  float2* xch = reinterpret_cast<float2*>(sm + C::kXch);
+  volatile int* abort = &bars->abort;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const uint32_t cid = cluster_id_x();
+  const uint32_t ncl = ncluster_x();
+  const int64_t ntiles = (a.N + kBM - 1) / kBM;
+  const int T = (int)((ntiles > (int64_t)cid) ? (ntiles - 1 - cid) / ncl + 1 : 0);
+
+  if (tid == 0) {
+    mbar_init(&bars->params, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->xfull[i], 1);
+      mbar_init(&bars->fmain[i], 2);
+      mbar_init(&bars->fempty[i], 1);
+      mbar_init(&bars->sfull[i], 1);
+      mbar_init(&bars->sfree[i], 4);
+      mbar_init(&bars->xch[i], 1);
+    }
+    mbar_init(&bars->fl, 2);
+    mbar_init(&bars->slfree, 1);
+    mbar_init(&bars->rfull, 4);
+    mbar_init(&bars->rfree, 1);
+    mbar_init(&bars->mdone, 1);
+    bars->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kWarpMma) tmem_alloc(&bars->tmem_base, kTmemCols);
+  // constants of this CTA's component chunk; constant rows of the aux operand(s)
+  for (int i = tid; i < 3 * 128; i += kThreads) c_mpm[i] = a.consts[(int64_t)rank * 3 * 128 + i];
+  for (int s = 0; s < (C::kDiag ? 1 : 2); ++s) {
+    char* aux = sm + C::aux(s);
+    for (int i = tid; i < 16 * 128; i += kThreads) {
+      const int n = i >> 7, r = i & 127;
+      *reinterpret_cast<__nv_bfloat16*>(aux + (r >> 6) * 2048 + sw128(n, r & 63)) =
+          __float2bfloat16(n == 0 ? 1.f : 0.f);
+    }
+  }
+  fence_proxy_async();
+  tmem_fence_before();
+  __syncthreads();
+  cluster_sync();  // peers' barriers initialised before any DSMEM traffic
+  tmem_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == kWarpTma) {
+    // ---------------- producer: component weights once, then X tiles ----------------
+    if (lane == 0) {
+      prefetch_tmap(&tmap);
+      mbar_expect_tx(&bars->params, C::kParamBlocks * kBlock);
+      const char* src = a.params + (int64_t)rank * C::kParamBlocks * kBlock;
+      for (int i = 0; i < C::kParamBlocks; ++i)
+        bulk_load(sm + C::kParams + i * kBlock, src + (int64_t)i * kBlock, kBlock, &bars->params);
+      for (int t = 0; t < T; ++t) {
+        const int s = t & 1;
+        if (t >= 2 && !mbar_wait(&bars->fempty[s], ((t >> 1) - 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        const int row0 = (int)((cid + (int64_t)t * ncl) * kBM);
+        mbar_expect_tx(&bars->xfull[s], DB * kBlock);
+        for (int db = 0; db < DB; ++db) tma_load_2d(sm + C::x_blk(s, db), &tmap, db * 64, row0, &bars->xfull[s]);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ---------------- MMA issuer (one thread) ----------------
+    if (lane == 0) {
+      const uint32_t id_e = idesc_bf16(128, kKC, 0, 0);
+      const uint32_t id_m = idesc_bf16(128, 64, 1, 1);
+      const uint32_t id_aux = idesc_bf16(128, 16, 1, 0);
+      const uint32_t base = smem_u32(sm);
+      const uint32_t r_base = base + C::kR;
+      bool ok = mbar_wait(&bars->params, 0, abort);
+      tmem_fence_after();
+      // one K=64 feature block times one K=64 weight block (4 MMAs of K=16)
+      auto block_mma = [&](uint32_t d, uint32_t fa, uint32_t wb, uint32_t& acc) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16(d, desc_kmajor(fa + kk * 32), desc_kmajor(wb + kk * 32), id_e, acc);
+          acc = 1;
+        }
+      };
+      // E-step, main part: x . a_j (+ s_hi . v_j for diag) into S[t & 1]
+      auto issue_e_main = [&](int t) -> bool {
+        const int s = t & 1;
+        if (!mbar_wait(&bars->fmain[s], (t >> 1) & 1, abort)) return false;
+        if (t >= 2 && !mbar_wait(&bars->sfree[s], ((t >> 1) - 1) & 1, abort)) return false;
+        tmem_fence_after();
+        const uint32_t d = tmem + (uint32_t)(s * kKC);
+        uint32_t acc = 0;
+        for (int db = 0; db < DB; ++db) {
+#pragma unroll
+          for (int j = 0; j < kNS; ++j) block_mma(d, base + C::x_blk(s, db), base + C::a_blk(j, db), acc);
+          if (C::kDiag) {
+#pragma unroll
+            for (int j = 0; j < kNS; ++j) block_mma(d, base + C::sh_blk(s, db), base + C::v_blk(j, db), acc);
+          }
+        }
+        if (!C::kDiag) mma_commit(&bars->sfull[s]);
+        return true;
+      };
+      // E-step, residual part (diag): s_lo . v_0 + s_lo . v_1, then S[t & 1] is complete
+      auto issue_e_lo = [&](int t) -> bool {
+        const int s = t & 1;
+        if (!mbar_wait(&bars->fl, t & 1, abort)) return false;
+        tmem_fence_after();
+        const uint32_t d = tmem + (uint32_t)(s * kKC);
+        uint32_t acc = 1;
+        for (int db = 0; db < DB; ++db) {
+          block_mma(d, base + C::sl_blk(db), base + C::v_blk(0, db), acc);
+          block_mma(d, base + C::sl_blk(db), base + C::v_blk(1, db), acc);
+        }
+        mma_commit(&bars->sfull[s]);
+        return true;
+      };
+      // M-step of tile t with R part `part` (0 = high bf16 terms, 1 = residual)
+      auto issue_m = [&](int t, int part) -> bool {
+        const int s = t & 1;
+        const int use = 2 * t + part;
+        if (!mbar_wait(&bars->rfull, use & 1, abort)) return false;
+        tmem_fence_after();
+        const uint32_t aux = base + C::aux(s);
+        const bool first = (t == 0 && part == 0);
+        for (int ks = 0; ks < 8; ++ks) {  // 16 rows per instruction
+          const uint64_t ra = desc_mnmajor(r_base + ks * 2048, kBlock);
+          const uint32_t acc = (first && ks == 0) ? 0u : 1u;
+          for (int db = 0; db < DB; ++db)
+            mma_bf16(tmem + kDmCol + db * 64, ra, desc_mnmajor(base + C::x_blk(s, db) + ks * 2048, kBlock), id_m,
+                     acc);
+          if (C::kDiag) {
+            for (int db = 0; db < DB; ++db) {
+              const uint32_t dcol = tmem + kDmCol + C::D + db * 64;
+              mma_bf16(dcol, ra, desc_mnmajor(base + C::sh_blk(s, db) + ks * 2048, kBlock), id_m, acc);
+              if (part == 0)
+                mma_bf16(dcol, ra, desc_mnmajor(base + C::sl_blk(db) + ks * 2048, kBlock), id_m, 1u);
+            }
+          }
+          mma_bf16(tmem + kDmCol + C::kAuxCol, ra, desc_kmajor(aux + (ks >> 2) * 2048 + (ks & 3) * 32), id_aux, acc);
+        }
+        mma_commit(&bars->rfree);
+        if (C::kDiag && part == 0) mma_commit(&bars->slfree);
+        if (part == 1) mma_commit(&bars->fempty[s]);
+        return true;
+      };
+      if (ok && T > 0) ok = issue_e_main(0) && (!C::kDiag || issue_e_lo(0));
+      for (int t = 0; ok && t < T; ++t) {
+        const bool more = t + 1 < T;
+        if (more && !issue_e_main(t + 1)) { ok = false; break; }
+        if (!issue_m(t, 0)) { ok = false; break; }
+        if (C::kDiag && more && !issue_e_lo(t + 1)) { ok = false; break; }
+        if (!issue_m(t, 1)) { ok = false; break; }
+      }
+      if (!ok) set_abort(bars, a.status);
+      mma_commit(&bars->mdone);
+    }
+  } else if (warp < kWarpSoftmax0) {
+    // ---------------- feature prep (2 warps) ----------------
+    const int ptid = tid - kWarpPrep0 * 32;  // 0..63
+    for (int t = 0; t < T; ++t) {
+      const int s = t & 1;
+      if (!mbar_wait_warp(&bars->xfull[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
+      if (C::kDiag) {
+        // x^2 = s_hi + s_lo exactly (bf16 x has 8 significant bits).  The
+        // buffers share one swizzled layout, so the map is elementwise.
+        for (int half = 0; half < 2; ++half) {
+          if (half == 1) {
+            // SL is single-buffered: wait until the previous tile's M-step high part read it
+            if (t >= 1 && !mbar_wait_warp(&bars->slfree, (t - 1) & 1, abort)) { set_abort(bars, a.status); break; }
+          }
+          for (int db = 0; db < DB; ++db) {
+            const uint4* xs = reinterpret_cast<const uint4*>(sm + C::x_blk(s, db));
+            uint4* dst = reinterpret_cast<uint4*>(sm + (half == 0 ? C::sh_blk(s, db) : C::sl_blk(db)));
+            for (int c = ptid; c < kBlock / 16; c += 64) {
+              const uint4 v = xs[c];
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+              uint32_t o[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
+                const float s0 = x0 * x0, s1 = x1 * x1;  // exact in fp32
+                const uint32_t hi = pack_bf16(s0, s1);
+                o[i] = half == 0 ? hi : pack_bf16(s0 - bf16lo_to_f32(hi), s1 - bf16hi_to_f32(hi));
+              }
+              dst[c] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(half == 0 ? &bars->fmain[s] : &bars->fl);
+        }
+        if (*abort) break;
+      } else {
+        // |x|^2 per row (two threads per row), q_hi / q_lo into the aux operand
+        char* aux = sm + C::aux(s);
+        const int r = ptid >> 1, hf = ptid & 1;
+        for (int rr = r; rr < kBM; rr += 32) {
+          float acc = 0.f;
+          for (int db = 0; db < DB; ++db)
+            for (int c = hf * 4; c < hf * 4 + 4; ++c) {
+              const uint4 v = *reinterpret_cast<const uint4*>(sm + C::x_blk(s, db) + rr * 128 + c * 16);
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
+                acc = fmaf(x0, x0, acc);
+                acc = fmaf(x1, x1, acc);
+              }
+            }
+          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+          if (hf == 0) {
+            qbuf[s * 128 + rr] = acc;
+            const __nv_bfloat16 qh = __float2bfloat16(acc);
+            const __nv_bfloat16 ql = __float2bfloat16(acc - __bfloat162float(qh));
+            char* blk = aux + (rr >> 6) * 2048;
+            *reinterpret_cast<__nv_bfloat16*>(blk + sw128(1, rr & 63)) = qh;
+            *reinterpret_cast<__nv_bfloat16*>(blk + sw128(2, rr & 63)) = ql;
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->fmain[s]);
+      }
+    }
+  } else {
+    // ---------------- softmax warpgroup: one thread per row ----------------
+    const int q4 = warp & 3;               // TMEM lane quarter of this warp
+    const int row = q4 * 32 + lane;        // row within the tile
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    double ll_acc = 0.0;
+    float p[kKC];
+    const uint32_t xch_mine = smem_u32(&xch[(int)rank * 128 + row]);  // slot 0 entry of (this rank, row)
+    const uint32_t slot_stride = (uint32_t)(nclus * 128 * 8);
+    for (int t = 0; t < T; ++t) {
+      const int s = t & 1;
+      const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
+      const bool valid = grow < a.N;
+      if (!mbar_wait_warp(&bars->sfull[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
+      tmem_fence_after();
+      const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC);
+#pragma unroll
+      for (int c = 0; c < kKC; c += 32) tmem_ld32(sc + c, p + c);
+      tmem_wait_ld();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->sfree[s]);
+      // logits (log2 units) and the CTA-local row max
+      float qn = 0.f;
+      if (!C::kDiag) {  // |x|^2 of this row (signalled by the prep warps before S was issued)
+        if (!mbar_wait_warp(&bars->fmain[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        qn = qbuf[s * 128 + row];
+      }
+      float m = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kKC; ++k) {
+        const float dist = fmaxf(p[k] + c_mpm[k] + qn, 0.f);
+        const float l = fmaf(-c_h[k], dist, c_c2[k]);
+        p[k] = l;
+        m = fmaxf(m, l);
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < kKC; ++k) {
+        p[k] = exp2f(p[k] - m);
+        sum += p[k];
+      }
+      // exchange (max, sum) of this row with every CTA of the cluster
+      if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
+      for (int q = 0; q < nclus; ++q)
+        st_async_f2(map_shared(xch_mine + s * slot_stride, q), m, sum, map_shared(smem_u32(&bars->xch[s]), q));
+      if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
+      float M = -INFINITY;
+      for (int q = 0; q < nclus; ++q) M = fmaxf(M, xch[(s * nclus + q) * 128 + row].x);
+      float S = 0.f;
+      for (int q = 0; q < nclus; ++q) {
+        const float2 e = xch[(s * nclus + q) * 128 + row];
+        S += e.y * exp2f(e.x - M);
+      }
+      const float f = valid ? exp2f(m - M) / S : 0.f;
+      if (valid && rank == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
+      // responsibilities -> R (two passes: bf16 high part, then the residual)
+      for (int part = 0; part < 2; ++part) {
+        const int use = 2 * t + part;
+        if (use >= 1 && !mbar_wait_warp(&bars->rfree, (use - 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        char* rb = sm + C::kR;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int k0 = g * 64 + c * 8 + 2 * i;
+              const float r0 = p[k0] * f, r1 = p[k0 + 1] * f;
+              const uint32_t h = pack_bf16(r0, r1);
+              w[i] = part == 0 ? h : pack_bf16(r0 - bf16lo_to_f32(h), r1 - bf16hi_to_f32(h));
+            }
+            *reinterpret_cast<uint4*>(rb + g * kBlock + sw128((uint32_t)row, (uint32_t)(c * 8))) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->rfull);
+      }
+      if (*abort) break;
+    }
+    // ---------------- epilogue: statistics partials ----------------
+    // drain: the MMA thread always commits `mdone` (also after an abort), so
+    // wait for it without the abort shortcut before touching TMEM again
+    if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 4000000000ull)) set_abort(bars, a.status);
+    tmem_fence_after();
+    const int comp = (int)rank * kKC + row;  // this thread's TMEM lane = component
+    float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
+    for (int c0 = 0; c0 < C::kFdm; c0 += 16) {
+      float v[32];
+      tmem_ld32(tmem + lane_addr + kDmCol + c0, v);  // 32 columns; 16 used per step
+      tmem_wait_ld();
+      for (int j = 0; j < 16 && c0 + j < C::kFdm; ++j) {
+        const int col = c0 + j;
+        if (col < C::D) out[1 + col] = v[j];                                  // sum r x
+        else if (C::kDiag && col < 2 * C::D) out[1 + col] = v[j];             // sum r x^2
+        else if (col == C::kAuxCol) out[0] = v[j];                            // n_k
+        else if (!C::kDiag && col == C::kAuxCol + 1) out[1 + C::D] = v[j] + v[j + 1];  // sum r |x|^2
+      }
+    }
+    tmem_fence_before();
+    // log-likelihood partial of this cluster (rank 0 holds it)
+    __shared__ double red[4];
+    double v = ll_acc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[q4] = v;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (tid == kWarpSoftmax0 * 32 && rank == 0) a.part_ll[cid] = red[0] + red[1] + red[2] + red[3];
+  }
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tmem_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  cluster_sync();  // no CTA exits while a peer may still write into its shared memory
+}
+
+// Pack the per-iteration component table into this kernel's shared-memory
+// images: split-bf16 weight blocks (128-byte swizzle) + epilogue constants.
+template <int COV, int DB>
+__global__ void tc_pack_kernel(int K, int64_t Kp_table, const float* wt, const CompConst* cc, char* params,
+                               float* consts) {
+  using C = Cfg<COV, DB>;
+  const int k = blockIdx.x;  // padded component index
+  const int chunk = k / kKC, kl = k % kKC;
+  char* img = params + (int64_t)chunk * C::kParamBlocks * kBlock;
+  const bool live = k < K;
+  for (int d = threadIdx.x; d < C::D; d += blockDim.x) {
+    const int db = d >> 6, c = d & 63;
+    // x coefficient: -2 mu (spherical) | -2 mu / var (diag, table rows D..2D)
+    float ra = live ? wt[(int64_t)(C::kDiag ? C::D + d : d) * Kp_table + k] : 0.f;
+    // x^2 coefficient (diag): 1 / var
+    float rv = (live && C::kDiag) ? wt[(int64_t)d * Kp_table + k] : 0.f;
+#pragma unroll
+    for (int j = 0; j < kNS; ++j) {  // w = w_0 + w_1 + w_2, each bf16
+      const __nv_bfloat16 ha = __float2bfloat16(ra);
+      *reinterpret_cast<__nv_bfloat16*>(img + C::a_blk(j, db) + sw128(kl, c)) = ha;
+      ra -= __bfloat162float(ha);
+      if (C::kDiag) {
+        const __nv_bfloat16 hv = __float2bfloat16(rv);
+        *reinterpret_cast<__nv_bfloat16*>(img + C::v_blk(j, db) + sw128(kl, c)) = hv;
+        rv -= __bfloat162float(hv);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    float* cs = consts + (int64_t)chunk * 3 * 128;
+    if (live) {
+      const CompConst q = cc[k];
+      cs[kl] = q.mpm;
+      cs[128 + kl] = 0.5f * kLog2e * q.s;
+      cs[256 + kl] = kLog2e * (q.lw - 0.5f * q.ln);
+    } else {  // padding component: logit -inf, no contribution anywhere
+      cs[kl] = 0.f;
+      cs[128 + kl] = 0.f;
+      cs[256 + kl] = -INFINITY;
+    }
+  }
+}
+
+// stats[k][f] += sum over clusters of part[cl][k][f] (fixed order), ll += sum part_ll
+__global__ void tc_reduce_kernel(const float* part, const double* part_ll, int ncl, int K, int64_t Kp, int F,
+                                 float* stats, double* ll) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < (int64_t)K * F) {
+    const int64_t k = i / F, f = i - k * F;
+    float s = 0.f;
+    for (int c = 0; c < ncl; ++c) s += part[((int64_t)c * Kp + k) * F + f];
+    stats[i] += s;
+  }
+  if (i == 0) {
+    double s = 0.0;
+    for (int c = 0; c < ncl; ++c) s += part_ll[c];
+    *ll += s;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+template <int COV, int DB>
+static int launch_t(const TcLaunch& L, cudaStream_t st) {
+  using C = Cfg<COV, DB>;
+  const int nclus = L.cluster_size;
+  static_assert(C::total(8) <= 232448 || C::kDiag, "shared memory budget");
+  // 1) pack the component table
+  tc_pack_kernel<COV, DB><<<(unsigned)(nclus * kKC), 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
+  if (int rc = check_launch("tc_pack_kernel")) return rc;
+  // 2) tensor map over X (N rows x D bf16), 128-row x 64-col boxes, 128-byte swizzle
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return set_error(GMMXX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap tmap;
+  cuuint64_t dims[2] = {(cuuint64_t)C::D, (cuuint64_t)L.N};
+  cuuint64_t strides[1] = {(cuuint64_t)C::D * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)kBM};
+  cuuint32_t es[2] = {1, 1};
+  CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(L.x), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return set_error(GMMXX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
+  // 3) persistent clustered launch
+  auto kern = em_tc_kernel<COV, DB>;
+  const int smem = C::total(nclus);
+  if (smem > 232448) return set_error(GMMXX_ERR_UNSUPPORTED, "tensor-core kernel shared memory over budget");
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_kernel attributes: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = nclus;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3((unsigned)nclus);
+  int max_clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&max_clusters, (void*)kern, &cfg);
+  if (e != cudaSuccess || max_clusters <= 0) {
+    cudaGetLastError();
+    return set_error(GMMXX_ERR_UNSUPPORTED, "no co-resident cluster of %d CTAs (%s)", nclus, cudaGetErrorString(e));
+  }
+  const int64_t ntiles = (L.N + kBM - 1) / kBM;
+  const int ncl = (int)std::min<int64_t>(std::min<int64_t>(max_clusters, kMaxClusters), ntiles);
+  cfg.gridDim = dim3((unsigned)(ncl * nclus));
+  TcArgs args{};
+  args.N = L.N;
+  args.Kp = L.Kp_part;
+  args.F = L.F;
+  args.cluster_size = nclus;
+  args.params = L.params;
+  args.consts = L.consts;
+  args.part = L.part;
+  args.part_ll = L.part_ll;
+  args.status = L.status;
+  e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
+  if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_kernel launch: %s", cudaGetErrorString(e));
+  // 4) deterministic reduction into the caller's statistics
+  const int64_t n = (int64_t)L.K * L.F;
+  tc_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(L.part, L.part_ll, ncl, L.K,
+                                                                                      L.Kp_part, L.F, L.stats, L.ll);
+  return check_launch("tc_reduce_kernel");
+}
+
+int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st) {
+  if (cov == GMMXX_DIAG && L.D == 64 && L.cluster_size <= kMaxClusterDiag) return launch_t<GMMXX_DIAG, 1>(L, st);
+  if (cov == GMMXX_SPHERICAL && L.D == 64) return launch_t<GMMXX_SPHERICAL, 1>(L, st);
+  if (cov == GMMXX_SPHERICAL && L.D == 128) return launch_t<GMMXX_SPHERICAL, 2>(L, st);
+  return set_error(GMMXX_ERR_UNSUPPORTED, "no tensor-core kernel for this shape");
+}
+
+}  // namespace tc
+}  // namespace gmmxx

@@ -65,6 +65,19 @@ __host__ __device__ inline int stat_width(int cov, int D) {
   }
 }
 
+// Tensor-core path window (em_tc.cu): bf16 X, B == 1, N >= 64K,
+// diag D == 64 with K <= 512, spherical D in {64, 128} with K <= 1024.
+constexpr int kTcMaxClusters = 160;
+constexpr int kMaxClusterDiag = 4;
+__host__ __device__ inline bool tc_eligible(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
+  if (B != 1 || N < 65536) return false;
+  if (cov == GMMXX_DIAG) return D == 64 && K <= 128 * kMaxClusterDiag;
+  if (cov == GMMXX_SPHERICAL) return (D == 64 || D == 128) && K <= 1024;
+  return false;
+}
+// three bf16 terms per weight: a_j (and v_j for diag)
+__host__ __device__ inline int tc_param_blocks(int cov, int D) { return (cov == GMMXX_DIAG ? 6 : 3) * (D / 64); }
+
 // Per-component constants of the logit epilogue.
 struct __align__(16) CompConst {
   float lw;   // log weight
@@ -80,6 +93,12 @@ struct Layout {
   int64_t wt;       // float[B][FE][Kp]  (feature-major component weights)
   int64_t prec;     // float[B][D][D] (tied) or float[B][K][D][D] (full)
   int64_t lse;      // float[B][max(N, K)] (per-row lse; per-matrix log det while preparing)
+  // tensor-core path (present when the shape is eligible)
+  int64_t tc_params;  // split-bf16 weight images [C][blocks][16 KB]
+  int64_t tc_consts;  // float[C][3][128]
+  int64_t tc_part;    // float[kTcMaxClusters][C*128][F]
+  int64_t tc_part_ll; // double[kTcMaxClusters]
+  int tc_cluster;     // C (0: tensor-core path not available)
   int64_t total;
   int64_t Kp;
   int FE;
@@ -98,6 +117,16 @@ inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   if (cov == GMMXX_TIED) off += al(B * D * D * 4);
   else if (cov == GMMXX_FULL) off += al(B * K * D * D * 4);
   L.lse = off; off += al(B * (N > K ? N : K) * 4);
+  L.tc_cluster = 0;
+  L.tc_params = L.tc_consts = L.tc_part = L.tc_part_ll = 0;
+  if (tc_eligible(cov, B, N, D, K)) {
+    const int C = (int)((K + 127) / 128);
+    L.tc_cluster = C;
+    L.tc_params = off; off += al((int64_t)C * tc_param_blocks(cov, (int)D) * 16384);
+    L.tc_consts = off; off += al((int64_t)C * 3 * 128 * 4);
+    L.tc_part = off; off += al((int64_t)kTcMaxClusters * C * 128 * stat_width(cov, (int)D) * 4);
+    L.tc_part_ll = off; off += al((int64_t)kTcMaxClusters * 8);
+  }
   L.total = off;
   return L;
 }

@@ -1,0 +1,115 @@
+"""Tensor-core (tcgen05) EM kernel parity: bf16 X, diag D=64 (K <= 512) /
+spherical D in {64, 128} (K <= 1024), 1-8 CTA clusters, against the numpy
+oracle and against the exact-fp32 CUDA-core kernels on the same inputs.
+bf16-input tolerances: parameters within 1e-4 (relative, atol 1e-4, or within
+the fp32 oracle's own error), mean log-likelihood within 1e-3 relative."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from test_gpu_parity import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+
+def _data(seed, n, d, k, cov, spread=3.0):
+    rng = np.random.default_rng(seed)
+    mu = rng.normal(0, spread, (k, d))
+    if cov == "diag":
+        var = np.exp(rng.uniform(np.log(0.1), np.log(4.0), (k, d)))
+    else:
+        var = np.repeat(rng.uniform(0.3, 1.5, (k, 1)) ** 2, d, 1)
+    w = rng.dirichlet(np.full(k, 0.5))
+    z = rng.choice(k, n, p=w)
+    x = (mu[z] + np.sqrt(var[z]) * rng.standard_normal((n, d))).astype(np.float32)
+    xb = torch.from_numpy(x).to(torch.bfloat16)[None]
+    init = (mu + 0.3 * rng.standard_normal(mu.shape)).astype(np.float32)[None]
+    icov = np.ones((1, k, d), np.float32) if cov == "diag" else np.ones((1, k), np.float32)
+    iw = np.full((1, k), 1.0 / k, np.float32)
+    return xb, init, icov, iw
+
+
+def _run(cov, xb, init, icov, iw, iters, dev, kernel):
+    from gmmxx_b200 import engine
+
+    os.environ["GMMXX_B200_KERNEL"] = kernel
+    try:
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        return engine.em_fit(cov, xb.to(dev), init.shape[1], max_iters=iters, tol=0.0, init_means=t(init),
+                             init_variances=t(icov), init_weights=t(iw))
+    finally:
+        os.environ.pop("GMMXX_B200_KERNEL", None)
+
+
+@pytest.mark.parametrize("cov,n,d,k", [
+    ("diag", 200_000, 64, 512),        # config-1 shape, cluster of 4
+    ("diag", 70_001, 64, 300),         # ragged N, padded components, cluster of 3
+    ("diag", 66_000, 64, 40),          # single-CTA cluster
+    ("diag", 80_000, 64, 512),         # many near-empty components (n_k < 1)
+    ("spherical", 100_000, 128, 256),
+    ("spherical", 70_000, 64, 64),
+    ("spherical", 80_000, 128, 1024),  # cluster of 8
+])
+def test_tc_matches_oracle(cuda_device, cov, n, d, k):
+    xb, init, icov, iw = _data(7 + k + n % 7, n, d, k, cov)
+    iters = 3
+    xf = xb.float().numpy()
+    r32 = oracle.fit(cov, xf, k, iters, 0.0, init, icov, iw)
+    r64 = oracle.fit(cov, xf, k, iters, 0.0, init, icov, iw, dtype=np.float64)
+    labels, means, c, w, info = _run(cov, xb, init, icov, iw, iters, cuda_device, "tc")
+    assert_parity(means.cpu().numpy(), r32[1], r64[1], name="means")
+    assert_parity(c.cpu().numpy(), r32[2], r64[2], name="covariances")
+    assert_parity(w.cpu().numpy(), r32[3], r64[3], name="weights")
+    lb, ref = info["lower_bound"], r32[4]["lower_bound"]
+    assert abs(lb - ref) <= 1e-3 * abs(ref), (lb, ref)
+    assert (labels.cpu().numpy() == r32[0]).mean() >= 0.999
+
+
+def test_tc_matches_simt_kernels(cuda_device):
+    xb, init, icov, iw = _data(3, 150_000, 64, 512, "diag")
+    a = _run("diag", xb, init, icov, iw, 2, cuda_device, "tc")
+    b = _run("diag", xb, init, icov, iw, 2, cuda_device, "simt")
+    for u, v, name in zip(a[1:4], b[1:4], ("means", "covariances", "weights")):
+        np.testing.assert_allclose(u.cpu().numpy(), v.cpu().numpy(), rtol=1e-4, atol=1e-4, err_msg=name)
+    assert abs(a[4]["lower_bound"] - b[4]["lower_bound"]) <= 1e-4 * abs(b[4]["lower_bound"])
+
+
+def test_tc_statistics_single_step(cuda_device):
+    """One accumulate call through the C ABI: tensor-core sufficient statistics
+    equal the CUDA-core ones (not just the fitted parameters)."""
+    from gmmxx_b200 import engine
+
+    xb, init, icov, iw = _data(5, 131_072, 64, 256, "diag")
+    x = xb.to(cuda_device)
+    means, cov, weights, _ = engine.initial_parameters("diag", x, 256, torch.from_numpy(init),
+                                                       torch.from_numpy(icov), torch.from_numpy(iw), 1e-6)
+    out = {}
+    for kernel in ("tc", "simt"):
+        os.environ["GMMXX_B200_KERNEL"] = kernel
+        try:
+            ops = engine.CudaOps("diag", x, 256)
+            stats = torch.zeros((1, 256, ops.stat_width), device=cuda_device)
+            ll = torch.zeros(1, dtype=torch.float64, device=cuda_device)
+            ops.prepare(means.clone(), cov.clone(), weights.clone(), 1e-6, 1e-8)
+            ops.accumulate(stats, ll)
+            ops.check_status()
+            out[kernel] = (stats.cpu().numpy(), float(ll.item()))
+        finally:
+            os.environ.pop("GMMXX_B200_KERNEL", None)
+    st, sr = out["tc"][0], out["simt"][0]
+    scale = np.abs(sr).max(axis=1, keepdims=True) + 1e-6
+    assert np.max(np.abs(st - sr) / scale) < 1e-4
+    assert abs(out["tc"][1] - out["simt"][1]) <= 1e-5 * abs(out["simt"][1])
+
+
+def test_tc_repeat_runs_bitwise_identical(cuda_device):
+    """The tensor-core path reduces per-cluster partials in a fixed order."""
+    xb, init, icov, iw = _data(9, 100_000, 64, 256, "diag")
+    a = _run("diag", xb, init, icov, iw, 2, cuda_device, "tc")
+    b = _run("diag", xb, init, icov, iw, 2, cuda_device, "tc")
+    for u, v in zip(a[1:4], b[1:4]):
+        assert torch.equal(u, v)
