@@ -73,7 +73,7 @@ _SIGNATURES = {
     "gmmxx_em_prepare": (_I32, [_I32, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _SZ, _P]),
     "gmmxx_em_accumulate": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P, _P, _P]),
     "gmmxx_em_finalize": (_I32, [_I32, _I64, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P]),
-    "gmmxx_xx_total": (_I32, [_I32, _P, _I64, _I64, _I64, _P, _P]),
+    "gmmxx_xx_total": (_I32, [_I32, _P, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "gmmxx_assign": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "gmmxx_logsumexp": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "gmmxx_resp": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _SZ, _P]),

@@ -34,7 +34,7 @@ int launch_finalize(int cov, int64_t B, int64_t D, int64_t K, int64_t n_total, c
                     const double* ll, const float* xx, float reg, float mw, float* means, float* covp,
                     float* weights, float* lb_out, cudaStream_t st);
 int launch_canary(const int32_t* in, int32_t* out, int64_t n, int32_t offset, cudaStream_t st);
-int launch_xx_total(const void* x, int dt, int64_t B, int64_t N, int D, float* xx, cudaStream_t st);
+int launch_xx_total(const void* x, int dt, int64_t B, int64_t N, int D, float* xx, float* part, cudaStream_t st);
 
 }  // namespace gmmxx
 
@@ -212,11 +212,14 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
   }
   RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
   a.lse_out = reinterpret_cast<float*>(ws + L.lse);
+  a.ll_part = reinterpret_cast<double*>(ws + L.llpart);
   a.ll = log_likelihood;
   if (int rc = launch_rows(cov_type, MODE_LSE, a, (int)B, st)) return rc;
   a.lse_in = a.lse_out;
   a.stats = stats;
-  return launch_mstep(cov_type, a, (int)B, st);
+  a.part = reinterpret_cast<float*>(ws + L.mpart);
+  if (int rc = launch_mstep(cov_type, a, (int)B, st)) return rc;
+  return launch_stats_reduce(a, (int)B, st);
 }
 
 int gmmxx_em_finalize(int cov_type, int64_t B, int64_t D, int64_t K, int64_t n_total, const float* stats,
@@ -235,11 +238,15 @@ int gmmxx_em_finalize(int cov_type, int64_t B, int64_t D, int64_t K, int64_t n_t
                          cov, weights, lower_bound_out, static_cast<cudaStream_t>(stream));
 }
 
-int gmmxx_xx_total(int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, float* xx_out, void* stream) {
+int gmmxx_xx_total(int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, float* xx_out, void* workspace,
+                   size_t workspace_bytes, void* stream) {
   if (int rc = check_shape(GMMXX_TIED, x_dtype, B, N, D, 1)) return rc;
   GMMXX_REQUIRE(xx_out, "xx_out");
   if (N > 0) GMMXX_REQUIRE(x, "x");
-  return launch_xx_total(x, x_dtype, B, N, (int)D, xx_out, static_cast<cudaStream_t>(stream));
+  const Layout L = make_layout(GMMXX_TIED, B, N, D, 1);
+  if (int rc = check_ws(workspace, workspace_bytes, L)) return rc;
+  return launch_xx_total(x, x_dtype, B, N, (int)D, xx_out, reinterpret_cast<float*>(static_cast<char*>(workspace) + L.xxpart),
+                         static_cast<cudaStream_t>(stream));
 }
 
 int gmmxx_assign(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,

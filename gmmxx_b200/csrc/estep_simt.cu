@@ -294,10 +294,10 @@ __global__ void __launch_bounds__(kThreads) rows_kernel(RowArgs a) {
         part += (double)l;
       }
     }
-    if (a.ll != nullptr) {
+    if (a.ll_part != nullptr) {
       __shared__ double red[kThreads / 32];
       const double tot = block_sum<double>(part, red);
-      if (threadIdx.x == 0) atomicAdd(a.ll, tot);
+      if (threadIdx.x == 0) a.ll_part[(int64_t)b * gridDim.x + blockIdx.x] = tot;
     }
   } else if (MODE == MODE_ARGMAX) {
 #pragma unroll
@@ -374,8 +374,8 @@ __global__ void __launch_bounds__(kThreads) mstep_kernel(RowArgs a) {
       }
     }
   }
-  // one flush per CTA
-  float* st = a.stats + (int64_t)b * a.K * a.FM;
+  // one flush per CTA into its own partial slot (reduced in a fixed order later)
+  float* st = a.part + ((int64_t)b * a.part_blocks + blockIdx.x) * a.Kp * a.FM;
 #pragma unroll
   for (int c = 0; c < NCH; ++c)
 #pragma unroll
@@ -385,9 +385,28 @@ __global__ void __launch_bounds__(kThreads) mstep_kernel(RowArgs a) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int f = c * 64 + fg * 4 + j;
-        if (f < a.FM) atomicAdd(st + (int64_t)k * a.FM + f, macc[c][i][j]);
+        if (f < a.FM) st[(int64_t)k * a.FM + f] = macc[c][i][j];
       }
     }
+}
+
+__global__ void stats_reduce_kernel(const float* part, int64_t nblk, int64_t stride, int64_t Kp, int K, int FM,
+                                    int B, float* stats, const double* ll_part, int64_t nll, double* ll) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t per_b = (int64_t)K * FM;
+  if (i < per_b * B) {
+    const int64_t b = i / per_b, r = i - b * per_b;
+    const int64_t k = r / FM, f = r - k * FM;
+    const float* p = part + (b * stride) * Kp * FM + k * FM + f;
+    float s = 0.f;
+    for (int64_t c = 0; c < nblk; ++c) s += p[c * Kp * FM];
+    stats[i] += s;
+  }
+  if (i == 0 && ll != nullptr) {
+    double s = 0.0;
+    for (int64_t c = 0; c < nll * B; ++c) s += ll_part[c];
+    *ll += s;
+  }
 }
 
 // xx (B, D, D) += sum_n x_n x_n^T  (tied covariance; torch_fallback.py:2856-2862)
@@ -426,7 +445,7 @@ __global__ void __launch_bounds__(kThreads) xx_total_kernel(const void* x, int d
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     const int e = threadIdx.x + i * kThreads;
-    if (e < D * D) atomicAdd(xx + (int64_t)b * D * D + e, acc[i]);
+    if (e < D * D) xx[((int64_t)b * gridDim.x + blockIdx.x) * D * D + e] = acc[i];  // this CTA's partial
   }
 }
 
@@ -488,11 +507,10 @@ static int launch_mstep_t(RowArgs a, int B, cudaStream_t st) {
   if (int rc = prep_smem(k, sm)) return rc;
   const int ktiles = (int)(a.Kp / kBK);
   const int64_t tiles = ceil_div(a.N, kBN);
-  const int64_t target = (int64_t)sm_count() * 4;
-  int64_t nblk = ceil_div(target, (int64_t)ktiles * B);
-  nblk = std::max<int64_t>(1, std::min<int64_t>(nblk, tiles));
-  a.rows_per_cta = ceil_div(tiles, nblk) * kBN;
-  nblk = ceil_div(a.N, a.rows_per_cta);
+  const int64_t nblk_max = mstep_blocks(B, a.N, a.Kp);  // partial slots reserved in the workspace
+  a.rows_per_cta = ceil_div(tiles, nblk_max) * kBN;
+  const int64_t nblk = ceil_div(a.N, a.rows_per_cta);
+  a.part_blocks = nblk_max;
   dim3 grid((unsigned)nblk, (unsigned)ktiles, (unsigned)B);
   k<<<grid, kThreads, sm, st>>>(a);
   return check_launch("mstep_kernel");
@@ -523,17 +541,35 @@ int launch_mstep(int cov, const RowArgs& a, int B, cudaStream_t st) {
   return set_error(GMMXX_ERR_INVALID, "bad covariance type %d", cov);
 }
 
-int launch_xx_total(const void* x, int dt, int64_t B, int64_t N, int D, float* xx, cudaStream_t st) {
+int launch_stats_reduce(const RowArgs& a, int B, cudaStream_t st) {
+  if (a.N == 0) return GMMXX_OK;
+  const int64_t tiles = ceil_div(a.N, kBN);
+  const int64_t nblk_max = mstep_blocks(B, a.N, a.Kp);
+  const int64_t nblk = ceil_div(a.N, ceil_div(tiles, nblk_max) * kBN);  // slots the M-step filled
+  const int64_t n = (int64_t)B * a.K * a.FM;
+  // partial slots are strided by nblk_max; only the first nblk are written
+  stats_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(
+      a.part, nblk, nblk_max, a.Kp, a.K, a.FM, B, a.stats, a.ll_part, tiles, a.ll);
+  return check_launch("stats_reduce_kernel");
+}
+
+int launch_xx_total(const void* x, int dt, int64_t B, int64_t N, int D, float* xx, float* part, cudaStream_t st) {
   if (N == 0) return GMMXX_OK;
   const int64_t sm = (int64_t)kBN * (D + 1) * 4;
   if (int rc = prep_smem(xx_total_kernel, sm)) return rc;
   const int64_t tiles = ceil_div(N, kBN);
-  int64_t nblk = std::max<int64_t>(1, std::min<int64_t>(ceil_div((int64_t)sm_count() * 2, B), tiles));
-  const int64_t rpc = ceil_div(tiles, nblk) * kBN;
-  nblk = ceil_div(N, rpc);
+  const int64_t nmax = xx_blocks(B, N);
+  const int64_t rpc = ceil_div(tiles, nmax) * kBN;
+  const int64_t nblk = ceil_div(N, rpc);
+  // partial slots of problem b start at (b * nblk) and are packed, so the
+  // reduction below uses stride nblk
   dim3 grid((unsigned)nblk, (unsigned)B);
-  xx_total_kernel<<<grid, kThreads, sm, st>>>(x, dt, N, D, rpc, xx);
-  return check_launch("xx_total_kernel");
+  xx_total_kernel<<<grid, kThreads, sm, st>>>(x, dt, N, D, rpc, part);
+  if (int rc = check_launch("xx_total_kernel")) return rc;
+  const int64_t n = B * (int64_t)D * D;
+  stats_reduce_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(part, nblk, nblk, D, D, D, (int)B, xx, nullptr, 0,
+                                                                  nullptr);
+  return check_launch("stats_reduce_kernel");
 }
 
 }  // namespace gmmxx

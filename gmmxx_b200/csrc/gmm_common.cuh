@@ -78,6 +78,25 @@ __host__ __device__ inline bool tc_eligible(int cov, int64_t B, int64_t N, int64
 // three bf16 terms per weight: a_j (and v_j for diag)
 __host__ __device__ inline int tc_param_blocks(int cov, int D) { return (cov == GMMXX_DIAG ? 6 : 3) * (D / 64); }
 
+// Row blocks of the CUDA-core M-step kernel (grid x): about 640 CTAs in total,
+// fixed so that the workspace size and the launch agree (deterministic partials).
+__host__ __device__ inline int64_t mstep_blocks(int64_t B, int64_t N, int64_t Kp) {
+  const int64_t ktiles = Kp / 64, tiles = (N + 63) / 64;
+  int64_t nblk = (640 + ktiles * B - 1) / (ktiles * B);
+  if (nblk > tiles) nblk = tiles;
+  if (nblk < 1) nblk = 1;
+  return nblk;
+}
+
+// Row blocks of the X^T X kernel (tied covariance), fixed like mstep_blocks.
+__host__ __device__ inline int64_t xx_blocks(int64_t B, int64_t N) {
+  const int64_t tiles = (N + 63) / 64;
+  int64_t nblk = (296 + B - 1) / B;
+  if (nblk > tiles) nblk = tiles;
+  if (nblk < 1) nblk = 1;
+  return nblk;
+}
+
 // Per-component constants of the logit epilogue.
 struct __align__(16) CompConst {
   float lw;   // log weight
@@ -93,6 +112,9 @@ struct Layout {
   int64_t wt;       // float[B][FE][Kp]  (feature-major component weights)
   int64_t prec;     // float[B][D][D] (tied) or float[B][K][D][D] (full)
   int64_t lse;      // float[B][max(N, K)] (per-row lse; per-matrix log det while preparing)
+  int64_t mpart;    // float[B][mstep_blocks][Kp][F]  CUDA-core M-step partials
+  int64_t llpart;   // double[B][ceil(N/64)]          per-CTA log-likelihood partials
+  int64_t xxpart;   // float[B][xx_blocks][D][D]      X^T X partials (tied)
   // tensor-core path (present when the shape is eligible)
   int64_t tc_params;  // split-bf16 weight images [C][blocks][16 KB]
   int64_t tc_consts;  // float[C][3][128]
@@ -117,6 +139,10 @@ inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   if (cov == GMMXX_TIED) off += al(B * D * D * 4);
   else if (cov == GMMXX_FULL) off += al(B * K * D * D * 4);
   L.lse = off; off += al(B * (N > K ? N : K) * 4);
+  L.mpart = off; off += al(B * mstep_blocks(B, N, L.Kp) * L.Kp * stat_width(cov, (int)D) * 4);
+  L.llpart = off; off += al(B * ((N + 63) / 64) * 8);
+  L.xxpart = off;
+  if (cov == GMMXX_TIED) off += al(B * xx_blocks(B, N) * D * D * 4);
   L.tc_cluster = 0;
   L.tc_params = L.tc_consts = L.tc_part = L.tc_part_ll = 0;
   if (tc_eligible(cov, B, N, D, K)) {

@@ -18,16 +18,21 @@ struct RowArgs {
   const float* lse_in;  // [B][N]
   float* lse_out;       // [B][N]
   double* ll;           // log-likelihood accumulator (may be null)
+  double* ll_part;      // per-CTA log-likelihood partials [B][gridDim.x] (LSE mode, may be null)
+  float* part;          // M-step partials [B][part_blocks][Kp][FM]
   int64_t* labels;      // [B][N]
   float* out;           // [B][N][K]
   float* stats;         // [B][K][FM]
   int FM;
   int64_t rows_per_cta;
+  int64_t part_blocks;
 };
 
 enum { MODE_LSE = 0, MODE_ARGMAX = 1, MODE_RESP = 2 };
 
 int launch_rows(int cov, int mode, const RowArgs& a, int B, cudaStream_t st);
 int launch_mstep(int cov, const RowArgs& a, int B, cudaStream_t st);
+// stats += sum of the M-step partials, ll += sum of the LSE partials (fixed order)
+int launch_stats_reduce(const RowArgs& a, int B, cudaStream_t st);
 
 }  // namespace gmmxx

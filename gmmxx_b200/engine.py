@@ -208,7 +208,8 @@ class CudaOps:
         self.ws = _WS.get(x.device, nat.workspace_bytes(self.covc, self.b, self.n, self.d, k))
 
     def xx_total(self, xx: torch.Tensor) -> None:
-        nat.call("gmmxx_xx_total", self.xdt, self.x.data_ptr(), self.b, self.n, self.d, xx.data_ptr(), self.stream)
+        nat.call("gmmxx_xx_total", self.xdt, self.x.data_ptr(), self.b, self.n, self.d, xx.data_ptr(),
+                 self.ws.data_ptr(), self.ws.numel(), self.stream)
 
     def prepare(self, means, cov, weights, reg_covar, min_weight) -> None:
         nat.call("gmmxx_em_prepare", self.covc, self.b, self.d, self.k, means.data_ptr(), cov.data_ptr(),

@@ -114,7 +114,8 @@ def em_fit_streamed(
         if covc == nat.TIED:
             xx = torch.zeros((1, d, d), dtype=torch.float32, device=device)
             for xc, _ in st.chunks():
-                nat.call("gmmxx_xx_total", xdt, xc.data_ptr(), 1, xc.shape[1], d, xx.data_ptr(), stream)
+                nat.call("gmmxx_xx_total", xdt, xc.data_ptr(), 1, xc.shape[1], d, xx.data_ptr(), ws.data_ptr(),
+                         ws.numel(), stream)
         prev = None
         it = 0
         t0 = time.perf_counter()

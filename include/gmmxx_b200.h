@@ -139,9 +139,11 @@ GMMXX_API int gmmxx_em_finalize(int cov_type, int64_t B, int64_t D, int64_t K, i
                       float* lower_bound_out, void* stream);
 
 /* xx_out (B, D, D) += sum_n x_n x_n^T (tied covariance, once per fit;
- * torch_fallback.py:2856-2862). */
+ * torch_fallback.py:2856-2862).  Per-CTA partials go through `workspace`
+ * (sized by gmmxx_workspace_bytes(GMMXX_TIED, B, N, D, 1) or larger) and are
+ * reduced in a fixed order. */
 GMMXX_API int gmmxx_xx_total(int x_dtype, const void* x, int64_t B, int64_t N, int64_t D,
-                   float* xx_out, void* stream);
+                             float* xx_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- inference on fixed parameters ---------------------------------------
  * Parameters are used as given (no clamp/renormalisation), like the
