@@ -78,6 +78,7 @@ _SIGNATURES = {
     "gmmxx_logsumexp": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "gmmxx_resp": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "gmmxx_predict_proba": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
+    "gmmxx_logsumexp_noalloc": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P]),
 }
 
 

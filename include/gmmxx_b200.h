@@ -178,6 +178,20 @@ GMMXX_API int gmmxx_predict_proba(int cov_type, int x_dtype, const void* x,
                         const float* means, const float* cov, const float* weights,
                         float* proba_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Per-sample log-likelihood like gmmxx_logsumexp, for callers that cannot
+ * allocate device memory (no workspace argument; nothing is allocated).  No
+ * counterpart in the reference.  The component table lives in a built-in
+ * device array of 8 MiB that every GPU loading this library keeps until the
+ * process exits; shapes whose table does not fit return GMMXX_ERR_WORKSPACE.
+ * The first call on a device looks up that array's device address (make it
+ * before any stream capture).  All calls on a device share the array, so
+ * calls that overlap on the GPU race; the covariance status word (jitter
+ * ladder) is cleared per call and not reported. */
+GMMXX_API int gmmxx_logsumexp_noalloc(int cov_type, int x_dtype, const void* x,
+                                      int64_t B, int64_t N, int64_t D, int64_t K,
+                                      const float* means, const float* cov, const float* weights,
+                                      float* lse_out, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
