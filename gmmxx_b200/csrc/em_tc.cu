@@ -41,7 +41,8 @@ using namespace ptx;
 constexpr int kBM = 128;          // rows per tile (UMMA M of the E-step)
 constexpr int kKC = 128;          // components per CTA
 constexpr int kNS = 3;            // bf16 terms of the split component weights (24 significant bits)
-constexpr int kThreads = 256;     // 8 warps
+constexpr int kThreads = 384;     // 12 warps: TMA, MMA, 2 prep, 8 softmax
+constexpr int kHalf = kKC / 2;    // components per softmax thread (two warps share a row)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kDmCol = 256;  // M-step accumulator columns [256, 256 + FDM)
 constexpr int kBlock = 16384;     // one [128][64] bf16 swizzled block
@@ -68,7 +69,8 @@ struct Cfg {
   static constexpr int kR = kAuxConst + (kDiag ? kAuxBytes : 0);
   static constexpr int kConsts = kR + 2 * kBlock;  // mpm[128], h[128], c2[128]
   static constexpr int kQ = kConsts + 3 * 128 * 4; // q[2][128] (spherical)
-  static constexpr int kXch = kQ + (kDiag ? 0 : 2 * 128 * 4);
+  static constexpr int kHalfX = kQ + (kDiag ? 0 : 2 * 128 * 4);  // [2 tiles][2 halves][128 rows] float2
+  static constexpr int kXch = kHalfX + 2 * 2 * 128 * 8;
   __host__ __device__ static constexpr int xch_bytes(int C) { return 2 * C * 128 * 8; }
   __host__ __device__ static constexpr int bars(int C) { return kXch + xch_bytes(C); }
   __host__ __device__ static constexpr int total(int C) { return bars(C) + 256 + 1024; }
@@ -99,6 +101,7 @@ struct Bars {
   uint64_t rfull;      // softmax: R part written
   uint64_t rfree;      // MMA: R part consumed
   uint64_t xch[2];     // cluster exchange of (row max, row sum)
+  uint64_t hx[2];      // softmax: both component halves of the row wrote (max, sum)
   uint64_t mdone;      // MMA: all MMAs issued and complete
   uint32_t tmem_base;
   int abort;
@@ -138,12 +141,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->fmain[i], 2);
       mbar_init(&bars->fempty[i], 1);
       mbar_init(&bars->sfull[i], 1);
-      mbar_init(&bars->sfree[i], 4);
+      mbar_init(&bars->sfree[i], 8);
       mbar_init(&bars->xch[i], 1);
+      mbar_init(&bars->hx[i], 8);
     }
     mbar_init(&bars->fl, 2);
     mbar_init(&bars->slfree, 1);
-    mbar_init(&bars->rfull, 4);
+    mbar_init(&bars->rfull, 8);
     mbar_init(&bars->rfree, 1);
     mbar_init(&bars->mdone, 1);
     bars->abort = 0;
@@ -343,51 +347,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax warpgroup: one thread per row ----------------
-    const int q4 = warp & 3;               // TMEM lane quarter of this warp
-    const int row = q4 * 32 + lane;        // row within the tile
+    // ---------------- softmax: 8 warps, two per TMEM lane quarter ----------------
+    // warp w handles rows 32*(w%4) .. +31 (its TMEM lane quarter) and the
+    // component half hf = (w-4)/4, i.e. 64 logits per thread.
+    const int q4 = warp & 3;
+    const int hf = (warp - kWarpSoftmax0) >> 2;
+    const int row = q4 * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    const int k0 = hf * kHalf;  // first component of this half
     double ll_acc = 0.0;
-    float p[kKC];
+    float p[kHalf];
+    float2* halfx = reinterpret_cast<float2*>(sm + C::kHalfX);  // [tile&1][half][row]
     const uint32_t xch_mine = smem_u32(&xch[(int)rank * 128 + row]);  // slot 0 entry of (this rank, row)
     const uint32_t slot_stride = (uint32_t)(nclus * 128 * 8);
+    const float4* cm4 = reinterpret_cast<const float4*>(c_mpm + k0);
+    const float4* ch4 = reinterpret_cast<const float4*>(c_h + k0);
+    const float4* cc4 = reinterpret_cast<const float4*>(c_c2 + k0);
     for (int t = 0; t < T; ++t) {
       const int s = t & 1;
       const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
       const bool valid = grow < a.N;
       if (!mbar_wait_warp(&bars->sfull[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
       tmem_fence_after();
-      const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC);
-#pragma unroll
-      for (int c = 0; c < kKC; c += 32) tmem_ld32(sc + c, p + c);
+      const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC + k0);
+      tmem_ld32(sc, p);
+      tmem_ld32(sc + 32, p + 32);
       tmem_wait_ld();
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->sfree[s]);
-      // logits (log2 units) and the CTA-local row max
       float qn = 0.f;
       if (!C::kDiag) {  // |x|^2 of this row (signalled by the prep warps before S was issued)
         if (!mbar_wait_warp(&bars->fmain[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
         qn = qbuf[s * 128 + row];
       }
-      float m = -INFINITY;
+      // logits (log2 units) and this half's row max; four independent chains
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int k = 0; k < kKC; ++k) {
-        const float dist = fmaxf(p[k] + c_mpm[k] + qn, 0.f);
-        const float l = fmaf(-c_h[k], dist, c_c2[k]);
-        p[k] = l;
-        m = fmaxf(m, l);
+      for (int k4 = 0; k4 < kHalf / 4; ++k4) {
+        const float4 vm = cm4[k4], vh = ch4[k4], vc = cc4[k4];
+        const float mm[4] = {vm.x, vm.y, vm.z, vm.w}, hh[4] = {vh.x, vh.y, vh.z, vh.w},
+                    cc[4] = {vc.x, vc.y, vc.z, vc.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k = 4 * k4 + j;
+          const float dist = fmaxf(p[k] + (mm[j] + qn), 0.f);
+          const float l = fmaf(-hh[j], dist, cc[j]);
+          p[k] = l;
+          mx[j] = fmaxf(mx[j], l);
+        }
       }
-      float sum = 0.f;
+      const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      float sm4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < kKC; ++k) {
+      for (int k = 0; k < kHalf; ++k) {
         p[k] = exp2f(p[k] - m);
-        sum += p[k];
+        sm4[k & 3] += p[k];
       }
-      // exchange (max, sum) of this row with every CTA of the cluster
-      if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
-      for (int q = 0; q < nclus; ++q)
-        st_async_f2(map_shared(xch_mine + s * slot_stride, q), m, sum, map_shared(smem_u32(&bars->xch[s]), q));
+      const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
+      // combine the two halves of the row (double-buffered by tile parity)
+      halfx[(s * 2 + hf) * 128 + row] = make_float2(m, sum);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->hx[s]);
+      if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
+      const float2 o = halfx[(s * 2 + (hf ^ 1)) * 128 + row];
+      const float mc = fmaxf(m, o.x);
+      const float sc2 = sum * exp2f(m - mc) + o.y * exp2f(o.x - mc);
+      // exchange (max, sum) of this CTA's components with the cluster (half 0 sends)
+      if (hf == 0) {
+        if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
+        for (int q = 0; q < nclus; ++q)
+          st_async_f2(map_shared(xch_mine + s * slot_stride, q), mc, sc2, map_shared(smem_u32(&bars->xch[s]), q));
+      }
       if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
       float M = -INFINITY;
       for (int q = 0; q < nclus; ++q) M = fmaxf(M, xch[(s * nclus + q) * 128 + row].x);
@@ -397,27 +428,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         S += e.y * exp2f(e.x - M);
       }
       const float f = valid ? exp2f(m - M) / S : 0.f;
-      if (valid && rank == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
-      // responsibilities -> R (two passes: bf16 high part, then the residual)
+      if (valid && rank == 0 && hf == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
+      // responsibilities -> R (two passes: bf16 high part, then the residual);
+      // this half's 64 components are exactly R's MN group hf
+      char* rg = sm + C::kR + hf * kBlock;
       for (int part = 0; part < 2; ++part) {
         const int use = 2 * t + part;
         if (use >= 1 && !mbar_wait_warp(&bars->rfree, (use - 1) & 1, abort)) { set_abort(bars, a.status); break; }
-        char* rb = sm + C::kR;
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
+        for (int c = 0; c < 8; ++c) {
+          uint32_t w[4];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint32_t w[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int k0 = g * 64 + c * 8 + 2 * i;
-              const float r0 = p[k0] * f, r1 = p[k0 + 1] * f;
-              const uint32_t h = pack_bf16(r0, r1);
-              w[i] = part == 0 ? h : pack_bf16(r0 - bf16lo_to_f32(h), r1 - bf16hi_to_f32(h));
-            }
-            *reinterpret_cast<uint4*>(rb + g * kBlock + sw128((uint32_t)row, (uint32_t)(c * 8))) =
-                make_uint4(w[0], w[1], w[2], w[3]);
+          for (int i = 0; i < 4; ++i) {
+            const int kk = c * 8 + 2 * i;
+            const float r0 = p[kk] * f, r1 = p[kk + 1] * f;
+            const uint32_t h = pack_bf16(r0, r1);
+            w[i] = part == 0 ? h : pack_bf16(r0 - bf16lo_to_f32(h), r1 - bf16hi_to_f32(h));
           }
+          *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)(c * 8))) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         fence_proxy_async();
         __syncwarp();
@@ -425,34 +453,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (*abort) break;
     }
-    // ---------------- epilogue: statistics partials ----------------
+    // ---------------- epilogue: statistics partials (half-0 warps) ----------------
     // drain: the MMA thread always commits `mdone` (also after an abort), so
     // wait for it without the abort shortcut before touching TMEM again
-    if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 4000000000ull)) set_abort(bars, a.status);
-    tmem_fence_after();
-    const int comp = (int)rank * kKC + row;  // this thread's TMEM lane = component
-    float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
-    for (int c0 = 0; c0 < C::kFdm; c0 += 16) {
-      float v[32];
-      tmem_ld32(tmem + lane_addr + kDmCol + c0, v);  // 32 columns; 16 used per step
-      tmem_wait_ld();
-      for (int j = 0; j < 16 && c0 + j < C::kFdm; ++j) {
-        const int col = c0 + j;
-        if (col < C::D) out[1 + col] = v[j];                                  // sum r x
-        else if (C::kDiag && col < 2 * C::D) out[1 + col] = v[j];             // sum r x^2
-        else if (col == C::kAuxCol) out[0] = v[j];                            // n_k
-        else if (!C::kDiag && col == C::kAuxCol + 1) out[1 + C::D] = v[j] + v[j + 1];  // sum r |x|^2
+    if (hf == 0) {
+      if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 4000000000ull)) set_abort(bars, a.status);
+      tmem_fence_after();
+      const int comp = (int)rank * kKC + row;  // this thread's TMEM lane = component
+      float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
+      for (int c0 = 0; c0 < C::kFdm; c0 += 16) {
+        float v[32];
+        tmem_ld32(tmem + lane_addr + kDmCol + c0, v);  // 32 columns; 16 used per step
+        tmem_wait_ld();
+        for (int j = 0; j < 16 && c0 + j < C::kFdm; ++j) {
+          const int col = c0 + j;
+          if (col < C::D) out[1 + col] = v[j];                                  // sum r x
+          else if (C::kDiag && col < 2 * C::D) out[1 + col] = v[j];             // sum r x^2
+          else if (col == C::kAuxCol) out[0] = v[j];                            // n_k
+          else if (!C::kDiag && col == C::kAuxCol + 1) out[1 + C::D] = v[j] + v[j + 1];  // sum r |x|^2
+        }
       }
-    }
-    tmem_fence_before();
-    // log-likelihood partial of this cluster (rank 0 holds it)
-    __shared__ double red[4];
-    double v = ll_acc;
+      tmem_fence_before();
+      // log-likelihood partial of this cluster (rank 0 holds it)
+      __shared__ double red[4];
+      double v = ll_acc;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[q4] = v;
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (tid == kWarpSoftmax0 * 32 && rank == 0) a.part_ll[cid] = red[0] + red[1] + red[2] + red[3];
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[q4] = v;
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (tid == kWarpSoftmax0 * 32 && rank == 0) a.part_ll[cid] = red[0] + red[1] + red[2] + red[3];
+    }
   }
   __syncthreads();
   if (warp == kWarpMma) {
@@ -548,7 +578,7 @@ template <int COV, int DB>
 static int launch_t(const TcLaunch& L, cudaStream_t st) {
   using C = Cfg<COV, DB>;
   const int nclus = L.cluster_size;
-  static_assert(C::total(8) <= 232448 || C::kDiag, "shared memory budget");
+  static_assert(C::total(C::kDiag ? kMaxClusterDiag : 8) <= 232448, "shared memory budget");
   // 1) pack the component table
   tc_pack_kernel<COV, DB><<<(unsigned)(nclus * kKC), 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
   if (int rc = check_launch("tc_pack_kernel")) return rc;
