@@ -69,8 +69,8 @@ struct Cfg {
   static constexpr int kR = kAuxConst + (kDiag ? kAuxBytes : 0);
   static constexpr int kConsts = kR + 2 * kBlock;  // mpm[128], h[128], c2[128]
   static constexpr int kQ = kConsts + 3 * 128 * 4; // q[2][128] (spherical)
-  static constexpr int kHalfX = kQ + (kDiag ? 0 : 2 * 128 * 4);  // [2 tiles][2 halves][128 rows] float2
-  static constexpr int kXch = kHalfX + 2 * 2 * 128 * 8;
+  static constexpr int kHalfX = kQ + (kDiag ? 0 : 2 * 128 * 4);  // [2 halves][128 rows] float2
+  static constexpr int kXch = kHalfX + 2 * 128 * 8;
   __host__ __device__ static constexpr int xch_bytes(int C) { return 2 * C * 128 * 8; }
   __host__ __device__ static constexpr int bars(int C) { return kXch + xch_bytes(C); }
   __host__ __device__ static constexpr int total(int C) { return bars(C) + 256 + 1024; }
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int k0 = hf * kHalf;  // first component of this half
     double ll_acc = 0.0;
     float p[kHalf];
-    float2* halfx = reinterpret_cast<float2*>(sm + C::kHalfX);  // [tile&1][half][row]
+    float2* halfx = reinterpret_cast<float2*>(sm + C::kHalfX);  // [half][row]
     const uint32_t xch_mine = smem_u32(&xch[(int)rank * 128 + row]);  // slot 0 entry of (this rank, row)
     const uint32_t slot_stride = (uint32_t)(nclus * 128 * 8);
     const float4* cm4 = reinterpret_cast<const float4*>(c_mpm + k0);
@@ -405,12 +405,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm4[k & 3] += p[k];
       }
       const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
-      // combine the two halves of the row (double-buffered by tile parity)
-      halfx[(s * 2 + hf) * 128 + row] = make_float2(m, sum);
+      // combine the two halves of the row.  One buffer suffices: a half
+      // rewrites its entry for tile t+1 only after writing R_lo(t), which
+      // waits for M_hi(t), which waited for the other half's R_hi(t) -- and
+      // that half read this entry before writing R_hi(t).
+      halfx[hf * 128 + row] = make_float2(m, sum);
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->hx[s]);
       if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
-      const float2 o = halfx[(s * 2 + (hf ^ 1)) * 128 + row];
+      const float2 o = halfx[(hf ^ 1) * 128 + row];
       const float mc = fmaxf(m, o.x);
       const float sc2 = sum * exp2f(m - mc) + o.y * exp2f(o.x - mc);
       // exchange (max, sum) of this CTA's components with the cluster (half 0 sends)
@@ -578,7 +581,8 @@ template <int COV, int DB>
 static int launch_t(const TcLaunch& L, cudaStream_t st) {
   using C = Cfg<COV, DB>;
   const int nclus = L.cluster_size;
-  static_assert(C::total(C::kDiag ? kMaxClusterDiag : 8) <= 232448, "shared memory budget");
+  // dynamic + static shared memory (the kernel's 1 KB static block) <= 227 KB
+  static_assert(C::total(C::kDiag ? kMaxClusterDiag : 8) + 1024 <= 232448, "shared memory budget");
   // 1) pack the component table
   tc_pack_kernel<COV, DB><<<(unsigned)(nclus * kKC), 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
   if (int rc = check_launch("tc_pack_kernel")) return rc;
