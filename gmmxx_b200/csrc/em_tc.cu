@@ -398,10 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      // a half made only of padding components has m = -inf: its p must be 0
+      const float mref = (m == -INFINITY) ? 0.f : m;
       float sm4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int k = 0; k < kHalf; ++k) {
-        p[k] = exp2f(p[k] - m);
+        p[k] = exp2f(p[k] - mref);
         sm4[k & 3] += p[k];
       }
       const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
