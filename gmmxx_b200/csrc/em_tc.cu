@@ -50,6 +50,13 @@ constexpr int kAuxBytes = 4096;   // [16][128] K-major aux operand (1, |x|^2 hi 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
+// 2^x on the SFU (ex2.approx.ftz: ~2^-22 relative error, subnormal results flushed)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 enum Warp { kWarpTma = 0, kWarpMma = 1, kWarpPrep0 = 2, kWarpSoftmax0 = 4 };
 
 // Shared-memory carve-up (byte offsets from a 1024-aligned base).
@@ -199,9 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_fence_after();
       // one K=64 feature block times one K=64 weight block (4 MMAs of K=16)
       auto block_mma = [&](uint32_t d, uint32_t fa, uint32_t wb, uint32_t& acc) {
+        const uint64_t da = desc_kmajor(fa), dw = desc_kmajor(wb);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mma_bf16(d, desc_kmajor(fa + kk * 32), desc_kmajor(wb + kk * 32), id_e, acc);
+        for (int kk = 0; kk < 4; ++kk) {  // +32 B along K per instruction
+          mma_bf16(d, da + 2 * kk, dw + 2 * kk, id_e, acc);
           acc = 1;
         }
       };
@@ -244,23 +252,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int use = 2 * t + part;
         if (!mbar_wait(&bars->rfull, use & 1, abort)) return false;
         tmem_fence_after();
-        const uint32_t aux = base + C::aux(s);
         const bool first = (t == 0 && part == 0);
+        // descriptors at row 0; each 16-row step adds 2048 B (MN-major) or
+        // 32 B / 2048 B per 4 steps (K-major aux)
+        const uint64_t r0 = desc_mnmajor(r_base, kBlock);
+        const uint64_t x0 = desc_mnmajor(base + C::x_blk(s, 0), kBlock);
+        const uint64_t sh0 = C::kDiag ? desc_mnmajor(base + C::sh_blk(s, 0), kBlock) : 0;
+        const uint64_t sl0 = C::kDiag ? desc_mnmajor(base + C::sl_blk(0), kBlock) : 0;
+        const uint64_t aux0 = desc_kmajor(base + C::aux(s));
+#pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // 16 rows per instruction
-          const uint64_t ra = desc_mnmajor(r_base + ks * 2048, kBlock);
+          const uint64_t step = (uint64_t)(ks * 128);  // 2048 B >> 4
+          const uint64_t ra = r0 + step;
           const uint32_t acc = (first && ks == 0) ? 0u : 1u;
+#pragma unroll
           for (int db = 0; db < DB; ++db)
-            mma_bf16(tmem + kDmCol + db * 64, ra, desc_mnmajor(base + C::x_blk(s, db) + ks * 2048, kBlock), id_m,
-                     acc);
+            mma_bf16(tmem + kDmCol + db * 64, ra, x0 + step + (uint64_t)(db * (kBlock >> 4)), id_m, acc);
           if (C::kDiag) {
-            for (int db = 0; db < DB; ++db) {
-              const uint32_t dcol = tmem + kDmCol + C::D + db * 64;
-              mma_bf16(dcol, ra, desc_mnmajor(base + C::sh_blk(s, db) + ks * 2048, kBlock), id_m, acc);
-              if (part == 0)
-                mma_bf16(dcol, ra, desc_mnmajor(base + C::sl_blk(db) + ks * 2048, kBlock), id_m, 1u);
-            }
+            const uint32_t dcol = tmem + kDmCol + C::D;
+            mma_bf16(dcol, ra, sh0 + step, id_m, acc);
+            if (part == 0) mma_bf16(dcol, ra, sl0 + step, id_m, 1u);
           }
-          mma_bf16(tmem + kDmCol + C::kAuxCol, ra, desc_kmajor(aux + (ks >> 2) * 2048 + (ks & 3) * 32), id_aux, acc);
+          mma_bf16(tmem + kDmCol + C::kAuxCol, ra, aux0 + (uint64_t)((ks >> 2) * 128 + (ks & 3) * 2), id_aux, acc);
         }
         mma_commit(&bars->rfree);
         if (C::kDiag && part == 0) mma_commit(&bars->slfree);
@@ -285,34 +298,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = t & 1;
       if (!mbar_wait_warp(&bars->xfull[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
       if (C::kDiag) {
-        // x^2 = s_hi + s_lo exactly (bf16 x has 8 significant bits).  The
-        // buffers share one swizzled layout, so the map is elementwise.
-        for (int half = 0; half < 2; ++half) {
-          if (half == 1) {
-            // SL is single-buffered: wait until the previous tile's M-step high part read it
-            if (t >= 1 && !mbar_wait_warp(&bars->slfree, (t - 1) & 1, abort)) { set_abort(bars, a.status); break; }
-          }
-          for (int db = 0; db < DB; ++db) {
-            const uint4* xs = reinterpret_cast<const uint4*>(sm + C::x_blk(s, db));
-            uint4* dst = reinterpret_cast<uint4*>(sm + (half == 0 ? C::sh_blk(s, db) : C::sl_blk(db)));
-            for (int c = ptid; c < kBlock / 16; c += 64) {
-              const uint4 v = xs[c];
-              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-              uint32_t o[4];
+        // x^2 = s_hi + s_lo exactly (bf16 x has 8 significant bits).  One pass
+        // writes SH (double-buffered) and keeps the s_lo words in registers
+        // until the single SL buffer is free.  The buffers share one swizzled
+        // layout, so the map is elementwise.
+        static_assert(!C::kDiag || DB == 1, "diag tensor-core path is D = 64");
+        constexpr int kPer = kBlock / 16 / 64;  // 16-byte chunks per prep thread
+        uint4 lo4[kPer];
+        const uint4* xs = reinterpret_cast<const uint4*>(sm + C::x_blk(s, 0));
+        uint4* sh = reinterpret_cast<uint4*>(sm + C::sh_blk(s, 0));
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
-                const float s0 = x0 * x0, s1 = x1 * x1;  // exact in fp32
-                const uint32_t hi = pack_bf16(s0, s1);
-                o[i] = half == 0 ? hi : pack_bf16(s0 - bf16lo_to_f32(hi), s1 - bf16hi_to_f32(hi));
-              }
-              dst[c] = make_uint4(o[0], o[1], o[2], o[3]);
-            }
+        for (int i4 = 0; i4 < kPer; ++i4) {
+          const int c = ptid + 64 * i4;
+          const uint4 v = xs[c];
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+          uint32_t hi[4], lo[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
+            const float s0 = x0 * x0, s1 = x1 * x1;  // exact in fp32
+            hi[i] = pack_bf16(s0, s1);
+            lo[i] = pack_bf16(s0 - bf16lo_to_f32(hi[i]), s1 - bf16hi_to_f32(hi[i]));
           }
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(half == 0 ? &bars->fmain[s] : &bars->fl);
+          sh[c] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          lo4[i4] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->fmain[s]);
+        // SL is single-buffered: wait until the previous tile's M-step high part read it
+        if (t >= 1 && !mbar_wait_warp(&bars->slfree, (t - 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        uint4* sl = reinterpret_cast<uint4*>(sm + C::sl_blk(0));
+#pragma unroll
+        for (int i4 = 0; i4 < kPer; ++i4) sl[ptid + 64 * i4] = lo4[i4];
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->fl);
         if (*abort) break;
       } else {
         // |x|^2 per row (two threads per row), q_hi / q_lo into the aux operand
@@ -403,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float sm4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int k = 0; k < kHalf; ++k) {
-        p[k] = exp2f(p[k] - mref);
+        p[k] = ex2_approx(p[k] - mref);
         sm4[k & 3] += p[k];
       }
       const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
