@@ -325,6 +325,8 @@ def main():
 
     if rank == 0:
         peaks = load_peaks()
+        tc_path = nat.accumulate_path(engine.cov_code(cfg.cov_type), engine._X_DTYPES[cfg.dtype], cfg.B, n_local, D,
+                                      K) == 1
         flops = algorithmic_flops(cfg.cov_type, n_local * cfg.B, D, K)
         achieved = flops / (acc_ms / 1e3) / 1e12
         long_run = ms * args.steps > 1000.0
@@ -335,7 +337,7 @@ def main():
             with open(tpath) as f:
                 tr = json.load(f).get(f"config{cfg.index}")
             if tr:
-                traffic = tr["bytes_per_row"] * n_local * cfg.B
+                traffic = tr["read_bytes_per_row"] * n_local * cfg.B + tr["write_bytes_per_launch"]
         line = {
             "metric": "EM samples/s per iteration", "value": value, "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -343,13 +345,16 @@ def main():
             "config": workload_config(cfg, args),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "gmmxx_em_accumulate (rows_kernel + mstep_kernel)",
+                         "kernel": ("em_tc_kernel (+ tc_pack_kernel, tc_reduce_kernel)" if tc_path
+                                    else "rows_kernel + mstep_kernel + stats_reduce_kernel"),
                          "peak_source": f"{peaks['source']} bf16 {'sustained' if long_run else 'burst'}",
                          "algorithmic_flops_per_launch": flops, "launch_ms": acc_ms,
                          "hbm_frac": (n_local * cfg.B * D * torch.empty((), dtype=cfg.dtype).element_size()) /
                                      (acc_ms / 1e3) / 1e9 / peaks["hbm_gbs"]},
             "clocks": clocks,
-            "gpu_launches": args.steps * (5 + (2 if cfg.cov_type in ("tied", "full") else 0)),
+            # per iteration: prep_weights + prep_table (+ 2 Cholesky kernels for tied / full),
+            # three statistics kernels, finalize
+            "gpu_launches": args.steps * (6 + (2 if cfg.cov_type in ("tied", "full") else 0)),
             "e2e": e2e,
         }
         if world == 1 and not args.no_cpu:

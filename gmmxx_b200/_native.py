@@ -70,6 +70,7 @@ _SIGNATURES = {
     "gmmxx_stat_width": (_I64, [_I32, _I64]),
     "gmmxx_workspace_bytes": (_SZ, [_I32, _I64, _I64, _I64, _I64]),
     "gmmxx_workspace_status": (_I32, [_P, _P, _P]),
+    "gmmxx_accumulate_path": (_I32, [_I32, _I32, _I64, _I64, _I64, _I64, _P]),
     "gmmxx_em_prepare": (_I32, [_I32, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _SZ, _P]),
     "gmmxx_em_accumulate": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P, _P, _P]),
     "gmmxx_em_finalize": (_I32, [_I32, _I64, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P]),
@@ -134,6 +135,13 @@ def call(name: str, *args) -> None:
 
 def stat_width(cov: int, d: int) -> int:
     return int(load().gmmxx_stat_width(cov, d))
+
+
+def accumulate_path(cov: int, xdt: int, b: int, n: int, d: int, k: int) -> int:
+    """1 when gmmxx_em_accumulate runs the tensor-core kernel for this shape, else 0."""
+    out = ctypes.c_int(0)
+    call("gmmxx_accumulate_path", cov, xdt, b, n, d, k, ctypes.addressof(out))
+    return out.value
 
 
 def workspace_bytes(cov: int, b: int, n: int, d: int, k: int) -> int:

@@ -154,8 +154,10 @@ int gmmxx_workspace_status(void* workspace, int* status_out, void* stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, sizeof(int), st);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "workspace status read: %s", cudaGetErrorString(e));
-  *status_out = (host & (1 << GMMXX_ERR_TIMEOUT)) ? GMMXX_ERR_TIMEOUT
-                : (host & (1 << GMMXX_ERR_NOT_PD)) ? GMMXX_ERR_NOT_PD : GMMXX_OK;
+  *status_out = (host & (1 << GMMXX_ERR_TIMEOUT))       ? GMMXX_ERR_TIMEOUT
+                : (host & (1 << GMMXX_ERR_UNSUPPORTED)) ? GMMXX_ERR_UNSUPPORTED
+                : (host & (1 << GMMXX_ERR_NOT_PD))      ? GMMXX_ERR_NOT_PD
+                                                        : GMMXX_OK;
   return GMMXX_OK;
 }
 
@@ -171,6 +173,15 @@ int gmmxx_em_prepare(int cov_type, int64_t B, int64_t D, int64_t K, float* means
   if (int rc = check_ws(workspace, workspace_bytes, L)) return rc;
   return launch_prepare(cov_type, B, D, K, means, cov, weights, reg_covar, min_weight, 1, L,
                         static_cast<char*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+int gmmxx_accumulate_path(int cov_type, int x_dtype, int64_t B, int64_t N, int64_t D, int64_t K, int* path_out) {
+  if (int rc = check_shape(cov_type, x_dtype, B, N, D, K)) return rc;
+  GMMXX_REQUIRE(path_out, "path_out");
+  const Layout L = make_layout(cov_type, B, N, D, K);
+  const bool tc_ok = L.tc_cluster > 0 && x_dtype == GMMXX_BFLOAT16;
+  *path_out = (tc_ok && kernel_mode() != 1) ? 1 : 0;
+  return GMMXX_OK;
 }
 
 int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,

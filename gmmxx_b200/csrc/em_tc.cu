@@ -32,6 +32,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <type_traits>
 
 namespace gmmxx {
 namespace tc {
@@ -49,6 +50,7 @@ constexpr int kBlock = 16384;     // one [128][64] bf16 swizzled block
 constexpr int kAuxBytes = 4096;   // [16][128] K-major aux operand (1, |x|^2 hi / lo)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (log2 units)
 
 // 2^x on the SFU (ex2.approx.ftz: ~2^-22 relative error, subnormal results flushed)
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -67,6 +69,7 @@ template <int COV, int DB>
 struct Cfg {
   static constexpr int D = 64 * DB;
   static constexpr bool kDiag = (COV == GMMXX_DIAG);
+  static constexpr int kMaxCluster = kDiag ? kMaxClusterDiag : 8;  // cluster ranks (128 components each)
   static constexpr int kParamBlocks = kDiag ? 2 * kNS * DB : kNS * DB;
   static constexpr int kParams = 0;
   static constexpr int kStage0 = kParams + kParamBlocks * kBlock;
@@ -80,7 +83,9 @@ struct Cfg {
   static constexpr int kXch = kHalfX + 2 * 128 * 8;
   __host__ __device__ static constexpr int xch_bytes(int C) { return 2 * C * 128 * 8; }
   __host__ __device__ static constexpr int bars(int C) { return kXch + xch_bytes(C); }
-  __host__ __device__ static constexpr int total(int C) { return bars(C) + 256 + 1024; }
+  // barriers (< 192 B) and the epilogue's 4-double reduction slot share the last 256 B
+  __host__ __device__ static constexpr int red(int C) { return bars(C) + 192; }
+  __host__ __device__ static constexpr int total(int C) { return bars(C) + 256; }
   // feature blocks of stage s (byte offsets)
   __host__ __device__ static constexpr int x_blk(int s, int db) { return kStage0 + s * kStageBytes + db * kBlock; }
   __host__ __device__ static constexpr int sh_blk(int s, int db) { return kStage0 + s * kStageBytes + (DB + db) * kBlock; }
@@ -96,7 +101,7 @@ struct Cfg {
   static constexpr int kFdm = kAuxCol + 16;
 };
 
-struct Bars {
+struct Bars {  // lives in dynamic shared memory; see Cfg::bars / Cfg::red
   uint64_t params;
   uint64_t xfull[2];   // TMA: X tile landed
   uint64_t fmain[2];   // prep: SH (diag) / |x|^2 (spherical) ready
@@ -114,6 +119,8 @@ struct Bars {
   int abort;
 };
 
+static_assert(sizeof(Bars) <= 192, "barrier block overlaps the reduction slot");
+
 __device__ __forceinline__ void set_abort(Bars* b, int* status) {
   b->abort = 1;
   atomicOr(status, 1 << GMMXX_ERR_TIMEOUT);
@@ -123,8 +130,16 @@ template <int COV, int DB>
 __global__ void __launch_bounds__(kThreads, 1)
     em_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
   using C = Cfg<COV, DB>;
+  // The dynamic block is the kernel's only shared memory, declared 1024-byte
+  // aligned (the 128-byte swizzle atoms need it).  All shared pointers derive
+  // from it by constant offsets, so every access compiles to a shared-space
+  // instruction rather than a generic one.
   extern __shared__ __align__(1024) char smem_raw[];
-  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  char* sm = smem_raw;
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // uniform across the grid: no CTA proceeds
+    if (threadIdx.x == 0) atomicOr(a.status, 1 << GMMXX_ERR_UNSUPPORTED);
+    return;
+  }
   const int nclus = a.cluster_size;
   Bars* bars = reinterpret_cast<Bars*>(sm + C::bars(nclus));
   float* c_mpm = reinterpret_cast<float*>(sm + C::kConsts);
@@ -199,6 +214,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t id_e = idesc_bf16(128, kKC, 0, 0);
       const uint32_t id_m = idesc_bf16(128, 64, 1, 1);
+      // x | s_hi (diag) or the DB column blocks of x (spherical) in one instruction
+      const uint32_t id_m2 = idesc_bf16(128, C::kDiag ? 128 : 64 * DB, 1, 1);
       const uint32_t id_aux = idesc_bf16(128, 16, 1, 0);
       const uint32_t base = smem_u32(sm);
       const uint32_t r_base = base + C::kR;
@@ -246,47 +263,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&bars->sfull[s]);
         return true;
       };
-      // M-step of tile t with R part `part` (0 = high bf16 terms, 1 = residual)
-      auto issue_m = [&](int t, int part) -> bool {
+      // M-step of tile t with R part PART (0 = high bf16 terms, 1 = residual).
+      // The feature blocks of a stage are adjacent 16 KB blocks ([x | s_hi] for
+      // diag, the DB column blocks of x for spherical), so one MN-major
+      // instruction of N = 128 covers them; PART is a template argument so
+      // that the issue sequence carries no branches between instructions.
+      auto issue_m = [&](int t, auto part_tag) -> bool {
+        constexpr int part = decltype(part_tag)::value;
         const int s = t & 1;
         const int use = 2 * t + part;
         if (!mbar_wait(&bars->rfull, use & 1, abort)) return false;
         tmem_fence_after();
-        const bool first = (t == 0 && part == 0);
+        const uint32_t acc0 = (t == 0 && part == 0) ? 0u : 1u;
         // descriptors at row 0; each 16-row step adds 2048 B (MN-major) or
         // 32 B / 2048 B per 4 steps (K-major aux)
         const uint64_t r0 = desc_mnmajor(r_base, kBlock);
         const uint64_t x0 = desc_mnmajor(base + C::x_blk(s, 0), kBlock);
-        const uint64_t sh0 = C::kDiag ? desc_mnmajor(base + C::sh_blk(s, 0), kBlock) : 0;
         const uint64_t sl0 = C::kDiag ? desc_mnmajor(base + C::sl_blk(0), kBlock) : 0;
         const uint64_t aux0 = desc_kmajor(base + C::aux(s));
+        static_assert(C::kDiag ? C::sh_blk(0, 0) == C::x_blk(0, 0) + kBlock : true, "x and s_hi blocks adjacent");
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // 16 rows per instruction
           const uint64_t step = (uint64_t)(ks * 128);  // 2048 B >> 4
           const uint64_t ra = r0 + step;
-          const uint32_t acc = (first && ks == 0) ? 0u : 1u;
-#pragma unroll
-          for (int db = 0; db < DB; ++db)
-            mma_bf16(tmem + kDmCol + db * 64, ra, x0 + step + (uint64_t)(db * (kBlock >> 4)), id_m, acc);
-          if (C::kDiag) {
-            const uint32_t dcol = tmem + kDmCol + C::D;
-            mma_bf16(dcol, ra, sh0 + step, id_m, acc);
-            if (part == 0) mma_bf16(dcol, ra, sl0 + step, id_m, 1u);
-          }
+          const uint32_t acc = ks == 0 ? acc0 : 1u;
+          mma_bf16(tmem + kDmCol, ra, x0 + step, id_m2, acc);  // [x | s_hi] (diag) or x (spherical)
+          if constexpr (C::kDiag && part == 0) mma_bf16(tmem + kDmCol + C::D, ra, sl0 + step, id_m, 1u);
           mma_bf16(tmem + kDmCol + C::kAuxCol, ra, aux0 + (uint64_t)((ks >> 2) * 128 + (ks & 3) * 2), id_aux, acc);
         }
         mma_commit(&bars->rfree);
-        if (C::kDiag && part == 0) mma_commit(&bars->slfree);
-        if (part == 1) mma_commit(&bars->fempty[s]);
+        if constexpr (C::kDiag && part == 0) mma_commit(&bars->slfree);
+        if constexpr (part == 1) mma_commit(&bars->fempty[s]);
         return true;
       };
+      using Hi = std::integral_constant<int, 0>;
+      using Lo = std::integral_constant<int, 1>;
       if (ok && T > 0) ok = issue_e_main(0) && (!C::kDiag || issue_e_lo(0));
       for (int t = 0; ok && t < T; ++t) {
         const bool more = t + 1 < T;
         if (more && !issue_e_main(t + 1)) { ok = false; break; }
-        if (!issue_m(t, 0)) { ok = false; break; }
+        if (!issue_m(t, Hi{})) { ok = false; break; }
         if (C::kDiag && more && !issue_e_lo(t + 1)) { ok = false; break; }
-        if (!issue_m(t, 1)) { ok = false; break; }
+        if (!issue_m(t, Lo{})) { ok = false; break; }
       }
       if (!ok) set_abort(bars, a.status);
       mma_commit(&bars->mdone);
@@ -402,17 +420,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait_warp(&bars->fmain[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
         qn = qbuf[s * 128 + row];
       }
-      // logits (log2 units) and this half's row max; four independent chains
+      // logits (log2 units) and this half's row max; four independent chains.
+      // Diag components all have distance scale s = 1, so h = log2(e) / 2 is a
+      // constant and only mpm and c2 are read from shared memory.
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int k4 = 0; k4 < kHalf / 4; ++k4) {
-        const float4 vm = cm4[k4], vh = ch4[k4], vc = cc4[k4];
+        const float4 vm = cm4[k4], vc = cc4[k4];
+        const float4 vh = C::kDiag ? make_float4(kHalfLog2e, kHalfLog2e, kHalfLog2e, kHalfLog2e) : ch4[k4];
         const float mm[4] = {vm.x, vm.y, vm.z, vm.w}, hh[4] = {vh.x, vh.y, vh.z, vh.w},
                     cc[4] = {vc.x, vc.y, vc.z, vc.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int k = 4 * k4 + j;
-          const float dist = fmaxf(p[k] + (mm[j] + qn), 0.f);
+          const float dist = C::kDiag ? fmaxf(p[k] + mm[j], 0.f) : fmaxf(p[k] + (mm[j] + qn), 0.f);
           const float l = fmaf(-hh[j], dist, cc[j]);
           p[k] = l;
           mx[j] = fmaxf(mx[j], l);
@@ -442,41 +463,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       // exchange (max, sum) of this CTA's components with the cluster (half 0 sends)
       if (hf == 0) {
         if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
-        for (int q = 0; q < nclus; ++q)
-          st_async_f2(map_shared(xch_mine + s * slot_stride, q), mc, sc2, map_shared(smem_u32(&bars->xch[s]), q));
+#pragma unroll
+        for (int q = 0; q < C::kMaxCluster; ++q)
+          if (q < nclus)
+            st_async_f2(map_shared(xch_mine + s * slot_stride, q), mc, sc2, map_shared(smem_u32(&bars->xch[s]), q));
       }
       if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
-      float M = -INFINITY;
-      for (int q = 0; q < nclus; ++q) M = fmaxf(M, xch[(s * nclus + q) * 128 + row].x);
+      // all ranks' (max, sum) of this row: loads issued together, then combined
+      float2 e[C::kMaxCluster];
+#pragma unroll
+      for (int q = 0; q < C::kMaxCluster; ++q)
+        e[q] = q < nclus ? xch[(s * nclus + q) * 128 + row] : make_float2(-INFINITY, 0.f);
+      float M = e[0].x;
+#pragma unroll
+      for (int q = 1; q < C::kMaxCluster; ++q) M = fmaxf(M, e[q].x);
       float S = 0.f;
-      for (int q = 0; q < nclus; ++q) {
-        const float2 e = xch[(s * nclus + q) * 128 + row];
-        S += e.y * exp2f(e.x - M);
-      }
+#pragma unroll
+      for (int q = 0; q < C::kMaxCluster; ++q)
+        if (q < nclus) S += e[q].y * exp2f(e[q].x - M);
       const float f = valid ? exp2f(m - M) / S : 0.f;
-      if (valid && rank == 0 && hf == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
-      // responsibilities -> R (two passes: bf16 high part, then the residual);
-      // this half's 64 components are exactly R's MN group hf
+      // responsibilities -> R in two passes (bf16 high part, then the residual);
+      // this half's 64 components are exactly R's MN group hf.  Both parts are
+      // formed now; the residual words wait in registers for the second pass.
       char* rg = sm + C::kR + hf * kBlock;
-      for (int part = 0; part < 2; ++part) {
-        const int use = 2 * t + part;
-        if (use >= 1 && !mbar_wait_warp(&bars->rfree, (use - 1) & 1, abort)) { set_abort(bars, a.status); break; }
+      if (t >= 1 && !mbar_wait_warp(&bars->rfree, 1u, abort)) { set_abort(bars, a.status); break; }  // M_lo(t-1)
+      uint32_t lo[kHalf / 2];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t w[4];
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int kk = c * 8 + 2 * i;
-            const float r0 = p[kk] * f, r1 = p[kk + 1] * f;
-            const uint32_t h = pack_bf16(r0, r1);
-            w[i] = part == 0 ? h : pack_bf16(r0 - bf16lo_to_f32(h), r1 - bf16hi_to_f32(h));
-          }
-          *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)(c * 8))) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int i = 0; i < 4; ++i) {
+          const int kk = c * 8 + 2 * i;
+          const float r0 = p[kk] * f, r1 = p[kk + 1] * f;
+          w[i] = pack_bf16(r0, r1);
+          lo[4 * c + i] = pack_bf16(r0 - bf16lo_to_f32(w[i]), r1 - bf16hi_to_f32(w[i]));
         }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->rfull);
+        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)(c * 8))) = make_uint4(w[0], w[1], w[2], w[3]);
       }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->rfull);
+      if (!mbar_wait_warp(&bars->rfree, 0u, abort)) { set_abort(bars, a.status); break; }  // M_hi(t)
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)(c * 8))) =
+            make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->rfull);
+      // log-likelihood of the row, off the R critical path (rank 0 holds it)
+      if (valid && rank == 0 && hf == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
       if (*abort) break;
     }
     // ---------------- epilogue: statistics partials (half-0 warps) ----------------
@@ -501,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_fence_before();
       // log-likelihood partial of this cluster (rank 0 holds it)
-      __shared__ double red[4];
+      double* red = reinterpret_cast<double*>(sm + C::red(nclus));
       double v = ll_acc;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -604,8 +640,8 @@ template <int COV, int DB>
 static int launch_t(const TcLaunch& L, cudaStream_t st) {
   using C = Cfg<COV, DB>;
   const int nclus = L.cluster_size;
-  // dynamic + static shared memory (the kernel's 1 KB static block) <= 227 KB
-  static_assert(C::total(C::kDiag ? kMaxClusterDiag : 8) + 1024 <= 232448, "shared memory budget");
+  // the dynamic block is the kernel's only shared memory: <= 227 KB per CTA
+  static_assert(C::total(C::kMaxCluster) <= 232448, "shared memory budget");
   // 1) pack the component table
   tc_pack_kernel<COV, DB><<<(unsigned)(nclus * kKC), 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
   if (int rc = check_launch("tc_pack_kernel")) return rc;

@@ -230,6 +230,8 @@ class CudaOps:
         nat.call("gmmxx_workspace_status", self.ws.data_ptr(), status.ref(), self.stream)
         if status.value == nat.ERR_TIMEOUT:
             raise nat.GmmxxError(status.value, "a bounded device-side wait expired in the EM kernel")
+        if status.value == nat.ERR_UNSUPPORTED:
+            raise nat.GmmxxError(status.value, "an EM kernel rejected its launch configuration on the device")
         if status.value != nat.OK:
             raise nat.GmmxxError(status.value, "covariance not positive definite after the jitter ladder")
 

@@ -91,8 +91,20 @@ GMMXX_API int64_t gmmxx_stat_width(int cov_type, int64_t D);
  * gmmxx_workspace_status). */
 GMMXX_API size_t gmmxx_workspace_bytes(int cov_type, int64_t B, int64_t N, int64_t D, int64_t K);
 
+/* Which statistics kernels gmmxx_em_accumulate launches for this shape:
+ * *path_out = 1 for the tensor-core kernel (tc_pack_kernel, em_tc_kernel,
+ * tc_reduce_kernel), 0 for the CUDA-core kernels (rows_kernel, mstep_kernel,
+ * stats_reduce_kernel).  Honours GMMXX_B200_KERNEL.  A device that cannot
+ * co-schedule the kernel's thread-block cluster falls back to the CUDA-core
+ * kernels at launch time, which this query does not predict.  No counterpart
+ * in the reference (its dispatch is the Python table in _runtime.py:31-216). */
+GMMXX_API int gmmxx_accumulate_path(int cov_type, int x_dtype, int64_t B, int64_t N, int64_t D, int64_t K,
+                                    int* path_out);
+
 /* Reads (and clears) the sticky device status word kept in `workspace`
- * (GMMXX_OK, GMMXX_ERR_NOT_PD or GMMXX_ERR_TIMEOUT).  Synchronises `stream`. */
+ * (GMMXX_OK, GMMXX_ERR_NOT_PD, GMMXX_ERR_TIMEOUT, or GMMXX_ERR_UNSUPPORTED when
+ * a kernel found its launch configuration unusable, e.g. a misaligned shared
+ * memory block).  Synchronises `stream`. */
 GMMXX_API int gmmxx_workspace_status(void* workspace, int* status_out, void* stream);
 
 /* ---- one soft-EM iteration, in the three steps a sharded driver needs ---- */

@@ -80,3 +80,21 @@ def test_workspace_too_small_is_reported(lib):
     rc = lib.gmmxx_em_prepare(_native.DIAG, 1, 4, 3, ctypes.addressof(m), ctypes.addressof(m), ctypes.addressof(m),
                               1e-6, 1e-8, addr, 16, None)
     assert rc == _native.ERR_WORKSPACE
+
+
+def test_accumulate_path_selection(lib, monkeypatch):
+    """Host-side kernel selection: config-1 shapes take the tensor-core kernel,
+    fp32 / tied / small-N shapes and GMMXX_B200_KERNEL=simt the CUDA-core ones."""
+    from gmmxx_b200 import _native as nat
+
+    monkeypatch.delenv("GMMXX_B200_KERNEL", raising=False)
+    assert nat.accumulate_path(nat.DIAG, nat.BFLOAT16, 1, 50_000_000, 64, 512) == 1
+    assert nat.accumulate_path(nat.SPHERICAL, nat.BFLOAT16, 1, 1 << 20, 128, 1024) == 1
+    assert nat.accumulate_path(nat.DIAG, nat.FLOAT32, 1, 50_000_000, 64, 512) == 0
+    assert nat.accumulate_path(nat.TIED, nat.BFLOAT16, 1, 1 << 20, 64, 256) == 0
+    assert nat.accumulate_path(nat.DIAG, nat.BFLOAT16, 1, 1000, 64, 512) == 0
+    assert nat.accumulate_path(nat.DIAG, nat.BFLOAT16, 2, 1 << 20, 64, 512) == 0
+    monkeypatch.setenv("GMMXX_B200_KERNEL", "simt")
+    assert nat.accumulate_path(nat.DIAG, nat.BFLOAT16, 1, 50_000_000, 64, 512) == 0
+    with pytest.raises(nat.GmmxxError):
+        nat.accumulate_path(7, nat.BFLOAT16, 1, 10, 4, 4)
