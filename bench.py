@@ -345,7 +345,8 @@ def main():
             "config": workload_config(cfg, args),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": ("em_tc_kernel (+ tc_pack_kernel, tc_reduce_kernel)" if tc_path
+                         "kernel": ((("em_tc_diag_kernel" if cfg.cov_type == "diag" else "em_tc_kernel")
+                                     + " (+ tc_pack_kernel, tc_reduce_kernel)") if tc_path
                                     else "rows_kernel + mstep_kernel + stats_reduce_kernel"),
                          "peak_source": f"{peaks['source']} bf16 {'sustained' if long_run else 'burst'}",
                          "algorithmic_flops_per_launch": flops, "launch_ms": acc_ms,

@@ -1,6 +1,9 @@
 // em_tc.cu -- fused soft-EM statistics kernel on the 5th-generation tensor
-// cores (tcgen05 + TMEM + TMA), for bf16 X with diagonal (D = 64, K <= 512)
-// or spherical (D = 64 / 128, K <= 1024) covariance, B == 1.
+// cores (tcgen05 + TMEM + TMA) for bf16 X with spherical covariance
+// (D = 64 / 128, K <= 1024), B == 1, plus the host pieces every tensor-core
+// kernel shares: the per-iteration weight-image packer, the tensor map of X,
+// the clustered launch and the fixed-order reduction of the partials.  The
+// diagonal-covariance kernel is em_tc_diag.cu.
 //
 // One thread-block cluster of C = ceil(K / 128) CTAs works on the same
 // 128-row tile of X at a time; CTA `rank` owns components
@@ -8,23 +11,23 @@
 // its shared memory for the whole launch.  Per row tile:
 //
 //   TMA          X tile (bf16, 128-byte swizzle) -> shared memory
-//   prep warps   exact x^2 = s_hi + s_lo (two bf16, diag) / |x|^2 (spherical)
-//   MMA warp     E-step  S[128 rows, 128 comps] (TMEM, fp32) = features . W^T
+//   prep warps   |x|^2 per row (the aux operand and the softmax's q)
+//   MMA warp     E-step  S[128 rows, 128 comps] (TMEM, fp32) = x . W^T
 //   softmax WG   logits from S, row max / exp / partial sum -> DSMEM exchange
 //                of (max, sum) with the cluster peers -> r = exp(l - lse),
 //                split r = r_hi + r_lo (two bf16) into shared memory
-//   MMA warp     M-step  stats[128 comps, F] (TMEM, fp32) += R^T . [x | x^2 | 1]
+//   MMA warp     M-step  stats[128 comps, F] (TMEM, fp32) += R^T . [x | 1 | |x|^2]
 //
 // so the (N, K) responsibilities never leave the SM and X is read from HBM
-// once per iteration.  Precision: X is exact in bf16; x^2 is split exactly
-// into two bf16 terms; the logit weights into three bf16 terms (24
-// significant bits, fp32-equivalent); r into two (16 bits).  Products are exact
-// and accumulate in fp32, so logits match the fp32 expanded-distance form.
-// Statistics leave the kernel once per cluster as partials that a second
-// kernel reduces in a fixed order (run-to-run deterministic).
+// once per iteration.  Precision: X is exact in bf16; the logit weights are
+// split into three bf16 terms (24 significant bits, fp32-equivalent); r into
+// two (16 bits).  Products are exact and accumulate in fp32, so logits match
+// the fp32 expanded-distance form.  Statistics leave the kernel once per
+// cluster as partials that a second kernel reduces in a fixed order
+// (run-to-run deterministic).
 //
 // Reference semantics: gmmxx/torch_fallback.py:2097-2291 (spherical E/M
-// chunk loop) and 2508-2651 (diag), expanded-distance logits 337-397.
+// chunk loop), expanded-distance logits 337-354.
 #include "gmm_common.cuh"
 #include "tc_ptx.cuh"
 #include "tc_api.cuh"
@@ -622,7 +625,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static EncodeTiledFn encode_fn() {
+EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static bool tried = false;
   if (!tried) {
@@ -636,37 +639,85 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int COV, int DB>
-static int launch_t(const TcLaunch& L, cudaStream_t st) {
-  using C = Cfg<COV, DB>;
-  const int nclus = L.cluster_size;
-  // the dynamic block is the kernel's only shared memory: <= 227 KB per CTA
-  static_assert(C::total(C::kMaxCluster) <= 232448, "shared memory budget");
-  // 1) pack the component table
-  tc_pack_kernel<COV, DB><<<(unsigned)(nclus * kKC), 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
-  if (int rc = check_launch("tc_pack_kernel")) return rc;
-  // 2) tensor map over X (N rows x D bf16), 128-row x 64-col boxes, 128-byte swizzle
+int launch_tc_pack(int cov, int db, const TcLaunch& L, cudaStream_t st) {
+  const unsigned grid = (unsigned)(L.cluster_size * kKC);
+  if (cov == GMMXX_DIAG && db == 1)
+    tc_pack_kernel<GMMXX_DIAG, 1><<<grid, 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
+  else if (cov == GMMXX_SPHERICAL && db == 1)
+    tc_pack_kernel<GMMXX_SPHERICAL, 1><<<grid, 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
+  else if (cov == GMMXX_SPHERICAL && db == 2)
+    tc_pack_kernel<GMMXX_SPHERICAL, 2><<<grid, 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
+  else
+    return set_error(GMMXX_ERR_UNSUPPORTED, "no weight image layout for this shape");
+  return check_launch("tc_pack_kernel");
+}
+
+int make_x_tensor_map(const TcLaunch& L, CUtensorMap* tmap) {
+  // X (N rows x D bf16), 128-row x 64-column boxes, 128-byte swizzle
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return set_error(GMMXX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  CUtensorMap tmap;
-  cuuint64_t dims[2] = {(cuuint64_t)C::D, (cuuint64_t)L.N};
-  cuuint64_t strides[1] = {(cuuint64_t)C::D * 2};
+  cuuint64_t dims[2] = {(cuuint64_t)L.D, (cuuint64_t)L.N};
+  cuuint64_t strides[1] = {(cuuint64_t)L.D * 2};
   cuuint32_t box[2] = {64, (cuuint32_t)kBM};
   cuuint32_t es[2] = {1, 1};
-  CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(L.x), dims, strides, box, es,
+  CUresult cr = enc(tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(L.x), dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return set_error(GMMXX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
-  // 3) persistent clustered launch
-  auto kern = em_tc_kernel<COV, DB>;
-  const int smem = C::total(nclus);
+  return GMMXX_OK;
+}
+
+int launch_tc_reduce(const TcLaunch& L, int ncl, cudaStream_t st) {
+  const int64_t n = (int64_t)L.K * L.F;
+  tc_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(L.part, L.part_ll, ncl, L.K,
+                                                                                      L.Kp_part, L.F, L.stats, L.ll);
+  return check_launch("tc_reduce_kernel");
+}
+
+int clustered_launch(const void* kern, int threads, int smem, const TcLaunch& L, int* ncl_out) {
+  const int nclus = L.cluster_size;
   if (smem > 232448) return set_error(GMMXX_ERR_UNSUPPORTED, "tensor-core kernel shared memory over budget");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_kernel attributes: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "tensor-core kernel attributes: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = nclus;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3((unsigned)nclus);
+  int max_clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
+  if (e != cudaSuccess || max_clusters <= 0) {
+    cudaGetLastError();
+    return set_error(GMMXX_ERR_UNSUPPORTED, "no co-resident cluster of %d CTAs (%s)", nclus, cudaGetErrorString(e));
+  }
+  const int64_t ntiles = (L.N + kBM - 1) / kBM;
+  const int ncl = (int)std::min<int64_t>(std::min<int64_t>(max_clusters, kMaxClusters), ntiles);
+  *ncl_out = ncl;
+  return GMMXX_OK;
+}
+
+template <int COV, int DB>
+static int launch_t(const TcLaunch& L, cudaStream_t st) {
+  using C = Cfg<COV, DB>;
+  // the dynamic block is the kernel's only shared memory: <= 227 KB per CTA
+  static_assert(C::total(C::kMaxCluster) <= 232448, "shared memory budget");
+  if (int rc = launch_tc_pack(COV, DB, L, st)) return rc;
+  CUtensorMap tmap;
+  if (int rc = make_x_tensor_map(L, &tmap)) return rc;
+  auto kern = em_tc_kernel<COV, DB>;
+  const int smem = C::total(L.cluster_size);
+  int ncl = 0;
+  if (int rc = clustered_launch((const void*)kern, kThreads, smem, L, &ncl)) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = L.cluster_size;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(kThreads);
@@ -674,37 +725,25 @@ static int launch_t(const TcLaunch& L, cudaStream_t st) {
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3((unsigned)nclus);
-  int max_clusters = 0;
-  e = cudaOccupancyMaxActiveClusters(&max_clusters, (void*)kern, &cfg);
-  if (e != cudaSuccess || max_clusters <= 0) {
-    cudaGetLastError();
-    return set_error(GMMXX_ERR_UNSUPPORTED, "no co-resident cluster of %d CTAs (%s)", nclus, cudaGetErrorString(e));
-  }
-  const int64_t ntiles = (L.N + kBM - 1) / kBM;
-  const int ncl = (int)std::min<int64_t>(std::min<int64_t>(max_clusters, kMaxClusters), ntiles);
-  cfg.gridDim = dim3((unsigned)(ncl * nclus));
+  cfg.gridDim = dim3((unsigned)(ncl * L.cluster_size));
   TcArgs args{};
   args.N = L.N;
   args.Kp = L.Kp_part;
   args.F = L.F;
-  args.cluster_size = nclus;
+  args.cluster_size = L.cluster_size;
   args.params = L.params;
   args.consts = L.consts;
   args.part = L.part;
   args.part_ll = L.part_ll;
   args.status = L.status;
-  e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_kernel launch: %s", cudaGetErrorString(e));
-  // 4) deterministic reduction into the caller's statistics
-  const int64_t n = (int64_t)L.K * L.F;
-  tc_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(L.part, L.part_ll, ncl, L.K,
-                                                                                      L.Kp_part, L.F, L.stats, L.ll);
-  return check_launch("tc_reduce_kernel");
+  // deterministic reduction into the caller's statistics
+  return launch_tc_reduce(L, ncl, st);
 }
 
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st) {
-  if (cov == GMMXX_DIAG && L.D == 64 && L.cluster_size <= kMaxClusterDiag) return launch_t<GMMXX_DIAG, 1>(L, st);
+  if (cov == GMMXX_DIAG && L.D == 64 && L.cluster_size <= kMaxClusterDiag) return launch_em_tc_diag(L, st);
   if (cov == GMMXX_SPHERICAL && L.D == 64) return launch_t<GMMXX_SPHERICAL, 1>(L, st);
   if (cov == GMMXX_SPHERICAL && L.D == 128) return launch_t<GMMXX_SPHERICAL, 2>(L, st);
   return set_error(GMMXX_ERR_UNSUPPORTED, "no tensor-core kernel for this shape");

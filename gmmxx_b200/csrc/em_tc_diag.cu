@@ -1,0 +1,558 @@
+// em_tc_diag.cu -- fused soft-EM statistics for diagonal covariance on the
+// 5th-generation tensor cores, bf16 X, D = 64, K <= 512, B == 1.
+//
+// A thread-block cluster of C = ceil(K / 128) CTAs works on one 128-row tile
+// of X at a time; CTA `rank` owns components [128 rank, 128 rank + 128) whose
+// split-bf16 logit weights stay resident in its shared memory.  Per tile t:
+//
+//   TMA       X(t) -> a double-buffered staging slot (bf16, 128-byte swizzle)
+//   prep      (4 warps, thread = row) exact x^2 = s_hi + s_lo; the E-step
+//             operand [x | s_hi | s_lo] goes straight into tensor memory, and,
+//             once the M-step of t-1 is done, [x | s_hi | s_lo] into the
+//             single M-step stage in shared memory
+//   MMA       E-step S(t)[rows, comps] = [x | s_hi | s_lo] . W^T with the
+//             A operand read from tensor memory (32 instructions, N = 128)
+//   softmax   (8 warps) logits, row max / exp / sum, (max, sum) exchanged with
+//             the cluster through DSMEM, r = exp(l - lse) split r_hi + r_lo
+//   MMA       M-step stats[comps, x | x^2 | 1] += R^T . [x | s_hi] (+ s_lo, 1)
+//
+// The E-step of tile t+1 therefore depends only on X(t+1) and on the E-step
+// of tile t (tensor-memory operand), never on the M-step buffers, and the
+// softmax warps are software-pipelined: the residual part r_lo of tile t-1
+// is written after the logits of tile t, so the wait for the M-step's high
+// part overlaps useful work.
+//
+// Precision as in em_tc.cu: X exact in bf16, x^2 split exactly into two bf16
+// terms, weights into three (24 significant bits), r into two; products exact,
+// fp32 accumulation.  Statistics leave the kernel once per cluster as
+// partials that tc_reduce_kernel sums in a fixed order.
+//
+// Reference semantics: gmmxx/torch_fallback.py:2508-2651 (diag E/M chunk
+// loop), expanded-distance logits 357-397.
+#include "gmm_common.cuh"
+#include "tc_ptx.cuh"
+#include "tc_api.cuh"
+
+#include <math.h>
+
+#include <algorithm>
+#include <type_traits>
+
+namespace gmmxx {
+namespace tc {
+namespace {
+
+using namespace ptx;
+
+constexpr int kBM = 128;        // rows per tile
+constexpr int kKC = 128;        // components per CTA
+constexpr int kNS = 3;          // bf16 terms of the split weights
+constexpr int kHalf = kKC / 2;  // components per softmax thread
+constexpr int kBlock = 16384;   // one [128][64] bf16 swizzled block
+constexpr int kAuxBytes = 4096; // [16][128] K-major ones operand (n_k)
+constexpr int kThreads = 512;   // 16 warps: 4 prep | TMA, MMA, 2 idle | 8 softmax (128 registers each)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kDmCol = 256;  // M-step statistics [x (64) | x^2 (64) | 1 (16)]
+constexpr uint32_t kFCol = 400;   // E-step operand [x | s_hi | s_lo], 32 columns each
+constexpr int kFdm = 144;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (diag: s = 1)
+constexpr int kMaxCluster = kMaxClusterDiag;
+
+enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpIdle0 = 6, kWarpSoftmax0 = 8 };
+
+// shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
+constexpr int kParams = 0;                     // a_0 a_1 a_2 | v_0 v_1 v_2 (16 KB each)
+constexpr int kStaging = kParams + 2 * kNS * kBlock;  // X staging slots [2]
+constexpr int kMX = kStaging + 2 * kBlock;     // M-step stage: x | s_hi | s_lo
+constexpr int kMSH = kMX + kBlock;
+constexpr int kMSL = kMSH + kBlock;
+constexpr int kAux = kMSL + kBlock;            // ones operand (constant)
+constexpr int kR = kAux + kAuxBytes;           // R: two 64-component MN groups
+constexpr int kConsts = kR + 2 * kBlock;       // mpm[128], h[128], c2[128]
+constexpr int kHalfX = kConsts + 3 * 128 * 4;  // [2 halves][128 rows] float2
+constexpr int kXch = kHalfX + 2 * 128 * 8;     // [2 slots][C][128 rows] float2
+__host__ __device__ constexpr int bars_off(int c) { return kXch + 2 * c * 128 * 8; }
+__host__ __device__ constexpr int red_off(int c) { return bars_off(c) + 192; }
+__host__ __device__ constexpr int smem_total(int c) { return bars_off(c) + 256; }
+static_assert(smem_total(kMaxCluster) <= 232448, "shared memory budget");
+static_assert(kFCol + 96 <= kTmemCols && kDmCol + kFdm <= kFCol, "tensor memory budget");
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+struct Bars {
+  uint64_t params;
+  uint64_t xfull[2];   // TMA: staging slot holds X(t)
+  uint64_t sempty[2];  // prep: staging slot copied into the M-step stage (4 warps)
+  uint64_t ffull;      // prep: E-step operand of tile t in tensor memory (4 warps)
+  uint64_t mfull;      // prep: M-step stage holds tile t (4 warps)
+  uint64_t mfree;      // MMA: M-step of tile t done reading the stage
+  uint64_t sfull[2];   // MMA: S(t) complete (the E-step operand is free again)
+  uint64_t sfree[2];   // softmax: S(t) loaded (8 warps)
+  uint64_t rfull;      // softmax: an R part written (8 warps)
+  uint64_t rfree;      // MMA: that R part consumed
+  uint64_t xch[2];     // cluster exchange of (row max, row sum)
+  uint64_t hx[2];      // both component halves of the row wrote (max, sum) (8 warps)
+  uint64_t mdone;      // MMA: all MMAs complete
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(sizeof(Bars) <= 192, "barrier block overlaps the reduction slot");
+
+__device__ __forceinline__ void set_abort(Bars* b, int* status) {
+  b->abort = 1;
+  atomicOr(status, 1 << GMMXX_ERR_TIMEOUT);
+}
+
+// x -> (s_hi, s_lo) for one packed pair of bf16 values: x^2 is exact in fp32
+// (8-bit significands) and splits exactly into two bf16 terms.
+__device__ __forceinline__ void square_split(uint32_t w, uint32_t& hi, uint32_t& lo) {
+  const float x0 = bf16lo_to_f32(w), x1 = bf16hi_to_f32(w);
+  const float s0 = x0 * x0, s1 = x1 * x1;
+  hi = pack_bf16(s0, s1);
+  lo = pack_bf16(s0 - bf16lo_to_f32(hi), s1 - bf16hi_to_f32(hi));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    em_tc_diag_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* sm = smem_raw;
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // uniform across the grid: no CTA proceeds
+    if (threadIdx.x == 0) atomicOr(a.status, 1 << GMMXX_ERR_UNSUPPORTED);
+    return;
+  }
+  const int nclus = a.cluster_size;
+  Bars* bars = reinterpret_cast<Bars*>(sm + bars_off(nclus));
+  float* c_mpm = reinterpret_cast<float*>(sm + kConsts);
+  float* c_c2 = c_mpm + 256;
+  float2* xch = reinterpret_cast<float2*>(sm + kXch);
+  volatile int* abort = &bars->abort;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const uint32_t cid = cluster_id_x();
+  const uint32_t ncl = ncluster_x();
+  const int64_t ntiles = (a.N + kBM - 1) / kBM;
+  const int T = (int)((ntiles > (int64_t)cid) ? (ntiles - 1 - cid) / ncl + 1 : 0);
+
+  if (tid == 0) {
+    mbar_init(&bars->params, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->xfull[i], 1);
+      mbar_init(&bars->sempty[i], 4);
+      mbar_init(&bars->sfull[i], 1);
+      mbar_init(&bars->sfree[i], 8);
+      mbar_init(&bars->xch[i], 1);
+      mbar_init(&bars->hx[i], 8);
+    }
+    mbar_init(&bars->ffull, 4);
+    mbar_init(&bars->mfull, 4);
+    mbar_init(&bars->mfree, 1);
+    mbar_init(&bars->rfull, 8);
+    mbar_init(&bars->rfree, 1);
+    mbar_init(&bars->mdone, 1);
+    bars->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kWarpMma) tmem_alloc(&bars->tmem_base, kTmemCols);
+  for (int i = tid; i < 3 * 128; i += kThreads) c_mpm[i] = a.consts[(int64_t)rank * 3 * 128 + i];
+  {  // ones operand of the n_k statistic: K-major [16][128], row 0 = 1
+    char* aux = sm + kAux;
+    for (int i = tid; i < 16 * 128; i += kThreads) {
+      const int n = i >> 7, r = i & 127;
+      *reinterpret_cast<__nv_bfloat16*>(aux + (r >> 6) * 2048 + sw128(n, r & 63)) = __float2bfloat16(n == 0 ? 1.f : 0.f);
+    }
+  }
+  fence_proxy_async();
+  tmem_fence_before();
+  __syncthreads();
+  cluster_sync();  // peers' barriers initialised before any DSMEM traffic
+  tmem_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp < kWarpTma) {
+    // ---------------- prep: 4 warps, thread = row (its TMEM lane) ----------------
+    const int r = warp * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const uint32_t swz = (uint32_t)(r & 7);
+    // the 32 words (64 bf16) of row r of staging slot `slot`, in element order
+    auto load_row = [&](int slot, uint32_t (&w)[32]) {
+      const char* base = sm + kStaging + slot * kBlock + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = *reinterpret_cast<const uint4*>(base + ((c ^ swz) << 4));
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+    };
+    // M-step stage of tile u: wait until the M-step of u-1 released it, then
+    // [x | s_hi | s_lo] (same swizzled layout as the staging slot)
+    auto fill_mstage = [&](int u) -> bool {
+      if (u >= 1 && !mbar_wait_warp(&bars->mfree, (u - 1) & 1, abort)) return false;
+      uint32_t w[32];
+      load_row(u & 1, w);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) square_split(w[4 * c + i], hi[i], lo[i]);
+        const int off = r * 128 + (int)((c ^ swz) << 4);
+        *reinterpret_cast<uint4*>(sm + kMX + off) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        *reinterpret_cast<uint4*>(sm + kMSH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(sm + kMSL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars->mfull);
+        mbar_arrive(&bars->sempty[u & 1]);
+      }
+      return true;
+    };
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int s = t & 1;
+      if (!mbar_wait_warp(&bars->xfull[s], (t >> 1) & 1, abort)) { ok = false; break; }
+      uint32_t w[32];
+      load_row(s, w);
+      // the E-step of t-1 read the operand region: wait for its completion
+      if (t >= 1 && !mbar_wait_warp(&bars->sfull[(t - 1) & 1], ((t - 1) >> 1) & 1, abort)) { ok = false; break; }
+      tmem_fence_after();
+      tmem_st32(tmem + lane_addr + kFCol, w);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {  // s_hi / s_lo in 16-column pieces
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) square_split(w[16 * h + i], hi[i], lo[i]);
+        tmem_st16(tmem + lane_addr + kFCol + 32 + 16 * h, hi);
+        tmem_st16(tmem + lane_addr + kFCol + 64 + 16 * h, lo);
+      }
+      tmem_wait_st();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->ffull);
+      if (t >= 1 && !fill_mstage(t - 1)) { ok = false; break; }
+      if (*abort) { ok = false; break; }
+    }
+    if (ok && T >= 1 && !fill_mstage(T - 1)) ok = false;
+    if (!ok) set_abort(bars, a.status);
+  } else if (warp == kWarpTma) {
+    // ---------------- producer: weights once, then X tiles into the staging slots ----------------
+    if (lane == 0) {
+      prefetch_tmap(&tmap);
+      constexpr int kParamBlocks = 2 * kNS;
+      mbar_expect_tx(&bars->params, kParamBlocks * kBlock);
+      const char* src = a.params + (int64_t)rank * kParamBlocks * kBlock;
+      for (int i = 0; i < kParamBlocks; ++i)
+        bulk_load(sm + kParams + i * kBlock, src + (int64_t)i * kBlock, kBlock, &bars->params);
+      int issued = 0;
+      for (int t = 0; t < T; ++t) {
+        const int s = t & 1;
+        if (t >= 2 && !mbar_wait(&bars->sempty[s], ((t >> 1) - 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        const int row0 = (int)((cid + (int64_t)t * ncl) * kBM);
+        mbar_expect_tx(&bars->xfull[s], kBlock);
+        tma_load_2d(sm + kStaging + s * kBlock, &tmap, 0, row0, &bars->xfull[s]);
+        issued = t + 1;
+      }
+      // before the CTA can exit, every copy it started has landed (bounded,
+      // also after an abort): the weights and the last load of each slot
+      mbar_wait(&bars->params, 0, nullptr, 1000000000ull);
+      for (int t = std::max(0, issued - 2); t < issued; ++t)
+        mbar_wait(&bars->xfull[t & 1], (t >> 1) & 1, nullptr, 1000000000ull);
+    }
+  } else if (warp == kWarpMma) {
+    // ---------------- MMA issuer (one thread) ----------------
+    if (lane == 0) {
+      const uint32_t id_e = idesc_bf16(128, kKC, 0, 0);  // A (TMEM) x W^T (K-major)
+      const uint32_t id_m2 = idesc_bf16(128, 128, 1, 1);  // R^T x [x | s_hi], both MN-major
+      const uint32_t id_m = idesc_bf16(128, 64, 1, 1);    // R_hi^T x s_lo
+      const uint32_t id_aux = idesc_bf16(128, 16, 1, 0);  // R^T x 1
+      const uint32_t base = smem_u32(sm);
+      bool ok = mbar_wait(&bars->params, 0, abort);
+      tmem_fence_after();
+      // weight descriptors: K-major blocks, +32 B per 16-feature step
+      uint64_t wa[kNS], wv[kNS];
+#pragma unroll
+      for (int j = 0; j < kNS; ++j) {
+        wa[j] = desc_kmajor(base + kParams + j * kBlock);
+        wv[j] = desc_kmajor(base + kParams + (kNS + j) * kBlock);
+      }
+      // E-step of tile t into S[t & 1]: x.a_j, s_hi.v_j (j < 3), s_lo.v_j (j < 2)
+      auto issue_e = [&](int t) -> bool {
+        const int s = t & 1;
+        if (!mbar_wait(&bars->ffull, t & 1, abort)) return false;
+        if (t >= 2 && !mbar_wait(&bars->sfree[s], ((t >> 1) - 1) & 1, abort)) return false;
+        tmem_fence_after();
+        const uint32_t d = tmem + (uint32_t)(s * kKC);
+        uint32_t acc = 0;
+#pragma unroll
+        for (int j = 0; j < kNS; ++j)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            mma_bf16_ts(d, tmem + kFCol + kk * 8, wa[j] + 2 * kk, id_e, acc);
+            acc = 1;
+          }
+#pragma unroll
+        for (int j = 0; j < kNS; ++j)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 32 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+        mma_commit(&bars->sfull[s]);
+        return true;
+      };
+      const uint64_t r0 = desc_mnmajor(base + kR, kBlock);
+      const uint64_t x0 = desc_mnmajor(base + kMX, kBlock);  // [x | s_hi]: adjacent 16 KB groups
+      const uint64_t sl0 = desc_mnmajor(base + kMSL, kBlock);
+      const uint64_t aux0 = desc_kmajor(base + kAux);
+      // M-step of tile t with R part PART (0 = high bf16 terms, 1 = residual)
+      auto issue_m = [&](int t, auto part_tag) -> bool {
+        constexpr int part = decltype(part_tag)::value;
+        const int use = 2 * t + part;
+        if (!mbar_wait(&bars->rfull, use & 1, abort)) return false;
+        if (part == 0 && !mbar_wait(&bars->mfull, t & 1, abort)) return false;
+        tmem_fence_after();
+        const uint32_t acc0 = (t == 0 && part == 0) ? 0u : 1u;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {  // 16 rows per instruction: +2048 B (MN-major)
+          const uint64_t step = (uint64_t)(ks * 128);
+          const uint64_t ra = r0 + step;
+          const uint32_t acc = ks == 0 ? acc0 : 1u;
+          mma_bf16(tmem + kDmCol, ra, x0 + step, id_m2, acc);
+          if constexpr (part == 0) mma_bf16(tmem + kDmCol + 64, ra, sl0 + step, id_m, 1u);
+          mma_bf16(tmem + kDmCol + 128, ra, aux0 + (uint64_t)((ks >> 2) * 128 + (ks & 3) * 2), id_aux, acc);
+        }
+        mma_commit(&bars->rfree);
+        if constexpr (part == 1) mma_commit(&bars->mfree);
+        return true;
+      };
+      using Hi = std::integral_constant<int, 0>;
+      using Lo = std::integral_constant<int, 1>;
+      // Issue order: E(0), E(1), then per tile M_hi(t), E(t+2), M_lo(t).  E(t+2)
+      // needs only the operand of t+2 (prep, after E(t+1)) and S slot t & 1
+      // (loaded by the softmax at the start of tile t); M_lo(t) waits for the
+      // residual R(t), written by the softmax after the logits of t+1.  So the
+      // E-steps run about two tiles ahead and never queue behind a residual part.
+      if (ok && T > 0) ok = issue_e(0);
+      if (ok && T > 1) ok = issue_e(1);
+      for (int t = 0; ok && t < T; ++t) {
+        if (!issue_m(t, Hi{})) { ok = false; break; }
+        if (t + 2 < T && !issue_e(t + 2)) { ok = false; break; }
+        if (!issue_m(t, Lo{})) { ok = false; break; }
+      }
+      if (!ok) set_abort(bars, a.status);
+      mma_commit(&bars->mdone);
+    }
+  } else if (warp >= kWarpSoftmax0) {
+    // ---------------- softmax: 8 warps, two per TMEM lane quarter ----------------
+    const int q4 = warp & 3;
+    const int hf = (warp - kWarpSoftmax0) >> 2;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    const int k0 = hf * kHalf;
+    double ll_acc = 0.0;
+    float p[kHalf];
+    uint32_t lo[kHalf / 2];  // residual words of the previous tile, written one iteration later
+    float2* halfx = reinterpret_cast<float2*>(sm + kHalfX);
+    const uint32_t xch_mine = smem_u32(&xch[(int)rank * 128 + row]);
+    const uint32_t slot_stride = (uint32_t)(nclus * 128 * 8);
+    const float4* cm4 = reinterpret_cast<const float4*>(c_mpm + k0);
+    const float4* cc4 = reinterpret_cast<const float4*>(c_c2 + k0);
+    char* rg = sm + kR + hf * kBlock;  // this half's 64 components are R's MN group hf
+    auto store_r = [&](const uint32_t* w) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)(c * 8))) =
+            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->rfull);
+    };
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int s = t & 1;
+      const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
+      const bool valid = grow < a.N;
+      if (!mbar_wait_warp(&bars->sfull[s], (t >> 1) & 1, abort)) { ok = false; break; }
+      tmem_fence_after();
+      const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC + k0);
+      tmem_ld32(sc, p);
+      tmem_ld32(sc + 32, p + 32);
+      tmem_wait_ld();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->sfree[s]);
+      // logits (log2 units) c2 - h max(S + mpm, 0), h = log2(e)/2, and this half's max
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int k4 = 0; k4 < kHalf / 4; ++k4) {
+        const float4 vm = cm4[k4], vc = cc4[k4];
+        const float mm[4] = {vm.x, vm.y, vm.z, vm.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k = 4 * k4 + j;
+          const float l = fmaf(-kHalfLog2e, fmaxf(p[k] + mm[j], 0.f), cc[j]);
+          p[k] = l;
+          mx[j] = fmaxf(mx[j], l);
+        }
+      }
+      // residual part of the previous tile (the M-step's high part of t-1 ran meanwhile)
+      if (t >= 1) {
+        if (!mbar_wait_warp(&bars->rfree, 0u, abort)) { ok = false; break; }  // M_hi(t-1)
+        store_r(lo);
+      }
+      const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float mref = (m == -INFINITY) ? 0.f : m;  // an all-padding half has p = 0
+      float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < kHalf; ++k) {
+        p[k] = ex2_approx(p[k] - mref);
+        sm4[k & 3] += p[k];
+      }
+      const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
+      // combine the two halves of the row.  One buffer suffices: a half
+      // rewrites its entry for tile t+1 only after writing R_lo(t), which
+      // waits for M_hi(t), which waited for the other half's R_hi(t) -- and
+      // that half read this entry before writing R_hi(t).
+      halfx[hf * 128 + row] = make_float2(m, sum);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->hx[s]);
+      if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort)) { ok = false; break; }
+      const float2 o = halfx[(hf ^ 1) * 128 + row];
+      const float mc = fmaxf(m, o.x);
+      // exponents <= 0 here; ex2.approx (relative error ~2^-22) flushes results
+      // below 2^-126, i.e. halves 2^126 times smaller than the row's largest
+      const float sc2 = sum * ex2_approx(m - mc) + o.y * ex2_approx(o.x - mc);
+      // exchange (max, sum) of this CTA's components with the cluster (half 0 sends)
+      if (hf == 0) {
+        if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
+#pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q)
+          if (q < nclus)
+            st_async_f2(map_shared(xch_mine + s * slot_stride, q), mc, sc2, map_shared(smem_u32(&bars->xch[s]), q));
+      }
+      if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort)) { ok = false; break; }
+      float2 e[kMaxCluster];
+#pragma unroll
+      for (int q = 0; q < kMaxCluster; ++q)
+        e[q] = q < nclus ? xch[(s * nclus + q) * 128 + row] : make_float2(-INFINITY, 0.f);
+      float M = e[0].x;
+#pragma unroll
+      for (int q = 1; q < kMaxCluster; ++q) M = fmaxf(M, e[q].x);
+      float S = 0.f;
+#pragma unroll
+      for (int q = 0; q < kMaxCluster; ++q)
+        if (q < nclus) S += e[q].y * ex2_approx(e[q].x - M);
+      const float f = valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f;
+      // high part of tile t now (after the M-step's residual part of t-1);
+      // the residual words stay in registers for the next iteration
+      if (t >= 1 && !mbar_wait_warp(&bars->rfree, 1u, abort)) { ok = false; break; }  // M_lo(t-1)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 8 components per 16-byte store
+        uint32_t hw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = 8 * c + 2 * i;
+          const float r0 = p[k] * f, r1 = p[k + 1] * f;
+          hw[i] = pack_bf16(r0, r1);
+          lo[4 * c + i] = pack_bf16(r0 - bf16lo_to_f32(hw[i]), r1 - bf16hi_to_f32(hw[i]));
+        }
+        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)(c * 8))) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->rfull);
+      if (valid && rank == 0 && hf == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
+      if (*abort) { ok = false; break; }
+    }
+    // the residual part of the last tile
+    if (ok && T >= 1) {
+      if (mbar_wait_warp(&bars->rfree, 0u, abort)) store_r(lo);
+      else ok = false;
+    }
+    if (!ok) set_abort(bars, a.status);
+    // ---------------- epilogue: statistics partials (half-0 warps) ----------------
+    // the MMA thread always commits `mdone` (also after an abort): wait for it
+    // without the abort shortcut before touching tensor memory again
+    if (hf == 0) {
+      if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 4000000000ull)) set_abort(bars, a.status);
+      tmem_fence_after();
+      const int comp = (int)rank * kKC + row;  // this thread's TMEM lane = component
+      float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
+      for (int c0 = 0; c0 < kFdm; c0 += 16) {
+        float v[32];
+        tmem_ld32(tmem + lane_addr + kDmCol + c0, v);  // 32 columns; 16 used per step
+        tmem_wait_ld();
+        for (int j = 0; j < 16 && c0 + j < kFdm; ++j) {
+          const int col = c0 + j;
+          if (col < 128) out[1 + col] = v[j];  // sum r x (0..63), sum r x^2 (64..127)
+          else if (col == 128) out[0] = v[j];  // n_k
+        }
+      }
+      tmem_fence_before();
+      double* red = reinterpret_cast<double*>(sm + red_off(nclus));
+      double v = ll_acc;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[q4] = v;
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (tid == kWarpSoftmax0 * 32 && rank == 0) a.part_ll[cid] = red[0] + red[1] + red[2] + red[3];
+    }
+  }
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tmem_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  cluster_sync();  // no CTA exits while a peer may still write into its shared memory
+}
+
+}  // namespace
+
+int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st) {
+  if (L.D != 64 || L.cluster_size < 1 || L.cluster_size > kMaxCluster)
+    return set_error(GMMXX_ERR_UNSUPPORTED, "diag tensor-core kernel: D = 64, K <= %d", 128 * kMaxCluster);
+  if (int rc = launch_tc_pack(GMMXX_DIAG, 1, L, st)) return rc;
+  CUtensorMap tmap;
+  if (int rc = make_x_tensor_map(L, &tmap)) return rc;
+  const int smem = smem_total(L.cluster_size);
+  int ncl = 0;
+  if (int rc = clustered_launch((const void*)em_tc_diag_kernel, kThreads, smem, L, &ncl)) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = L.cluster_size;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3((unsigned)(ncl * L.cluster_size));
+  TcArgs args{};
+  args.N = L.N;
+  args.Kp = L.Kp_part;
+  args.F = L.F;
+  args.cluster_size = L.cluster_size;
+  args.params = L.params;
+  args.consts = L.consts;
+  args.part = L.part;
+  args.part_ll = L.part_ll;
+  args.status = L.status;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, em_tc_diag_kernel, tmap, args);
+  if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_diag_kernel launch: %s", cudaGetErrorString(e));
+  return launch_tc_reduce(L, ncl, st);
+}
+
+}  // namespace tc
+}  // namespace gmmxx

@@ -4,6 +4,8 @@
 
 #include "gmm_common.cuh"
 
+#include <cuda.h>
+
 namespace gmmxx {
 namespace tc {
 
@@ -42,6 +44,16 @@ struct TcLaunch {
 };
 
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st);
+
+// pieces shared by the tensor-core kernels (em_tc.cu, em_tc_diag.cu)
+int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st);
+int launch_tc_pack(int cov, int db, const TcLaunch& L, cudaStream_t st);  // weight images + logit constants
+int make_x_tensor_map(const TcLaunch& L, CUtensorMap* tmap);             // 128 x 64 bf16 boxes, 128 B swizzle
+int launch_tc_reduce(const TcLaunch& L, int ncl, cudaStream_t st);       // fixed-order partials -> stats
+// Sets the kernel's shared-memory attribute and returns in *ncl_out how many
+// clusters of L.cluster_size CTAs (threads x smem each) run at once, capped by
+// the partials buffer and the tile count.
+int clustered_launch(const void* kern, int threads, int smem, const TcLaunch& L, int* ncl_out);
 
 }  // namespace tc
 }  // namespace gmmxx
