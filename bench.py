@@ -204,7 +204,7 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
         comm = engine.Comm()
     nat.load()
 
