@@ -206,9 +206,12 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
     t.D = (int)D;
     t.K = (int)K;
     t.Kp_table = L.Kp;
-    t.Kp_part = (int64_t)L.tc_cluster * 128;
+    t.Kp_part = (int64_t)L.tc_cluster * 128;  // per group for the grouped large-K path
     t.F = stat_width(cov_type, (int)D);
     t.cluster_size = L.tc_cluster;
+    t.nchunks = L.tc_chunks;
+    t.rowstat = L.tc_rowstat ? reinterpret_cast<float2*>(ws + L.tc_rowstat) : nullptr;
+    t.lse = L.tc_lse ? reinterpret_cast<float*>(ws + L.tc_lse) : nullptr;
     t.wt = reinterpret_cast<const float*>(ws + L.wt);
     t.cc = reinterpret_cast<const CompConst*>(ws + L.cc);
     t.params = ws + L.tc_params;

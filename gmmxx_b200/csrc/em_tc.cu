@@ -64,6 +64,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 enum Warp { kWarpTma = 0, kWarpMma = 1, kWarpPrep0 = 2, kWarpSoftmax0 = 4 };
 
+// Launch modes.  kModeFull: the whole of K in one cluster (K <= 1024).
+// Large K runs as groups of 8 chunks (1024 components) in two passes:
+// kModeRowStat writes each row's (max, scaled sum) over the group's
+// components, tc_lse_combine_kernel folds the groups into the row's
+// log-sum-exp, and kModeExtLse turns that into responsibilities and the
+// M-step statistics of the group's components.
+enum Mode { kModeFull = 0, kModeRowStat = 1, kModeExtLse = 2 };
+
 // Shared-memory carve-up (byte offsets from a 1024-aligned base).
 //   diag      : weights (a_j, v_j) | stages{X, SH} x2 | SL (single) | aux (constant)
 //   spherical : weights (a_j)      | stages{X, aux} x2
@@ -83,7 +91,7 @@ struct Cfg {
   static constexpr int kConsts = kR + 2 * kBlock;  // mpm[128], h[128], c2[128]
   static constexpr int kQ = kConsts + 3 * 128 * 4; // q[2][128] (spherical)
   static constexpr int kHalfX = kQ + (kDiag ? 0 : 2 * 128 * 4);  // [2 halves][128 rows] float2
-  static constexpr int kXch = kHalfX + 2 * 128 * 8;
+  static constexpr int kXch = kHalfX + 2 * 2 * 128 * 8;  // halfx: [tile parity][half][row] float2
   __host__ __device__ static constexpr int xch_bytes(int C) { return 2 * C * 128 * 8; }
   __host__ __device__ static constexpr int bars(int C) { return kXch + xch_bytes(C); }
   // barriers (< 192 B) and the epilogue's 4-double reduction slot share the last 256 B
@@ -129,9 +137,10 @@ __device__ __forceinline__ void set_abort(Bars* b, int* status) {
   atomicOr(status, 1 << GMMXX_ERR_TIMEOUT);
 }
 
-template <int COV, int DB>
+template <int COV, int DB, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     em_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
+  static_assert(MODE == kModeFull || COV == GMMXX_SPHERICAL, "grouped passes are spherical only");
   using C = Cfg<COV, DB>;
   // The dynamic block is the kernel's only shared memory, declared 1024-byte
   // aligned (the 128-byte swizzle atoms need it).  All shared pointers derive
@@ -180,7 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == kWarpMma) tmem_alloc(&bars->tmem_base, kTmemCols);
   // constants of this CTA's component chunk; constant rows of the aux operand(s)
-  for (int i = tid; i < 3 * 128; i += kThreads) c_mpm[i] = a.consts[(int64_t)rank * 3 * 128 + i];
+  const int chunk = a.chunk0 + (int)rank;  // this CTA's 128-component chunk of K
+  for (int i = tid; i < 3 * 128; i += kThreads) c_mpm[i] = a.consts[(int64_t)chunk * 3 * 128 + i];
   for (int s = 0; s < (C::kDiag ? 1 : 2); ++s) {
     char* aux = sm + C::aux(s);
     for (int i = tid; i < 16 * 128; i += kThreads) {
@@ -201,12 +211,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       prefetch_tmap(&tmap);
       mbar_expect_tx(&bars->params, C::kParamBlocks * kBlock);
-      const char* src = a.params + (int64_t)rank * C::kParamBlocks * kBlock;
+      const char* src = a.params + (int64_t)chunk * C::kParamBlocks * kBlock;
       for (int i = 0; i < C::kParamBlocks; ++i)
         bulk_load(sm + C::kParams + i * kBlock, src + (int64_t)i * kBlock, kBlock, &bars->params);
       for (int t = 0; t < T; ++t) {
         const int s = t & 1;
         if (t >= 2 && !mbar_wait(&bars->fempty[s], ((t >> 1) - 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        // without an M-step the stage is free once the E-step read it; the
+        // softmax must also have read the stage's |x|^2 entries (qbuf)
+        if (MODE == kModeRowStat && t >= 2 && !mbar_wait(&bars->sfree[s], ((t >> 1) - 1) & 1, abort)) {
+          set_abort(bars, a.status);
+          break;
+        }
         const int row0 = (int)((cid + (int64_t)t * ncl) * kBM);
         mbar_expect_tx(&bars->xfull[s], DB * kBlock);
         for (int db = 0; db < DB; ++db) tma_load_2d(sm + C::x_blk(s, db), &tmap, db * 64, row0, &bars->xfull[s]);
@@ -301,13 +317,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       using Hi = std::integral_constant<int, 0>;
       using Lo = std::integral_constant<int, 1>;
-      if (ok && T > 0) ok = issue_e_main(0) && (!C::kDiag || issue_e_lo(0));
-      for (int t = 0; ok && t < T; ++t) {
-        const bool more = t + 1 < T;
-        if (more && !issue_e_main(t + 1)) { ok = false; break; }
-        if (!issue_m(t, Hi{})) { ok = false; break; }
-        if (C::kDiag && more && !issue_e_lo(t + 1)) { ok = false; break; }
-        if (!issue_m(t, Lo{})) { ok = false; break; }
+      if constexpr (MODE == kModeRowStat) {
+        for (int t = 0; ok && t < T; ++t) {
+          if (!issue_e_main(t)) { ok = false; break; }
+          mma_commit(&bars->fempty[t & 1]);  // no M-step: the stage is free after E(t)
+        }
+      } else {
+        if (ok && T > 0) ok = issue_e_main(0) && (!C::kDiag || issue_e_lo(0));
+        for (int t = 0; ok && t < T; ++t) {
+          const bool more = t + 1 < T;
+          if (more && !issue_e_main(t + 1)) { ok = false; break; }
+          if (!issue_m(t, Hi{})) { ok = false; break; }
+          if (C::kDiag && more && !issue_e_lo(t + 1)) { ok = false; break; }
+          if (!issue_m(t, Lo{})) { ok = false; break; }
+        }
       }
       if (!ok) set_abort(bars, a.status);
       mma_commit(&bars->mdone);
@@ -357,7 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&bars->fl);
         if (*abort) break;
       } else {
-        // |x|^2 per row (two threads per row), q_hi / q_lo into the aux operand
+        // |x|^2 per row (two threads per row), three bf16 terms q_0 + q_1 + q_2
+        // (24 significant bits) into the aux operand
         char* aux = sm + C::aux(s);
         const int r = ptid >> 1, hf = ptid & 1;
         for (int rr = r; rr < kBM; rr += 32) {
@@ -376,11 +400,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc += __shfl_xor_sync(0xffffffffu, acc, 1);
           if (hf == 0) {
             qbuf[s * 128 + rr] = acc;
-            const __nv_bfloat16 qh = __float2bfloat16(acc);
-            const __nv_bfloat16 ql = __float2bfloat16(acc - __bfloat162float(qh));
             char* blk = aux + (rr >> 6) * 2048;
-            *reinterpret_cast<__nv_bfloat16*>(blk + sw128(1, rr & 63)) = qh;
-            *reinterpret_cast<__nv_bfloat16*>(blk + sw128(2, rr & 63)) = ql;
+            float rem = acc;
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+              const __nv_bfloat16 qj = __float2bfloat16(rem);
+              *reinterpret_cast<__nv_bfloat16*>(blk + sw128(1 + j, rr & 63)) = qj;
+              rem -= __bfloat162float(qj);
+            }
           }
         }
         fence_proxy_async();
@@ -414,15 +441,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC + k0);
       tmem_ld32(sc, p);
       tmem_ld32(sc + 32, p + 32);
-      tmem_wait_ld();
-      tmem_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sfree[s]);
       float qn = 0.f;
       if (!C::kDiag) {  // |x|^2 of this row (signalled by the prep warps before S was issued)
         if (!mbar_wait_warp(&bars->fmain[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
         qn = qbuf[s * 128 + row];
       }
+      tmem_wait_ld();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->sfree[s]);  // S(t) and this row's |x|^2 consumed
       // logits (log2 units) and this half's row max; four independent chains.
       // Diag components all have distance scale s = 1, so h = log2(e) / 2 is a
       // constant and only mpm and c2 are read from shared memory.
@@ -443,6 +470,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      float M = 0.f, S = 1.f, f = 0.f;
+      if constexpr (MODE == kModeExtLse) {
+        // responsibilities from the row's log-sum-exp over all K (log2 units)
+        const float lse = valid ? a.lse_in[grow] : 0.f;
+#pragma unroll
+        for (int k = 0; k < kHalf; ++k) p[k] = ex2_approx(p[k] - lse);
+        f = valid ? 1.f : 0.f;
+      } else {
       // a half made only of padding components has m = -inf: its p must be 0
       const float mref = (m == -INFINITY) ? 0.f : m;
       float sm4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -452,15 +487,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm4[k & 3] += p[k];
       }
       const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
-      // combine the two halves of the row.  One buffer suffices: a half
-      // rewrites its entry for tile t+1 only after writing R_lo(t), which
-      // waits for M_hi(t), which waited for the other half's R_hi(t) -- and
-      // that half read this entry before writing R_hi(t).
-      halfx[hf * 128 + row] = make_float2(m, sum);
+      // combine the two halves of the row, one buffer per tile parity: a half
+      // writes its entry for tile t+2 only after the hx barrier of tile t+1,
+      // which the other half passes after reading this tile's entry.
+      float2* hxs = halfx + s * 2 * 128;
+      hxs[hf * 128 + row] = make_float2(m, sum);
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->hx[s]);
       if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
-      const float2 o = halfx[(hf ^ 1) * 128 + row];
+      const float2 o = hxs[(hf ^ 1) * 128 + row];
       const float mc = fmaxf(m, o.x);
       const float sc2 = sum * exp2f(m - mc) + o.y * exp2f(o.x - mc);
       // exchange (max, sum) of this CTA's components with the cluster (half 0 sends)
@@ -477,14 +512,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int q = 0; q < C::kMaxCluster; ++q)
         e[q] = q < nclus ? xch[(s * nclus + q) * 128 + row] : make_float2(-INFINITY, 0.f);
-      float M = e[0].x;
+      M = e[0].x;
 #pragma unroll
       for (int q = 1; q < C::kMaxCluster; ++q) M = fmaxf(M, e[q].x);
-      float S = 0.f;
+      S = 0.f;
 #pragma unroll
       for (int q = 0; q < C::kMaxCluster; ++q)
         if (q < nclus) S += e[q].y * exp2f(e[q].x - M);
-      const float f = valid ? exp2f(m - M) / S : 0.f;
+      if constexpr (MODE == kModeRowStat) {
+        // the row's (max, scaled sum) over this group's components; no R, no M-step
+        if (valid && rank == 0 && hf == 0) a.rowstat[grow] = make_float2(M, S);
+        if (*abort) break;
+        continue;
+      }
+      f = valid ? exp2f(m - M) / S : 0.f;
+      }
       // responsibilities -> R in two passes (bf16 high part, then the residual);
       // this half's 64 components are exactly R's MN group hf.  Both parts are
       // formed now; the residual words wait in registers for the second pass.
@@ -515,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->rfull);
       // log-likelihood of the row, off the R critical path (rank 0 holds it)
-      if (valid && rank == 0 && hf == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
+      if (MODE == kModeFull && valid && rank == 0 && hf == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
       if (*abort) break;
     }
     // ---------------- epilogue: statistics partials (half-0 warps) ----------------
@@ -524,6 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (hf == 0) {
       if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 4000000000ull)) set_abort(bars, a.status);
       tmem_fence_after();
+    }
+    if (hf == 0 && MODE != kModeRowStat) {
       const int comp = (int)rank * kKC + row;  // this thread's TMEM lane = component
       float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
       for (int c0 = 0; c0 < C::kFdm; c0 += 16) {
@@ -535,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (col < C::D) out[1 + col] = v[j];                                  // sum r x
           else if (C::kDiag && col < 2 * C::D) out[1 + col] = v[j];             // sum r x^2
           else if (col == C::kAuxCol) out[0] = v[j];                            // n_k
-          else if (!C::kDiag && col == C::kAuxCol + 1) out[1 + C::D] = v[j] + v[j + 1];  // sum r |x|^2
+          else if (!C::kDiag && col == C::kAuxCol + 1) out[1 + C::D] = v[j] + v[j + 1] + v[j + 2];  // sum r |x|^2
         }
       }
       tmem_fence_before();
@@ -546,7 +590,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       if (lane == 0) red[q4] = v;
       asm volatile("bar.sync 2, 128;" ::: "memory");
-      if (tid == kWarpSoftmax0 * 32 && rank == 0) a.part_ll[cid] = red[0] + red[1] + red[2] + red[3];
+      if (MODE == kModeFull && tid == kWarpSoftmax0 * 32 && rank == 0)
+        a.part_ll[cid] = red[0] + red[1] + red[2] + red[3];
     }
   }
   __syncthreads();
@@ -610,9 +655,45 @@ __global__ void tc_reduce_kernel(const float* part, const double* part_ll, int n
     for (int c = 0; c < ncl; ++c) s += part[((int64_t)c * Kp + k) * F + f];
     stats[i] += s;
   }
-  if (i == 0) {
+  if (i == 0 && ll != nullptr) {
     double s = 0.0;
     for (int c = 0; c < ncl; ++c) s += part_ll[c];
+    *ll += s;
+  }
+}
+
+// Grouped large-K path: each row's log-sum-exp over all groups (log2 units)
+// from the per-group (max, scaled sum), and one fixed-order log-likelihood
+// partial per block.
+__global__ void tc_lse_combine_kernel(const float2* rowstat, int groups, int64_t N, float* lse, double* ll_part) {
+  double acc = 0.0;
+  for (int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; n < N; n += (int64_t)gridDim.x * blockDim.x) {
+    float M = -INFINITY;
+    for (int g = 0; g < groups; ++g) M = fmaxf(M, rowstat[(int64_t)g * N + n].x);
+    float S = 0.f;
+    for (int g = 0; g < groups; ++g) {
+      const float2 e = rowstat[(int64_t)g * N + n];
+      S += e.y * exp2f(e.x - M);
+    }
+    const float l2 = M + log2f(S);
+    lse[n] = l2;
+    acc += (double)l2 * (double)kLn2;
+  }
+  __shared__ double red[32];
+  acc = warp_sum_d(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+    ll_part[blockIdx.x] = s;
+  }
+}
+
+__global__ void tc_ll_sum_kernel(const double* ll_part, int n, double* ll) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    double s = 0.0;
+    for (int i = 0; i < n; ++i) s += ll_part[i];
     *ll += s;
   }
 }
@@ -640,7 +721,7 @@ EncodeTiledFn encode_fn() {
 }
 
 int launch_tc_pack(int cov, int db, const TcLaunch& L, cudaStream_t st) {
-  const unsigned grid = (unsigned)(L.cluster_size * kKC);
+  const unsigned grid = (unsigned)(L.nchunks * kKC);
   if (cov == GMMXX_DIAG && db == 1)
     tc_pack_kernel<GMMXX_DIAG, 1><<<grid, 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
   else if (cov == GMMXX_SPHERICAL && db == 1)
@@ -702,22 +783,25 @@ int clustered_launch(const void* kern, int threads, int smem, const TcLaunch& L,
   return GMMXX_OK;
 }
 
-template <int COV, int DB>
-static int launch_t(const TcLaunch& L, cudaStream_t st) {
+// One clustered launch of em_tc_kernel over chunks [chunk0, chunk0 + csize).
+template <int COV, int DB, int MODE>
+static int launch_mode(const TcLaunch& L, int chunk0, int csize, const float* lse_in, float2* rowstat, int* ncl_out,
+                       cudaStream_t st) {
   using C = Cfg<COV, DB>;
   // the dynamic block is the kernel's only shared memory: <= 227 KB per CTA
   static_assert(C::total(C::kMaxCluster) <= 232448, "shared memory budget");
-  if (int rc = launch_tc_pack(COV, DB, L, st)) return rc;
   CUtensorMap tmap;
   if (int rc = make_x_tensor_map(L, &tmap)) return rc;
-  auto kern = em_tc_kernel<COV, DB>;
-  const int smem = C::total(L.cluster_size);
+  auto kern = em_tc_kernel<COV, DB, MODE>;
+  const int smem = C::total(csize);
+  TcLaunch Lc = L;
+  Lc.cluster_size = csize;
   int ncl = 0;
-  if (int rc = clustered_launch((const void*)kern, kThreads, smem, L, &ncl)) return rc;
+  if (int rc = clustered_launch((const void*)kern, kThreads, smem, Lc, &ncl)) return rc;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = L.cluster_size;
+  attr[0].val.clusterDim.x = csize;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(kThreads);
@@ -725,25 +809,77 @@ static int launch_t(const TcLaunch& L, cudaStream_t st) {
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3((unsigned)(ncl * L.cluster_size));
+  cfg.gridDim = dim3((unsigned)(ncl * csize));
   TcArgs args{};
   args.N = L.N;
-  args.Kp = L.Kp_part;
+  args.Kp = (int64_t)csize * kKC;
   args.F = L.F;
-  args.cluster_size = L.cluster_size;
+  args.cluster_size = csize;
   args.params = L.params;
   args.consts = L.consts;
   args.part = L.part;
   args.part_ll = L.part_ll;
   args.status = L.status;
+  args.chunk0 = chunk0;
+  args.lse_in = lse_in;
+  args.rowstat = rowstat;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_kernel launch: %s", cudaGetErrorString(e));
-  // deterministic reduction into the caller's statistics
+  *ncl_out = ncl;
+  return GMMXX_OK;
+}
+
+// K <= 1024: one launch over the whole of K, then the fixed-order reduction.
+template <int COV, int DB>
+static int launch_t(const TcLaunch& L, cudaStream_t st) {
+  if (int rc = launch_tc_pack(COV, DB, L, st)) return rc;
+  int ncl = 0;
+  if (int rc = launch_mode<COV, DB, kModeFull>(L, 0, L.cluster_size, nullptr, nullptr, &ncl, st)) return rc;
   return launch_tc_reduce(L, ncl, st);
+}
+
+// Spherical K > 1024: groups of 8 chunks (1024 components).  Pass 1 writes
+// each row's (max, sum) per group; the combine folds them into the row's
+// log-sum-exp and the log-likelihood; pass 2 forms the responsibilities of
+// each group's components from it and accumulates their statistics.
+template <int DB>
+static int launch_grouped(const TcLaunch& L, cudaStream_t st) {
+  if (int rc = launch_tc_pack(GMMXX_SPHERICAL, DB, L, st)) return rc;
+  const int groups = (L.nchunks + kMaxClusterSph - 1) / kMaxClusterSph;
+  int ncl = 0;
+  for (int g = 0; g < groups; ++g) {
+    const int csize = std::min(kMaxClusterSph, L.nchunks - g * kMaxClusterSph);
+    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(L, g * kMaxClusterSph, csize, nullptr,
+                                                                 L.rowstat + (int64_t)g * L.N, &ncl, st))
+      return rc;
+  }
+  const int nb = std::min<int>(kMaxClusters, 148);
+  tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.lse, L.part_ll);
+  if (int rc = check_launch("tc_lse_combine_kernel")) return rc;
+  tc_ll_sum_kernel<<<1, 32, 0, st>>>(L.part_ll, nb, L.ll);
+  if (int rc = check_launch("tc_ll_sum_kernel")) return rc;
+  for (int g = 0; g < groups; ++g) {
+    const int csize = std::min(kMaxClusterSph, L.nchunks - g * kMaxClusterSph);
+    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeExtLse>(L, g * kMaxClusterSph, csize, L.lse, nullptr, &ncl, st))
+      return rc;
+    TcLaunch Lg = L;  // statistics rows of this group's components
+    const int k0 = g * kMaxClusterSph * kKC;
+    Lg.stats = L.stats + (int64_t)k0 * L.F;
+    Lg.K = std::min(kMaxClusterSph * kKC, L.K - k0);
+    Lg.Kp_part = (int64_t)csize * kKC;
+    Lg.ll = nullptr;
+    if (int rc = launch_tc_reduce(Lg, ncl, st)) return rc;
+  }
+  return GMMXX_OK;
 }
 
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st) {
   if (cov == GMMXX_DIAG && L.D == 64 && L.cluster_size <= kMaxClusterDiag) return launch_em_tc_diag(L, st);
+  if (cov == GMMXX_SPHERICAL && L.nchunks > kMaxClusterSph) {
+    if (L.rowstat == nullptr || L.lse == nullptr) return set_error(GMMXX_ERR_WORKSPACE, "grouped pass buffers missing");
+    if (L.D == 64) return launch_grouped<1>(L, st);
+    if (L.D == 128) return launch_grouped<2>(L, st);
+  }
   if (cov == GMMXX_SPHERICAL && L.D == 64) return launch_t<GMMXX_SPHERICAL, 1>(L, st);
   if (cov == GMMXX_SPHERICAL && L.D == 128) return launch_t<GMMXX_SPHERICAL, 2>(L, st);
   return set_error(GMMXX_ERR_UNSUPPORTED, "no tensor-core kernel for this shape");

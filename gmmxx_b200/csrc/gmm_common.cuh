@@ -69,11 +69,19 @@ __host__ __device__ inline int stat_width(int cov, int D) {
 // diag D == 64 with K <= 512, spherical D in {64, 128} with K <= 1024.
 constexpr int kTcMaxClusters = 160;
 constexpr int kMaxClusterDiag = 4;
+constexpr int kMaxClusterSph = 8;      // spherical: up to 8 CTAs (1024 components) per cluster
+constexpr int kMaxComponentsSph = 16384;  // larger K runs as groups of 1024 components
 __host__ __device__ inline bool tc_eligible(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   if (B != 1 || N < 65536) return false;
   if (cov == GMMXX_DIAG) return D == 64 && K <= 128 * kMaxClusterDiag;
-  if (cov == GMMXX_SPHERICAL) return (D == 64 || D == 128) && K <= 1024;
+  if (cov == GMMXX_SPHERICAL) return (D == 64 || D == 128) && K <= kMaxComponentsSph;
   return false;
+}
+// 128-component groups of one tensor-core launch: all of K up to 8 chunks,
+// else groups of 8 chunks (spherical large K)
+__host__ __device__ inline int tc_groups(int64_t K) {
+  const int nch = (int)((K + 127) / 128);
+  return (nch + kMaxClusterSph - 1) / kMaxClusterSph;
 }
 // three bf16 terms per weight: a_j (and v_j for diag)
 __host__ __device__ inline int tc_param_blocks(int cov, int D) { return (cov == GMMXX_DIAG ? 6 : 3) * (D / 64); }
@@ -120,7 +128,10 @@ struct Layout {
   int64_t tc_consts;  // float[C][3][128]
   int64_t tc_part;    // float[kTcMaxClusters][C*128][F]
   int64_t tc_part_ll; // double[kTcMaxClusters]
+  int64_t tc_rowstat; // float2[groups][N] per-row partials of the grouped large-K path
+  int64_t tc_lse;     // float[N]          per-row log-sum-exp (log2 units), grouped path
   int tc_cluster;     // C (0: tensor-core path not available)
+  int tc_chunks;      // 128-component chunks of K
   int64_t total;
   int64_t Kp;
   int FE;
@@ -143,15 +154,22 @@ inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   L.llpart = off; off += al(B * ((N + 63) / 64) * 8);
   L.xxpart = off;
   if (cov == GMMXX_TIED) off += al(B * xx_blocks(B, N) * D * D * 4);
-  L.tc_cluster = 0;
-  L.tc_params = L.tc_consts = L.tc_part = L.tc_part_ll = 0;
+  L.tc_cluster = L.tc_chunks = 0;
+  L.tc_params = L.tc_consts = L.tc_part = L.tc_part_ll = L.tc_rowstat = L.tc_lse = 0;
   if (tc_eligible(cov, B, N, D, K)) {
-    const int C = (int)((K + 127) / 128);
+    const int nch = (int)((K + 127) / 128);
+    const int G = tc_groups(K);
+    const int C = G > 1 ? kMaxClusterSph : nch;
     L.tc_cluster = C;
-    L.tc_params = off; off += al((int64_t)C * tc_param_blocks(cov, (int)D) * 16384);
-    L.tc_consts = off; off += al((int64_t)C * 3 * 128 * 4);
+    L.tc_chunks = nch;
+    L.tc_params = off; off += al((int64_t)nch * tc_param_blocks(cov, (int)D) * 16384);
+    L.tc_consts = off; off += al((int64_t)nch * 3 * 128 * 4);
     L.tc_part = off; off += al((int64_t)kTcMaxClusters * C * 128 * stat_width(cov, (int)D) * 4);
     L.tc_part_ll = off; off += al((int64_t)kTcMaxClusters * 8);
+    if (G > 1) {
+      L.tc_rowstat = off; off += al((int64_t)G * N * 8);
+      L.tc_lse = off; off += al(N * 4);
+    }
   }
   L.total = off;
   return L;

@@ -22,6 +22,11 @@ struct TcArgs {
   float* part;       // [kMaxClusters][Kp][F]
   double* part_ll;   // [kMaxClusters]
   int* status;       // sticky workspace status word
+  // grouped large-K passes (spherical, K > 1024): the cluster covers chunks
+  // [chunk0, chunk0 + cluster_size) of 128 components
+  int chunk0;
+  const float* lse_in;  // external per-row log-sum-exp over all K (log2 units)
+  float2* rowstat;      // per-row (max, scaled sum) over this group (log2 units)
 };
 
 struct TcLaunch {
@@ -32,6 +37,7 @@ struct TcLaunch {
   int64_t Kp_part;
   int F;
   int cluster_size;
+  int nchunks;       // 128-component chunks of the weight images (>= cluster_size)
   const float* wt;
   const CompConst* cc;
   char* params;
@@ -41,6 +47,8 @@ struct TcLaunch {
   int* status;
   float* stats;
   double* ll;
+  float2* rowstat;   // [groups][N] (grouped large-K path)
+  float* lse;        // [N]         (grouped large-K path)
 };
 
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st);
