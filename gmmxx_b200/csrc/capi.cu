@@ -228,8 +228,11 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
   a.lse_out = reinterpret_cast<float*>(ws + L.lse);
   a.ll_part = reinterpret_cast<double*>(ws + L.llpart);
   a.ll = log_likelihood;
+  if (cov_type == GMMXX_TIED) a.q_out = reinterpret_cast<float*>(ws + L.qrow);
   if (int rc = launch_rows(cov_type, MODE_LSE, a, (int)B, st)) return rc;
   a.lse_in = a.lse_out;
+  a.q_in = a.q_out;  // the M-step reads x^T P x instead of recomputing it per component tile
+  a.q_out = nullptr;
   a.stats = stats;
   a.part = reinterpret_cast<float*>(ws + L.mpart);
   if (int rc = launch_mstep(cov_type, a, (int)B, st)) return rc;

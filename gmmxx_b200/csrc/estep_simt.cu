@@ -109,19 +109,56 @@ __device__ __forceinline__ void load_rows(const RowArgs& a, const Smem& s, int b
       s.q[threadIdx.x] = acc;
     }
   } else if (COV == GMMXX_TIED) {
-    // x^T P x (torch_fallback.py:452): 4 threads per row
-    const int r = threadIdx.x >> 2, part = threadIdx.x & 3;
-    const float* xr = s.xs + r * xst;
-    float acc = 0.f;
-    for (int d = part; d < D; d += 4) {
-      const float* pr = s.prec + d * D;
-      float t = 0.f;
-      for (int e = 0; e < D; ++e) t = fmaf(pr[e], xr[e], t);
-      acc = fmaf(xr[d], t, acc);
+    if (a.q_in != nullptr) {  // computed by the LSE pass of this iteration
+      if (threadIdx.x < kBN) {
+        const int64_t row = row0 + threadIdx.x;
+        s.q[threadIdx.x] = row < a.N ? a.q_in[(int64_t)b * a.N + row] : 0.f;
+      }
+    } else {
+      // x^T P x (torch_fallback.py:452) as Y = X P on 4x4 register tiles
+      // (thread: rows 4 ty.., columns 4 tx.. of each 64-column block), then
+      // q = sum_j Y_j x_j reduced over the 16 threads of a row group
+      const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+      float qp[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c0 = 0; c0 < D; c0 += 64) {
+        const int col = c0 + tx * 4;
+        float y[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) y[i][j] = 0.f;
+        if (col < D) {
+          for (int d = 0; d < D; ++d) {
+            float xv[4], pv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = s.xs[(ty * 4 + i) * xst + d];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) pv[j] = (col + j < D) ? s.prec[d * D + col + j] : 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) y[i][j] = fmaf(xv[i], pv[j], y[i][j]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (col + j < D) qp[i] = fmaf(y[i][j], s.xs[(ty * 4 + i) * xst + col + j], qp[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) qp[i] += __shfl_xor_sync(0xffffffffu, qp[i], o);
+      if (tx == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          s.q[ty * 4 + i] = qp[i];
+          const int64_t row = row0 + ty * 4 + i;
+          if (a.q_out != nullptr && row < a.N) a.q_out[(int64_t)b * a.N + row] = qp[i];
+        }
+      }
     }
-    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-    if (part == 0) s.q[r] = acc;
   } else {
     if (threadIdx.x < kBN) s.q[threadIdx.x] = 0.f;
   }

@@ -120,6 +120,7 @@ struct Layout {
   int64_t wt;       // float[B][FE][Kp]  (feature-major component weights)
   int64_t prec;     // float[B][D][D] (tied) or float[B][K][D][D] (full)
   int64_t lse;      // float[B][max(N, K)] (per-row lse; per-matrix log det while preparing)
+  int64_t qrow;     // float[B][N] x^T P x per row (tied)
   int64_t mpart;    // float[B][mstep_blocks][Kp][F]  CUDA-core M-step partials
   int64_t llpart;   // double[B][ceil(N/64)]          per-CTA log-likelihood partials
   int64_t xxpart;   // float[B][xx_blocks][D][D]      X^T X partials (tied)
@@ -150,6 +151,8 @@ inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   if (cov == GMMXX_TIED) off += al(B * D * D * 4);
   else if (cov == GMMXX_FULL) off += al(B * K * D * D * 4);
   L.lse = off; off += al(B * (N > K ? N : K) * 4);
+  L.qrow = off;
+  if (cov == GMMXX_TIED) off += al(B * N * 4);
   L.mpart = off; off += al(B * mstep_blocks(B, N, L.Kp) * L.Kp * stat_width(cov, (int)D) * 4);
   L.llpart = off; off += al(B * ((N + 63) / 64) * 8);
   L.xxpart = off;

@@ -26,6 +26,10 @@ struct RowArgs {
   int FM;
   int64_t rows_per_cta;
   int64_t part_blocks;
+  // tied: x^T P x per row, written by the LSE pass and read by the M-step
+  // instead of being recomputed for every component tile (may be null)
+  float* q_out;         // [B][N]
+  const float* q_in;    // [B][N]
 };
 
 enum { MODE_LSE = 0, MODE_ARGMAX = 1, MODE_RESP = 2 };
