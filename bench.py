@@ -53,6 +53,20 @@ def algorithmic_flops(cov: str, n: int, d: int, k: int) -> float:
     return 2.0 * n * k * (d + q) + 2.0 * n * k * (1 + d + q)
 
 
+def launches_per_iteration(cfg, tc_path: bool) -> int:
+    """Kernels of this library launched per EM iteration: prep_weights +
+    prep_table (+ 2 Cholesky kernels for tied / full), the statistics kernels,
+    finalize.  Statistics: 3 (pack, tensor-core kernel, reduce; or rows, mstep,
+    reduce), and for spherical K > 1024 the grouped passes: pack, G row-partial
+    launches, combine, log-likelihood sum, G x (M-step launch + reduce)."""
+    prep = 2 + (2 if cfg.cov_type in ("tied", "full") else 0)
+    stats = 3
+    if tc_path and cfg.cov_type == "spherical" and cfg.K > 1024:
+        groups = (((cfg.K + 127) // 128) + 7) // 8
+        stats = 3 + 3 * groups
+    return prep + stats + 1
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -353,9 +367,7 @@ def main():
                          "hbm_frac": (n_local * cfg.B * D * torch.empty((), dtype=cfg.dtype).element_size()) /
                                      (acc_ms / 1e3) / 1e9 / peaks["hbm_gbs"]},
             "clocks": clocks,
-            # per iteration: prep_weights + prep_table (+ 2 Cholesky kernels for tied / full),
-            # three statistics kernels, finalize
-            "gpu_launches": args.steps * (6 + (2 if cfg.cov_type in ("tied", "full") else 0)),
+            "gpu_launches": args.steps * launches_per_iteration(cfg, tc_path),
             "e2e": e2e,
         }
         if world == 1 and not args.no_cpu:

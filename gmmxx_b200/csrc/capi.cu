@@ -221,6 +221,11 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
     t.status = reinterpret_cast<int*>(ws + L.status);
     t.stats = stats;
     t.ll = log_likelihood;
+    {  // test hook: GMMXX_B200_TEST_STALL=1 makes the tensor-core kernel's bounded waits run out (100 ms)
+      const char* e = getenv("GMMXX_B200_TEST_STALL");
+      t.test_stall = (e != nullptr && strcmp(e, "1") == 0) ? 1 : 0;
+      t.wait_ns = t.test_stall ? 100000000ull : 2000000000ull;
+    }
     const int rc = tc::launch_em_tc(cov_type, t, st);
     if (rc != GMMXX_ERR_UNSUPPORTED || mode == 2) return rc;  // else: no co-resident cluster -> CUDA-core kernels
   }

@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* c_c2 = c_mpm + 256;
   float2* xch = reinterpret_cast<float2*>(sm + kXch);
   volatile int* abort = &bars->abort;
+  const uint64_t lim = a.wait_ns;  // every wait below gives up after this long
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // M-step stage of tile u: wait until the M-step of u-1 released it, then
     // [x | s_hi | s_lo] (same swizzled layout as the staging slot)
     auto fill_mstage = [&](int u) -> bool {
-      if (u >= 1 && !mbar_wait_warp(&bars->mfree, (u - 1) & 1, abort)) return false;
+      if (u >= 1 && !mbar_wait_warp(&bars->mfree, (u - 1) & 1, abort, lim)) return false;
       uint32_t w[32];
       load_row(u & 1, w);
 #pragma unroll
@@ -219,11 +220,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int t = 0; t < T; ++t) {
       const int s = t & 1;
-      if (!mbar_wait_warp(&bars->xfull[s], (t >> 1) & 1, abort)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars->xfull[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
       uint32_t w[32];
       load_row(s, w);
       // the E-step of t-1 read the operand region: wait for its completion
-      if (t >= 1 && !mbar_wait_warp(&bars->sfull[(t - 1) & 1], ((t - 1) >> 1) & 1, abort)) { ok = false; break; }
+      if (t >= 1 && !mbar_wait_warp(&bars->sfull[(t - 1) & 1], ((t - 1) >> 1) & 1, abort, lim)) { ok = false; break; }
       tmem_fence_after();
       tmem_st32(tmem + lane_addr + kFCol, w);
 #pragma unroll
@@ -255,7 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       for (int t = 0; t < T; ++t) {
         const int s = t & 1;
-        if (t >= 2 && !mbar_wait(&bars->sempty[s], ((t >> 1) - 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        if (t >= 2 && !mbar_wait(&bars->sempty[s], ((t >> 1) - 1) & 1, abort, lim)) { set_abort(bars, a.status); break; }
+        if (a.test_stall) break;  // test hook: no X tile ever lands, every wait on it runs out
         const int row0 = (int)((cid + (int64_t)t * ncl) * kBM);
         mbar_expect_tx(&bars->xfull[s], kBlock);
         tma_load_2d(sm + kStaging + s * kBlock, &tmap, 0, row0, &bars->xfull[s]);
@@ -263,9 +265,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // before the CTA can exit, every copy it started has landed (bounded,
       // also after an abort): the weights and the last load of each slot
-      mbar_wait(&bars->params, 0, nullptr, 1000000000ull);
+      mbar_wait(&bars->params, 0, nullptr, lim);
       for (int t = std::max(0, issued - 2); t < issued; ++t)
-        mbar_wait(&bars->xfull[t & 1], (t >> 1) & 1, nullptr, 1000000000ull);
+        mbar_wait(&bars->xfull[t & 1], (t >> 1) & 1, nullptr, lim);
     }
   } else if (warp == kWarpMma) {
     // ---------------- MMA issuer (one thread) ----------------
@@ -275,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_m = idesc_bf16(128, 64, 1, 1);    // R_hi^T x s_lo
       const uint32_t id_aux = idesc_bf16(128, 16, 1, 0);  // R^T x 1
       const uint32_t base = smem_u32(sm);
-      bool ok = mbar_wait(&bars->params, 0, abort);
+      bool ok = mbar_wait(&bars->params, 0, abort, lim);
       tmem_fence_after();
       // weight descriptors: K-major blocks, +32 B per 16-feature step
       uint64_t wa[kNS], wv[kNS];
@@ -287,8 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // E-step of tile t into S[t & 1]: x.a_j, s_hi.v_j (j < 3), s_lo.v_j (j < 2)
       auto issue_e = [&](int t) -> bool {
         const int s = t & 1;
-        if (!mbar_wait(&bars->ffull, t & 1, abort)) return false;
-        if (t >= 2 && !mbar_wait(&bars->sfree[s], ((t >> 1) - 1) & 1, abort)) return false;
+        if (!mbar_wait(&bars->ffull, t & 1, abort, lim)) return false;
+        if (t >= 2 && !mbar_wait(&bars->sfree[s], ((t >> 1) - 1) & 1, abort, lim)) return false;
         tmem_fence_after();
         const uint32_t d = tmem + (uint32_t)(s * kKC);
         uint32_t acc = 0;
@@ -318,8 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_m = [&](int t, auto part_tag) -> bool {
         constexpr int part = decltype(part_tag)::value;
         const int use = 2 * t + part;
-        if (!mbar_wait(&bars->rfull, use & 1, abort)) return false;
-        if (part == 0 && !mbar_wait(&bars->mfull, t & 1, abort)) return false;
+        if (!mbar_wait(&bars->rfull, use & 1, abort, lim)) return false;
+        if (part == 0 && !mbar_wait(&bars->mfull, t & 1, abort, lim)) return false;
         tmem_fence_after();
         const uint32_t acc0 = (t == 0 && part == 0) ? 0u : 1u;
 #pragma unroll
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = t & 1;
       const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
       const bool valid = grow < a.N;
-      if (!mbar_wait_warp(&bars->sfull[s], (t >> 1) & 1, abort)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars->sfull[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
       tmem_fence_after();
       const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC + k0);
       tmem_ld32(sc, p);
@@ -407,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // residual part of the previous tile (the M-step's high part of t-1 ran meanwhile)
       if (t >= 1) {
-        if (!mbar_wait_warp(&bars->rfree, 0u, abort)) { ok = false; break; }  // M_hi(t-1)
+        if (!mbar_wait_warp(&bars->rfree, 0u, abort, lim)) { ok = false; break; }  // M_hi(t-1)
         store_r(lo);
       }
       const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       halfx[hf * 128 + row] = make_float2(m, sum);
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->hx[s]);
-      if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
       const float2 o = halfx[(hf ^ 1) * 128 + row];
       const float mc = fmaxf(m, o.x);
       // exponents <= 0 here; ex2.approx (relative error ~2^-22) flushes results
@@ -440,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (q < nclus)
             st_async_f2(map_shared(xch_mine + s * slot_stride, q), mc, sc2, map_shared(smem_u32(&bars->xch[s]), q));
       }
-      if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
       float2 e[kMaxCluster];
 #pragma unroll
       for (int q = 0; q < kMaxCluster; ++q)
@@ -455,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float f = valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f;
       // high part of tile t now (after the M-step's residual part of t-1);
       // the residual words stay in registers for the next iteration
-      if (t >= 1 && !mbar_wait_warp(&bars->rfree, 1u, abort)) { ok = false; break; }  // M_lo(t-1)
+      if (t >= 1 && !mbar_wait_warp(&bars->rfree, 1u, abort, lim)) { ok = false; break; }  // M_lo(t-1)
 #pragma unroll
       for (int c = 0; c < 8; ++c) {  // 8 components per 16-byte store
         uint32_t hw[4];
@@ -476,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // the residual part of the last tile
     if (ok && T >= 1) {
-      if (mbar_wait_warp(&bars->rfree, 0u, abort)) store_r(lo);
+      if (mbar_wait_warp(&bars->rfree, 0u, abort, lim)) store_r(lo);
       else ok = false;
     }
     if (!ok) set_abort(bars, a.status);
@@ -484,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the MMA thread always commits `mdone` (also after an abort): wait for it
     // without the abort shortcut before touching tensor memory again
     if (hf == 0) {
-      if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 4000000000ull)) set_abort(bars, a.status);
+      if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 2 * lim)) set_abort(bars, a.status);
       tmem_fence_after();
       const int comp = (int)rank * kKC + row;  // this thread's TMEM lane = component
       float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
@@ -549,6 +551,8 @@ int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st) {
   args.part = L.part;
   args.part_ll = L.part_ll;
   args.status = L.status;
+  args.wait_ns = L.wait_ns ? L.wait_ns : 2000000000ull;
+  args.test_stall = L.test_stall;
   cudaError_t e = cudaLaunchKernelEx(&cfg, em_tc_diag_kernel, tmap, args);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_diag_kernel launch: %s", cudaGetErrorString(e));
   return launch_tc_reduce(L, ncl, st);

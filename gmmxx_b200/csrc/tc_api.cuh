@@ -27,6 +27,8 @@ struct TcArgs {
   int chunk0;
   const float* lse_in;  // external per-row log-sum-exp over all K (log2 units)
   float2* rowstat;      // per-row (max, scaled sum) over this group (log2 units)
+  uint64_t wait_ns;     // limit of every bounded wait (diag kernel)
+  int test_stall;       // test hook (diag kernel): the producer issues no X loads
 };
 
 struct TcLaunch {
@@ -49,6 +51,8 @@ struct TcLaunch {
   double* ll;
   float2* rowstat;   // [groups][N] (grouped large-K path)
   float* lse;        // [N]         (grouped large-K path)
+  uint64_t wait_ns;  // bounded-wait limit (0: 2 s)
+  int test_stall;    // GMMXX_B200_TEST_STALL=1: make the diag kernel's waits run out
 };
 
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st);
