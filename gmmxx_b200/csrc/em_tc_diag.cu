@@ -12,7 +12,8 @@
 //             single M-step stage in shared memory
 //   MMA       E-step S(t)[rows, comps] = [x | s_hi | s_lo] . W^T with the
 //             A operand read from tensor memory (32 instructions, N = 128)
-//   softmax   (8 warps) logits, row max / exp / sum, (max, sum) exchanged with
+//   softmax   (16 warps, four threads per row) logits, row max / exp / sum,
+//             (max, sum) combined across the row's four threads, exchanged with
 //             the cluster through DSMEM, r = exp(l - lse) split r_hi + r_lo
 //   MMA       M-step stats[comps, x | x^2 | 1] += R^T . [x | s_hi] (+ s_lo, 1)
 //
@@ -47,10 +48,11 @@ using namespace ptx;
 constexpr int kBM = 128;        // rows per tile
 constexpr int kKC = 128;        // components per CTA
 constexpr int kNS = 3;          // bf16 terms of the split weights
-constexpr int kHalf = kKC / 2;  // components per softmax thread
+constexpr int kSplit = 4;                // softmax threads per row
+constexpr int kPart = kKC / kSplit;      // components per softmax thread
+constexpr int kSoftWarps = 4 * kSplit;   // every TMEM lane quarter kSplit times
 constexpr int kBlock = 16384;   // one [128][64] bf16 swizzled block
 constexpr int kAuxBytes = 4096; // [16][128] K-major ones operand (n_k)
-constexpr int kThreads = 512;   // 16 warps: 4 prep | TMA, MMA, 2 idle | 8 softmax (128 registers each)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kDmCol = 256;  // M-step statistics [x (64) | x^2 (64) | 1 (16)]
 constexpr uint32_t kFCol = 400;   // E-step operand [x | s_hi | s_lo], 32 columns each
@@ -60,7 +62,8 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (diag: s = 1)
 constexpr int kMaxCluster = kMaxClusterDiag;
 
-enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpIdle0 = 6, kWarpSoftmax0 = 8 };
+enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpSoftmax0 = 6 };
+constexpr int kThreads = (kWarpSoftmax0 + kSoftWarps) * 32;  // 22 warps, <= 88 registers each
 
 // shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
 constexpr int kParams = 0;                     // a_0 a_1 a_2 | v_0 v_1 v_2 (16 KB each)
@@ -71,8 +74,8 @@ constexpr int kMSL = kMSH + kBlock;
 constexpr int kAux = kMSL + kBlock;            // ones operand (constant)
 constexpr int kR = kAux + kAuxBytes;           // R: two 64-component MN groups
 constexpr int kConsts = kR + 2 * kBlock;       // mpm[128], h[128], c2[128]
-constexpr int kHalfX = kConsts + 3 * 128 * 4;  // [2 halves][128 rows] float2
-constexpr int kXch = kHalfX + 2 * 128 * 8;     // [2 slots][C][128 rows] float2
+constexpr int kHalfX = kConsts + 3 * 128 * 4;  // [kSplit parts][128 rows] float2
+constexpr int kXch = kHalfX + kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
 __host__ __device__ constexpr int bars_off(int c) { return kXch + 2 * c * 128 * 8; }
 __host__ __device__ constexpr int red_off(int c) { return bars_off(c) + 192; }
 __host__ __device__ constexpr int smem_total(int c) { return bars_off(c) + 256; }
@@ -93,11 +96,11 @@ struct Bars {
   uint64_t mfull;      // prep: M-step stage holds tile t (4 warps)
   uint64_t mfree;      // MMA: M-step of tile t done reading the stage
   uint64_t sfull[2];   // MMA: S(t) complete (the E-step operand is free again)
-  uint64_t sfree[2];   // softmax: S(t) loaded (8 warps)
-  uint64_t rfull;      // softmax: an R part written (8 warps)
+  uint64_t sfree[2];   // softmax: S(t) loaded (16 warps)
+  uint64_t rfull;      // softmax: an R part written (16 warps)
   uint64_t rfree;      // MMA: that R part consumed
   uint64_t xch[2];     // cluster exchange of (row max, row sum)
-  uint64_t hx[2];      // both component halves of the row wrote (max, sum) (8 warps)
+  uint64_t hx[2];      // every part of the row wrote its (max, sum) (16 warps)
   uint64_t mdone;      // MMA: all MMAs complete
   uint32_t tmem_base;
   int abort;
@@ -128,8 +131,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int nclus = a.cluster_size;
   Bars* bars = reinterpret_cast<Bars*>(sm + bars_off(nclus));
-  float* c_mpm = reinterpret_cast<float*>(sm + kConsts);
-  float* c_c2 = c_mpm + 256;
+  float* c_lz = reinterpret_cast<float*>(sm + kConsts);  // c2 - h mpm: the logit at S = 0
+  float* c_c2 = c_lz + 256;
   float2* xch = reinterpret_cast<float2*>(sm + kXch);
   volatile int* abort = &bars->abort;
   const uint64_t lim = a.wait_ns;  // every wait below gives up after this long
@@ -147,21 +150,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->xfull[i], 1);
       mbar_init(&bars->sempty[i], 4);
       mbar_init(&bars->sfull[i], 1);
-      mbar_init(&bars->sfree[i], 8);
+      mbar_init(&bars->sfree[i], kSoftWarps);
       mbar_init(&bars->xch[i], 1);
-      mbar_init(&bars->hx[i], 8);
+      mbar_init(&bars->hx[i], kSoftWarps);
     }
     mbar_init(&bars->ffull, 4);
     mbar_init(&bars->mfull, 4);
     mbar_init(&bars->mfree, 1);
-    mbar_init(&bars->rfull, 8);
+    mbar_init(&bars->rfull, kSoftWarps);
     mbar_init(&bars->rfree, 1);
     mbar_init(&bars->mdone, 1);
     bars->abort = 0;
     fence_barrier_init();
   }
   if (warp == kWarpMma) tmem_alloc(&bars->tmem_base, kTmemCols);
-  for (int i = tid; i < 3 * 128; i += kThreads) c_mpm[i] = a.consts[(int64_t)rank * 3 * 128 + i];
+  // logit = c2 - h max(S + mpm, 0) = min(lz - h S, c2) with lz = c2 - h mpm
+  // (h > 0); a padding component has c2 = -inf, so lz = -inf too
+  for (int i = tid; i < 128; i += kThreads) {
+    const float* cs = a.consts + (int64_t)rank * 3 * 128;
+    c_lz[i] = fmaf(-kHalfLog2e, cs[i], cs[256 + i]);
+    c_c2[i] = cs[256 + i];
+  }
   {  // ones operand of the n_k statistic: K-major [16][128], row 0 = 1
     char* aux = sm + kAux;
     for (int i = tid; i < 16 * 128; i += kThreads) {
@@ -339,41 +348,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       using Hi = std::integral_constant<int, 0>;
       using Lo = std::integral_constant<int, 1>;
-      // Issue order: E(0), E(1), then per tile M_hi(t), E(t+2), M_lo(t).  E(t+2)
-      // needs only the operand of t+2 (prep, after E(t+1)) and S slot t & 1
-      // (loaded by the softmax at the start of tile t); M_lo(t) waits for the
-      // residual R(t), written by the softmax after the logits of t+1.  So the
-      // E-steps run about two tiles ahead and never queue behind a residual part.
+      // Issue order: E(0), E(1), then per tile M_hi(t), M_lo(t), E(t+2).
+      // M_lo(t) waits for the residual R(t), written by the softmax after the
+      // logits of t+1 (whose S(t+1) is already queued); E(t+2) then still ends
+      // well before the softmax finishes tile t+1.  Keeping M_lo(t) ahead of
+      // E(t+2) matters: its completion frees the single M-step stage, the
+      // stage refill frees the staging slot, and that slot receives X(t+2) --
+      // with E(t+2) first, that chain closed a cycle through the tensor pipe,
+      // the prep warps and a TMA round trip once per tile.
       if (ok && T > 0) ok = issue_e(0);
       if (ok && T > 1) ok = issue_e(1);
       for (int t = 0; ok && t < T; ++t) {
         if (!issue_m(t, Hi{})) { ok = false; break; }
-        if (t + 2 < T && !issue_e(t + 2)) { ok = false; break; }
         if (!issue_m(t, Lo{})) { ok = false; break; }
+        if (t + 2 < T && !issue_e(t + 2)) { ok = false; break; }
       }
       if (!ok) set_abort(bars, a.status);
       mma_commit(&bars->mdone);
     }
   } else if (warp >= kWarpSoftmax0) {
-    // ---------------- softmax: 8 warps, two per TMEM lane quarter ----------------
+    // ---------------- softmax: 16 warps, kSplit per TMEM lane quarter ----------------
+    // warp w reads lanes 32 (w % 4) .. +31 (the tensor-memory access rule);
+    // part qc of the row owns components [qc kPart, qc kPart + kPart)
     const int q4 = warp & 3;
-    const int hf = (warp - kWarpSoftmax0) >> 2;
+    const int qc = (warp - kWarpSoftmax0) >> 2;
     const int row = q4 * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
-    const int k0 = hf * kHalf;
+    const int k0 = qc * kPart;
     double ll_acc = 0.0;
-    float p[kHalf];
-    uint32_t lo[kHalf / 2];  // residual words of the previous tile, written one iteration later
+    float p[kPart];
+    uint32_t lo[kPart / 2];  // residual words of the previous tile, written one iteration later
     float2* halfx = reinterpret_cast<float2*>(sm + kHalfX);
     const uint32_t xch_mine = smem_u32(&xch[(int)rank * 128 + row]);
     const uint32_t slot_stride = (uint32_t)(nclus * 128 * 8);
-    const float4* cm4 = reinterpret_cast<const float4*>(c_mpm + k0);
+    const float4* cz4 = reinterpret_cast<const float4*>(c_lz + k0);
     const float4* cc4 = reinterpret_cast<const float4*>(c_c2 + k0);
-    char* rg = sm + kR + hf * kBlock;  // this half's 64 components are R's MN group hf
+    // R holds two 64-component MN groups; this part's components are 16-byte
+    // chunks rc0 .. rc0 + kPart / 8 - 1 of group k0 / 64
+    char* rg = sm + kR + (k0 / 64) * kBlock;
+    const int rc0 = (k0 % 64) / 8;
     auto store_r = [&](const uint32_t* w) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)(c * 8))) =
+      for (int c = 0; c < kPart / 8; ++c)
+        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)((rc0 + c) * 8))) =
             make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
       fence_proxy_async();
       __syncwarp();
@@ -387,22 +404,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(&bars->sfull[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
       tmem_fence_after();
       const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC + k0);
-      tmem_ld32(sc, p);
-      tmem_ld32(sc + 32, p + 32);
+#pragma unroll
+      for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
       tmem_wait_ld();
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->sfree[s]);
-      // logits (log2 units) c2 - h max(S + mpm, 0), h = log2(e)/2, and this half's max
+      // logits (log2 units) min(lz - h S, c2), h = log2(e)/2, and this part's max
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int k4 = 0; k4 < kHalf / 4; ++k4) {
-        const float4 vm = cm4[k4], vc = cc4[k4];
-        const float mm[4] = {vm.x, vm.y, vm.z, vm.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
+      for (int k4 = 0; k4 < kPart / 4; ++k4) {
+        const float4 vz = cz4[k4], vc = cc4[k4];
+        const float lz[4] = {vz.x, vz.y, vz.z, vz.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int k = 4 * k4 + j;
-          const float l = fmaf(-kHalfLog2e, fmaxf(p[k] + mm[j], 0.f), cc[j]);
+          const float l = fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
           p[k] = l;
           mx[j] = fmaxf(mx[j], l);
         }
@@ -413,29 +430,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         store_r(lo);
       }
       const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      const float mref = (m == -INFINITY) ? 0.f : m;  // an all-padding half has p = 0
+      const float mref = (m == -INFINITY) ? 0.f : m;  // an all-padding part has p = 0
       float sm4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < kHalf; ++k) {
+      for (int k = 0; k < kPart; ++k) {
         p[k] = ex2_approx(p[k] - mref);
         sm4[k & 3] += p[k];
       }
       const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
-      // combine the two halves of the row.  One buffer suffices: a half
-      // rewrites its entry for tile t+1 only after writing R_lo(t), which
-      // waits for M_hi(t), which waited for the other half's R_hi(t) -- and
-      // that half read this entry before writing R_hi(t).
-      halfx[hf * 128 + row] = make_float2(m, sum);
+      // combine the parts of the row.  One buffer suffices: a part rewrites
+      // its entry for tile t+1 only after writing R_lo(t), which waits for
+      // M_hi(t), which waited for every other part's R_hi(t) -- and each part
+      // read this entry before writing R_hi(t).
+      halfx[qc * 128 + row] = make_float2(m, sum);
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->hx[s]);
       if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
-      const float2 o = halfx[(hf ^ 1) * 128 + row];
-      const float mc = fmaxf(m, o.x);
+      float2 o[kSplit];
+#pragma unroll
+      for (int q = 0; q < kSplit; ++q) o[q] = q == qc ? make_float2(m, sum) : halfx[q * 128 + row];
+      float mc = o[0].x;
+#pragma unroll
+      for (int q = 1; q < kSplit; ++q) mc = fmaxf(mc, o[q].x);
       // exponents <= 0 here; ex2.approx (relative error ~2^-22) flushes results
-      // below 2^-126, i.e. halves 2^126 times smaller than the row's largest
-      const float sc2 = sum * ex2_approx(m - mc) + o.y * ex2_approx(o.x - mc);
-      // exchange (max, sum) of this CTA's components with the cluster (half 0 sends)
-      if (hf == 0) {
+      // below 2^-126, i.e. parts 2^126 times smaller than the row's largest.
+      // Every CTA owns at least one live component, so mc is finite.
+      float sc2 = 0.f;
+#pragma unroll
+      for (int q = 0; q < kSplit; ++q) sc2 += o[q].y * ex2_approx(o[q].x - mc);
+      // exchange (max, sum) of this CTA's components with the cluster (part 0 sends)
+      if (qc == 0) {
         if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
 #pragma unroll
         for (int q = 0; q < kMaxCluster; ++q)
@@ -459,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the residual words stay in registers for the next iteration
       if (t >= 1 && !mbar_wait_warp(&bars->rfree, 1u, abort, lim)) { ok = false; break; }  // M_lo(t-1)
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 8 components per 16-byte store
+      for (int c = 0; c < kPart / 8; ++c) {  // 8 components per 16-byte store
         uint32_t hw[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -468,12 +492,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           hw[i] = pack_bf16(r0, r1);
           lo[4 * c + i] = pack_bf16(r0 - bf16lo_to_f32(hw[i]), r1 - bf16hi_to_f32(hw[i]));
         }
-        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)(c * 8))) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)((rc0 + c) * 8))) =
+            make_uint4(hw[0], hw[1], hw[2], hw[3]);
       }
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->rfull);
-      if (valid && rank == 0 && hf == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
+      if (valid && rank == 0 && qc == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
       if (*abort) { ok = false; break; }
     }
     // the residual part of the last tile
@@ -482,25 +507,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       else ok = false;
     }
     if (!ok) set_abort(bars, a.status);
-    // ---------------- epilogue: statistics partials (half-0 warps) ----------------
+    // ---------------- epilogue: statistics partials (all softmax warps) ----------------
     // the MMA thread always commits `mdone` (also after an abort): wait for it
-    // without the abort shortcut before touching tensor memory again
-    if (hf == 0) {
-      if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 2 * lim)) set_abort(bars, a.status);
-      tmem_fence_after();
-      const int comp = (int)rank * kKC + row;  // this thread's TMEM lane = component
+    // without the abort shortcut before touching tensor memory again.  TMEM
+    // lane = component; part qc writes columns 32 qc .. 32 qc + 31 (sums of
+    // r x and r x^2), part 0 also column 128 (n_k).
+    if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 2 * lim)) set_abort(bars, a.status);
+    tmem_fence_after();
+    {
+      static_assert(kSplit * 32 == 128, "epilogue column split");
+      const int comp = (int)rank * kKC + row;
       float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
-      for (int c0 = 0; c0 < kFdm; c0 += 16) {
-        float v[32];
-        tmem_ld32(tmem + lane_addr + kDmCol + c0, v);  // 32 columns; 16 used per step
+      float v[32];
+      tmem_ld32(tmem + lane_addr + kDmCol + 32 * qc, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) out[1 + 32 * qc + j] = v[j];
+      if (qc == 0) {
+        tmem_ld32(tmem + lane_addr + kDmCol + 128, v);  // 32 columns; the first is n_k
         tmem_wait_ld();
-        for (int j = 0; j < 16 && c0 + j < kFdm; ++j) {
-          const int col = c0 + j;
-          if (col < 128) out[1 + col] = v[j];  // sum r x (0..63), sum r x^2 (64..127)
-          else if (col == 128) out[0] = v[j];  // n_k
-        }
+        out[0] = v[0];
       }
-      tmem_fence_before();
+    }
+    tmem_fence_before();
+    if (qc == 0) {
       double* red = reinterpret_cast<double*>(sm + red_off(nclus));
       double v = ll_acc;
 #pragma unroll
