@@ -5,17 +5,20 @@
 // of X at a time; CTA `rank` owns components [128 rank, 128 rank + 128) whose
 // split-bf16 logit weights stay resident in its shared memory.  Per tile t:
 //
-//   TMA       X(t) -> a double-buffered staging slot (bf16, 128-byte swizzle)
+//   TMA       X(t) -> the staging slot (bf16, 128-byte swizzle); once the
+//             M-step of t-1 is done, X(t) again (an L2 hit) -> the M-step stage
 //   prep      (4 warps, thread = row) exact x^2 = s_hi + s_lo; the E-step
-//             operand [x | s_hi | s_lo] goes straight into tensor memory, and,
-//             once the M-step of t-1 is done, [x | s_hi | s_lo] into the
-//             single M-step stage in shared memory
+//             operand [x | s_hi | s_lo] goes straight into tensor memory (which
+//             frees the staging slot), and [s_hi | s_lo] next to X(t) in the
+//             M-step stage
 //   MMA       E-step S(t)[rows, comps] = [x | s_hi | s_lo] . W^T with the
 //             A operand read from tensor memory (32 instructions, N = 128)
 //   softmax   (16 warps, four threads per row) logits, row max / exp / sum,
 //             (max, sum) combined across the row's four threads, exchanged with
 //             the cluster through DSMEM, r = exp(l - lse) split r_hi + r_lo
-//   MMA       M-step stats[comps, x | x^2 | 1] += R^T . [x | s_hi] (+ s_lo, 1)
+//   MMA       M-step stats[comps, x | s_hi | s_lo | 1] += R^T . [x | s_hi | s_lo | 1],
+//             one N = 208 instruction per 16 rows and R part (the four
+//             operand groups sit 16 KB apart; the last is a constant ones block)
 //
 // The E-step of tile t+1 therefore depends only on X(t+1) and on the E-step
 // of tile t (tensor-memory operand), never on the M-step buffers, and the
@@ -52,11 +55,11 @@ constexpr int kSplit = 4;                // softmax threads per row
 constexpr int kPart = kKC / kSplit;      // components per softmax thread
 constexpr int kSoftWarps = 4 * kSplit;   // every TMEM lane quarter kSplit times
 constexpr int kBlock = 16384;   // one [128][64] bf16 swizzled block
-constexpr int kAuxBytes = 4096; // [16][128] K-major ones operand (n_k)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kDmCol = 256;  // M-step statistics [x (64) | x^2 (64) | 1 (16)]
-constexpr uint32_t kFCol = 400;   // E-step operand [x | s_hi | s_lo], 32 columns each
-constexpr int kFdm = 144;
+constexpr uint32_t kSCol = 0;     // E-step logits S (128 columns)
+constexpr uint32_t kDmCol = 128;  // M-step statistics [x | s_hi | s_lo (64 each) | 1 (16)]
+constexpr uint32_t kFCol = 336;   // E-step operand [x | s_hi | s_lo], 32 columns each
+constexpr int kFdm = 208;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (diag: s = 1)
@@ -67,20 +70,20 @@ constexpr int kThreads = (kWarpSoftmax0 + kSoftWarps) * 32;  // 22 warps, <= 88 
 
 // shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
 constexpr int kParams = 0;                     // a_0 a_1 a_2 | v_0 v_1 v_2 (16 KB each)
-constexpr int kStaging = kParams + 2 * kNS * kBlock;  // X staging slots [2]
-constexpr int kMX = kStaging + 2 * kBlock;     // M-step stage: x | s_hi | s_lo
+constexpr int kStaging = kParams + 2 * kNS * kBlock;  // X staging slot
+constexpr int kMX = kStaging + kBlock;         // M-step stage: x | s_hi | s_lo | ones
 constexpr int kMSH = kMX + kBlock;
 constexpr int kMSL = kMSH + kBlock;
-constexpr int kAux = kMSL + kBlock;            // ones operand (constant)
-constexpr int kR = kAux + kAuxBytes;           // R: two 64-component MN groups
-constexpr int kConsts = kR + 2 * kBlock;       // mpm[128], h[128], c2[128]
-constexpr int kHalfX = kConsts + 3 * 128 * 4;  // [kSplit parts][128 rows] float2
+constexpr int kOnes = kMSL + kBlock;           // MN-major, column 0 = 1 (constant)
+constexpr int kR = kOnes + kBlock;             // R: two 64-component MN groups
+constexpr int kConsts = kR + 2 * kBlock;       // lz[128], c2[128]
+constexpr int kHalfX = kConsts + 2 * 128 * 4;  // [kSplit parts][128 rows] float2
 constexpr int kXch = kHalfX + kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
 __host__ __device__ constexpr int bars_off(int c) { return kXch + 2 * c * 128 * 8; }
 __host__ __device__ constexpr int red_off(int c) { return bars_off(c) + 192; }
 __host__ __device__ constexpr int smem_total(int c) { return bars_off(c) + 256; }
 static_assert(smem_total(kMaxCluster) <= 232448, "shared memory budget");
-static_assert(kFCol + 96 <= kTmemCols && kDmCol + kFdm <= kFCol, "tensor memory budget");
+static_assert(kFCol + 96 <= kTmemCols && kDmCol + kFdm <= kFCol && kSCol + kKC <= kDmCol, "tensor memory budget");
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -90,13 +93,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 struct Bars {
   uint64_t params;
-  uint64_t xfull[2];   // TMA: staging slot holds X(t)
-  uint64_t sempty[2];  // prep: staging slot copied into the M-step stage (4 warps)
+  uint64_t xfull;      // TMA: staging slot holds X(t)
+  uint64_t sempty;     // prep: staging slot read (4 warps)
+  uint64_t mxfull;     // TMA: M-step stage holds X(t)
   uint64_t ffull;      // prep: E-step operand of tile t in tensor memory (4 warps)
-  uint64_t mfull;      // prep: M-step stage holds tile t (4 warps)
+  uint64_t mfull;      // prep: M-step stage holds [x | s_hi | s_lo] of tile t (4 warps)
   uint64_t mfree;      // MMA: M-step of tile t done reading the stage
-  uint64_t sfull[2];   // MMA: S(t) complete (the E-step operand is free again)
-  uint64_t sfree[2];   // softmax: S(t) loaded (16 warps)
+  uint64_t sfull;      // MMA: S(t) complete (the E-step operand is free again)
+  uint64_t sfree;      // softmax: S(t) loaded (16 warps)
   uint64_t rfull;      // softmax: an R part written (16 warps)
   uint64_t rfree;      // MMA: that R part consumed
   uint64_t xch[2];     // cluster exchange of (row max, row sum)
@@ -132,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nclus = a.cluster_size;
   Bars* bars = reinterpret_cast<Bars*>(sm + bars_off(nclus));
   float* c_lz = reinterpret_cast<float*>(sm + kConsts);  // c2 - h mpm: the logit at S = 0
-  float* c_c2 = c_lz + 256;
+  float* c_c2 = c_lz + 128;
   float2* xch = reinterpret_cast<float2*>(sm + kXch);
   volatile int* abort = &bars->abort;
   const uint64_t lim = a.wait_ns;  // every wait below gives up after this long
@@ -146,11 +150,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(&bars->params, 1);
+    mbar_init(&bars->xfull, 1);
+    mbar_init(&bars->sempty, 4);
+    mbar_init(&bars->mxfull, 1);
+    mbar_init(&bars->sfull, 1);
+    mbar_init(&bars->sfree, kSoftWarps);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->xfull[i], 1);
-      mbar_init(&bars->sempty[i], 4);
-      mbar_init(&bars->sfull[i], 1);
-      mbar_init(&bars->sfree[i], kSoftWarps);
       mbar_init(&bars->xch[i], 1);
       mbar_init(&bars->hx[i], kSoftWarps);
     }
@@ -171,12 +176,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     c_lz[i] = fmaf(-kHalfLog2e, cs[i], cs[256 + i]);
     c_c2[i] = cs[256 + i];
   }
-  {  // ones operand of the n_k statistic: K-major [16][128], row 0 = 1
-    char* aux = sm + kAux;
-    for (int i = tid; i < 16 * 128; i += kThreads) {
-      const int n = i >> 7, r = i & 127;
-      *reinterpret_cast<__nv_bfloat16*>(aux + (r >> 6) * 2048 + sw128(n, r & 63)) = __float2bfloat16(n == 0 ? 1.f : 0.f);
-    }
+  // ones group of the M-step operand (n_k): MN-major like X, element (row, 0)
+  // = 1 and the rest 0, i.e. 16-byte chunk 0 of every row holds bf16 1.0 in
+  // its first element; the chunk sits at position (row & 7) after the swizzle
+  for (int i = tid; i < kBlock / 16; i += kThreads) {
+    const int row = i >> 3, chunk = i & 7;
+    reinterpret_cast<uint4*>(sm + kOnes)[i] = make_uint4(chunk == (row & 7) ? 0x3F80u : 0u, 0u, 0u, 0u);
   }
   fence_proxy_async();
   tmem_fence_before();
@@ -190,9 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = warp * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
     const uint32_t swz = (uint32_t)(r & 7);
-    // the 32 words (64 bf16) of row r of staging slot `slot`, in element order
-    auto load_row = [&](int slot, uint32_t (&w)[32]) {
-      const char* base = sm + kStaging + slot * kBlock + r * 128;
+    // the 32 words (64 bf16) of row r of a swizzled X block, in element order
+    auto load_row = [&](int off, uint32_t (&w)[32]) {
+      const char* base = sm + off + r * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 v = *reinterpret_cast<const uint4*>(base + ((c ^ swz) << 4));
@@ -202,38 +207,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         w[4 * c + 3] = v.w;
       }
     };
-    // M-step stage of tile u: wait until the M-step of u-1 released it, then
-    // [x | s_hi | s_lo] (same swizzled layout as the staging slot)
+    // M-step stage of tile u: X(u) lands there by TMA once the M-step of u-1
+    // is done; add [s_hi | s_lo] (same swizzled layout)
     auto fill_mstage = [&](int u) -> bool {
-      if (u >= 1 && !mbar_wait_warp(&bars->mfree, (u - 1) & 1, abort, lim)) return false;
+      if (!mbar_wait_warp(&bars->mxfull, u & 1, abort, lim)) return false;
       uint32_t w[32];
-      load_row(u & 1, w);
+      load_row(kMX, w);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) square_split(w[4 * c + i], hi[i], lo[i]);
         const int off = r * 128 + (int)((c ^ swz) << 4);
-        *reinterpret_cast<uint4*>(sm + kMX + off) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
         *reinterpret_cast<uint4*>(sm + kMSH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         *reinterpret_cast<uint4*>(sm + kMSL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       fence_proxy_async();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars->mfull);
-        mbar_arrive(&bars->sempty[u & 1]);
-      }
+      if (lane == 0) mbar_arrive(&bars->mfull);
       return true;
     };
     bool ok = true;
     for (int t = 0; t < T; ++t) {
-      const int s = t & 1;
-      if (!mbar_wait_warp(&bars->xfull[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars->xfull, t & 1, abort, lim)) { ok = false; break; }
       uint32_t w[32];
-      load_row(s, w);
+      load_row(kStaging, w);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->sempty);  // the TMA may refill the slot
       // the E-step of t-1 read the operand region: wait for its completion
-      if (t >= 1 && !mbar_wait_warp(&bars->sfull[(t - 1) & 1], ((t - 1) >> 1) & 1, abort, lim)) { ok = false; break; }
+      if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
       tmem_fence_after();
       tmem_st32(tmem + lane_addr + kFCol, w);
 #pragma unroll
@@ -254,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && T >= 1 && !fill_mstage(T - 1)) ok = false;
     if (!ok) set_abort(bars, a.status);
   } else if (warp == kWarpTma) {
-    // ---------------- producer: weights once, then X tiles into the staging slots ----------------
+    // ---------------- producer: weights once, then X tiles (staging slot and M-step stage) ----------------
     if (lane == 0) {
       prefetch_tmap(&tmap);
       constexpr int kParamBlocks = 2 * kNS;
@@ -262,29 +264,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       const char* src = a.params + (int64_t)rank * kParamBlocks * kBlock;
       for (int i = 0; i < kParamBlocks; ++i)
         bulk_load(sm + kParams + i * kBlock, src + (int64_t)i * kBlock, kBlock, &bars->params);
-      int issued = 0;
-      for (int t = 0; t < T; ++t) {
-        const int s = t & 1;
-        if (t >= 2 && !mbar_wait(&bars->sempty[s], ((t >> 1) - 1) & 1, abort, lim)) { set_abort(bars, a.status); break; }
+      auto row0 = [&](int t) { return (int)((cid + (int64_t)t * ncl) * kBM); };
+      int issued = 0, missued = 0;
+      // X(u) into the M-step stage once the M-step of u-1 released it
+      auto load_m = [&](int u) -> bool {
+        if (u >= 1 && !mbar_wait(&bars->mfree, (u - 1) & 1, abort, lim)) return false;
+        mbar_expect_tx(&bars->mxfull, kBlock);
+        tma_load_2d(sm + kMX, &tmap, 0, row0(u), &bars->mxfull);
+        missued = u + 1;
+        return true;
+      };
+      bool ok = true;
+      for (int t = 0; t < T && ok; ++t) {
+        if (t >= 1 && !mbar_wait(&bars->sempty, (t - 1) & 1, abort, lim)) { ok = false; break; }
         if (a.test_stall) break;  // test hook: no X tile ever lands, every wait on it runs out
-        const int row0 = (int)((cid + (int64_t)t * ncl) * kBM);
-        mbar_expect_tx(&bars->xfull[s], kBlock);
-        tma_load_2d(sm + kStaging + s * kBlock, &tmap, 0, row0, &bars->xfull[s]);
+        mbar_expect_tx(&bars->xfull, kBlock);
+        tma_load_2d(sm + kStaging, &tmap, 0, row0(t), &bars->xfull);
         issued = t + 1;
+        if (t >= 1) ok = load_m(t - 1);
       }
+      if (ok && T >= 1 && issued == T) ok = load_m(T - 1);
+      if (!ok) set_abort(bars, a.status);
       // before the CTA can exit, every copy it started has landed (bounded,
-      // also after an abort): the weights and the last load of each slot
+      // also after an abort): the weights and the last load of each buffer
       mbar_wait(&bars->params, 0, nullptr, lim);
-      for (int t = std::max(0, issued - 2); t < issued; ++t)
-        mbar_wait(&bars->xfull[t & 1], (t >> 1) & 1, nullptr, lim);
+      if (issued > 0) mbar_wait(&bars->xfull, (issued - 1) & 1, nullptr, lim);
+      if (missued > 0) mbar_wait(&bars->mxfull, (missued - 1) & 1, nullptr, lim);
     }
   } else if (warp == kWarpMma) {
     // ---------------- MMA issuer (one thread) ----------------
     if (lane == 0) {
-      const uint32_t id_e = idesc_bf16(128, kKC, 0, 0);  // A (TMEM) x W^T (K-major)
-      const uint32_t id_m2 = idesc_bf16(128, 128, 1, 1);  // R^T x [x | s_hi], both MN-major
-      const uint32_t id_m = idesc_bf16(128, 64, 1, 1);    // R_hi^T x s_lo
-      const uint32_t id_aux = idesc_bf16(128, 16, 1, 0);  // R^T x 1
+      const uint32_t id_e = idesc_bf16(128, kKC, 0, 0);   // A (TMEM) x W^T (K-major)
+      const uint32_t id_m = idesc_bf16(128, kFdm, 1, 1);  // R^T x [x | s_hi | s_lo | 1], both MN-major
       const uint32_t base = smem_u32(sm);
       bool ok = mbar_wait(&bars->params, 0, abort, lim);
       tmem_fence_after();
@@ -295,13 +306,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         wa[j] = desc_kmajor(base + kParams + j * kBlock);
         wv[j] = desc_kmajor(base + kParams + (kNS + j) * kBlock);
       }
-      // E-step of tile t into S[t & 1]: x.a_j, s_hi.v_j (j < 3), s_lo.v_j (j < 2)
+      // E-step of tile t into S: x.a_j, s_hi.v_j (j < 3), s_lo.v_j (j < 2)
       auto issue_e = [&](int t) -> bool {
-        const int s = t & 1;
         if (!mbar_wait(&bars->ffull, t & 1, abort, lim)) return false;
-        if (t >= 2 && !mbar_wait(&bars->sfree[s], ((t >> 1) - 1) & 1, abort, lim)) return false;
+        if (t >= 1 && !mbar_wait(&bars->sfree, (t - 1) & 1, abort, lim)) return false;
         tmem_fence_after();
-        const uint32_t d = tmem + (uint32_t)(s * kKC);
+        const uint32_t d = tmem + kSCol;
         uint32_t acc = 0;
 #pragma unroll
         for (int j = 0; j < kNS; ++j)
@@ -318,13 +328,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 2; ++j)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
-        mma_commit(&bars->sfull[s]);
+        mma_commit(&bars->sfull);
         return true;
       };
       const uint64_t r0 = desc_mnmajor(base + kR, kBlock);
-      const uint64_t x0 = desc_mnmajor(base + kMX, kBlock);  // [x | s_hi]: adjacent 16 KB groups
-      const uint64_t sl0 = desc_mnmajor(base + kMSL, kBlock);
-      const uint64_t aux0 = desc_kmajor(base + kAux);
+      const uint64_t x0 = desc_mnmajor(base + kMX, kBlock);  // [x | s_hi | s_lo | 1]: 16 KB apart
       // M-step of tile t with R part PART (0 = high bf16 terms, 1 = residual)
       auto issue_m = [&](int t, auto part_tag) -> bool {
         constexpr int part = decltype(part_tag)::value;
@@ -336,11 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // 16 rows per instruction: +2048 B (MN-major)
           const uint64_t step = (uint64_t)(ks * 128);
-          const uint64_t ra = r0 + step;
-          const uint32_t acc = ks == 0 ? acc0 : 1u;
-          mma_bf16(tmem + kDmCol, ra, x0 + step, id_m2, acc);
-          if constexpr (part == 0) mma_bf16(tmem + kDmCol + 64, ra, sl0 + step, id_m, 1u);
-          mma_bf16(tmem + kDmCol + 128, ra, aux0 + (uint64_t)((ks >> 2) * 128 + (ks & 3) * 2), id_aux, acc);
+          mma_bf16(tmem + kDmCol, r0 + step, x0 + step, id_m, ks == 0 ? acc0 : 1u);
         }
         mma_commit(&bars->rfree);
         if constexpr (part == 1) mma_commit(&bars->mfree);
@@ -351,11 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Issue order: E(0), E(1), then per tile M_hi(t), M_lo(t), E(t+2).
       // M_lo(t) waits for the residual R(t), written by the softmax after the
       // logits of t+1 (whose S(t+1) is already queued); E(t+2) then still ends
-      // well before the softmax finishes tile t+1.  Keeping M_lo(t) ahead of
-      // E(t+2) matters: its completion frees the single M-step stage, the
-      // stage refill frees the staging slot, and that slot receives X(t+2) --
-      // with E(t+2) first, that chain closed a cycle through the tensor pipe,
-      // the prep warps and a TMA round trip once per tile.
+      // before the softmax finishes tile t+1.  Keeping M_lo(t) ahead of E(t+2)
+      // matters: its completion frees the M-step stage for X(t+1) (TMA, then
+      // the prep's s_hi / s_lo), which M_hi(t+1) needs.  Queued behind E(t+2)
+      // it would put an E-step, a TMA round trip and the stage refill into the
+      // critical path of every tile.
       if (ok && T > 0) ok = issue_e(0);
       if (ok && T > 1) ok = issue_e(1);
       for (int t = 0; ok && t < T; ++t) {
@@ -401,15 +405,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = t & 1;
       const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
       const bool valid = grow < a.N;
-      if (!mbar_wait_warp(&bars->sfull[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars->sfull, t & 1, abort, lim)) { ok = false; break; }
       tmem_fence_after();
-      const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC + k0);
+      const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
 #pragma unroll
       for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
       tmem_wait_ld();
       tmem_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sfree[s]);
+      if (lane == 0) mbar_arrive(&bars->sfree);
       // logits (log2 units) min(lz - h S, c2), h = log2(e)/2, and this part's max
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -510,21 +514,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue: statistics partials (all softmax warps) ----------------
     // the MMA thread always commits `mdone` (also after an abort): wait for it
     // without the abort shortcut before touching tensor memory again.  TMEM
-    // lane = component; part qc writes columns 32 qc .. 32 qc + 31 (sums of
-    // r x and r x^2), part 0 also column 128 (n_k).
+    // lane = component; columns [x | s_hi | s_lo | 1].  Parts 0, 1 write the
+    // sums of r x (32 features each), parts 2, 3 those of r x^2 = s_hi + s_lo
+    // columns, part 0 also n_k.
     if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 2 * lim)) set_abort(bars, a.status);
     tmem_fence_after();
     {
-      static_assert(kSplit * 32 == 128, "epilogue column split");
+      static_assert(kSplit == 4, "epilogue column split");
       const int comp = (int)rank * kKC + row;
       float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
+      const uint32_t dm = tmem + lane_addr + kDmCol;
       float v[32];
-      tmem_ld32(tmem + lane_addr + kDmCol + 32 * qc, v);
-      tmem_wait_ld();
+      if (qc < 2) {
+        tmem_ld32(dm + 32 * qc, v);
+        tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) out[1 + 32 * qc + j] = v[j];
+        for (int j = 0; j < 32; ++j) out[1 + 32 * qc + j] = v[j];
+      } else {
+        const int f0 = 32 * (qc - 2);
+        float w2[16];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // 16 features at a time: fewer live registers
+          tmem_ld16(dm + 64 + f0 + 16 * h, v);
+          tmem_ld16(dm + 128 + f0 + 16 * h, w2);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) out[1 + 64 + f0 + 16 * h + j] = v[j] + w2[j];
+        }
+      }
       if (qc == 0) {
-        tmem_ld32(tmem + lane_addr + kDmCol + 128, v);  // 32 columns; the first is n_k
+        tmem_ld32(dm + 192, v);  // 32 columns; the first is n_k
         tmem_wait_ld();
         out[0] = v[0];
       }
