@@ -230,9 +230,14 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
     if (rc != GMMXX_ERR_UNSUPPORTED || mode == 2) return rc;  // else: no co-resident cluster -> CUDA-core kernels
   }
   RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
-  a.lse_out = reinterpret_cast<float*>(ws + L.lse);
   a.ll_part = reinterpret_cast<double*>(ws + L.llpart);
   a.ll = log_likelihood;
+  if (L.Kp == kBK) {  // one component tile: logsumexp and statistics in one pass
+    a.stats = stats;
+    a.part = reinterpret_cast<float*>(ws + L.mpart);
+    return launch_em_small(cov_type, a, (int)B, st);
+  }
+  a.lse_out = reinterpret_cast<float*>(ws + L.lse);
   if (cov_type == GMMXX_TIED) a.q_out = reinterpret_cast<float*>(ws + L.qrow);
   if (int rc = launch_rows(cov_type, MODE_LSE, a, (int)B, st)) return rc;
   a.lse_in = a.lse_out;

@@ -15,7 +15,11 @@
 //   mstep_kernel  grid (row blocks, K tiles, B): recomputes the logits of its
 //                 64-component slice, r = exp(logit - lse), and accumulates
 //                 sum_n r_nk psi(x_n) in registers over many row tiles; one
-//                 atomic flush per CTA.  (N, K) is never materialised.
+//                 flush per CTA into its own partial slot.  (N, K) is never
+//                 materialised.
+//   em_small_kernel  K <= 64 (one component tile): the two passes above in
+//                 one -- logits, the row's logsumexp, r and the statistics per
+//                 row tile, the log-likelihood summed per CTA.
 #include "rows_api.cuh"
 
 #include <float.h>
@@ -427,6 +431,112 @@ __global__ void __launch_bounds__(kThreads) mstep_kernel(RowArgs a) {
     }
 }
 
+// One pass for K <= 64: every component of a row is in this CTA's tile, so
+// the row's logsumexp is complete after one tile_dots.  Same arithmetic, in
+// the same order, as rows_kernel<MODE_LSE> followed by mstep_kernel (the
+// statistics are bitwise identical; the log-likelihood is summed per CTA).
+template <int COV, int NCH>
+__global__ void __launch_bounds__(kThreads) em_small_kernel(RowArgs a) {
+  extern __shared__ __align__(16) char smem_raw[];
+  const Smem s = carve<COV>(smem_raw, a.D, true);
+  const int b = blockIdx.z;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int kg = threadIdx.x >> 4, fg = threadIdx.x & 15;
+  const int D = a.D, xst = D + 1;
+  if (COV == GMMXX_TIED) {
+    const float* pb = a.prec + (int64_t)b * D * D;
+    for (int e = threadIdx.x; e < D * D; e += kThreads) s.prec[e] = pb[e];
+  }
+  if (COV == GMMXX_FULL) {
+    for (int i = threadIdx.x; i < D; i += kThreads) {
+      int p = i * D - i * (i - 1) / 2;
+      for (int j = i; j < D; ++j) s.pairs[p++] = (uint16_t)(i | (j << 8));
+    }
+  }
+  float macc[NCH][4][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) macc[c][i][j] = 0.f;
+  double ll = 0.0;
+
+  const int64_t rstart = (int64_t)blockIdx.x * a.rows_per_cta;
+  const int64_t rend = min(rstart + a.rows_per_cta, a.N);
+  float acc[4][4];
+  for (int64_t row0 = rstart; row0 < rend; row0 += kBN) {
+    __syncthreads();
+    load_rows<COV>(a, s, b, row0);
+    tile_dots<COV>(a, s, b, 0, acc);
+    to_logits(a, s, b, 0, acc);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      // the row's logsumexp over its 16 threads (as rows_kernel<MODE_LSE>)
+      float m = fmaxf(fmaxf(acc[i][0], acc[i][1]), fmaxf(acc[i][2], acc[i][3]));
+      float sm = 0.f;
+      if (m != -INFINITY) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sm += expf(acc[i][j] - m);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, sm, o);
+        lse_merge(m, sm, m2, s2);
+      }
+      float run_m = -INFINITY, run_s = 0.f;
+      lse_merge(run_m, run_s, m, sm);
+      const float l = run_m + logf(run_s);
+      const int64_t row = row0 + ty * 4 + i;
+      const bool ok = row < rend;
+      if (ok && tx == 0) ll += (double)l;
+      float r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = ok ? expf(acc[i][j] - l) : 0.f;  // -inf -> 0
+      *reinterpret_cast<float4*>(s.R + (ty * 4 + i) * kBK + tx * 4) = make_float4(r[0], r[1], r[2], r[3]);
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      __syncthreads();
+      for (int e = threadIdx.x; e < kBN * 64; e += kThreads) {
+        const int r = e >> 6, f = e & 63;
+        s.phim[e] = feat_m<COV>(s.xs + r * xst, s.q[r], c * 64 + f, D, a.FM, s.pairs);
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int r = 0; r < kBN; ++r) {
+        const float4 rv = *reinterpret_cast<const float4*>(s.R + r * kBK + kg * 4);
+        const float4 pv = *reinterpret_cast<const float4*>(s.phim + r * 64 + fg * 4);
+        const float ra[4] = {rv.x, rv.y, rv.z, rv.w};
+        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) macc[c][i][j] = fmaf(ra[i], pa[j], macc[c][i][j]);
+      }
+    }
+  }
+  float* st = a.part + ((int64_t)b * a.part_blocks + blockIdx.x) * a.Kp * a.FM;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = kg * 4 + i;
+      if (k >= a.K) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int f = c * 64 + fg * 4 + j;
+        if (f < a.FM) st[(int64_t)k * a.FM + f] = macc[c][i][j];
+      }
+    }
+  if (a.ll_part != nullptr) {
+    __shared__ double red[kThreads / 32];
+    const double tot = block_sum<double>(ll, red);
+    if (threadIdx.x == 0) a.ll_part[(int64_t)b * gridDim.x + blockIdx.x] = tot;
+  }
+}
+
 __global__ void stats_reduce_kernel(const float* part, int64_t nblk, int64_t stride, int64_t Kp, int K, int FM,
                                     int B, float* stats, const double* ll_part, int64_t nll, double* ll) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -574,6 +684,51 @@ int launch_mstep(int cov, const RowArgs& a, int B, cudaStream_t st) {
     case GMMXX_DIAG: return launch_mstep_c<GMMXX_DIAG>(a, B, st);
     case GMMXX_TIED: return launch_mstep_c<GMMXX_TIED>(a, B, st);
     case GMMXX_FULL: return launch_mstep_c<GMMXX_FULL>(a, B, st);
+  }
+  return set_error(GMMXX_ERR_INVALID, "bad covariance type %d", cov);
+}
+
+template <int COV, int NCH>
+static int launch_small_t(RowArgs a, int B, cudaStream_t st) {
+  const int64_t sm = smem_bytes(COV, a.D, true);
+  auto k = em_small_kernel<COV, NCH>;
+  if (int rc = prep_smem(k, sm)) return rc;
+  const int64_t tiles = ceil_div(a.N, kBN);
+  const int64_t nblk_max = mstep_blocks(B, a.N, a.Kp);
+  a.rows_per_cta = ceil_div(tiles, nblk_max) * kBN;
+  const int64_t nblk = ceil_div(a.N, a.rows_per_cta);
+  a.part_blocks = nblk_max;
+  dim3 grid((unsigned)nblk, 1u, (unsigned)B);
+  k<<<grid, kThreads, sm, st>>>(a);
+  if (int rc = check_launch("em_small_kernel")) return rc;
+  // statistics: the first nblk of nblk_max slots; log-likelihood: nblk per problem, packed
+  const int64_t n = (int64_t)B * a.K * a.FM;
+  stats_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(
+      a.part, nblk, nblk_max, a.Kp, a.K, a.FM, B, a.stats, a.ll_part, nblk, a.ll);
+  return check_launch("stats_reduce_kernel");
+}
+
+template <int COV>
+static int launch_small_c(const RowArgs& a, int B, cudaStream_t st) {
+  switch ((int)ceil_div(a.FM, 64)) {
+    case 1: return launch_small_t<COV, 1>(a, B, st);
+    case 2: return launch_small_t<COV, 2>(a, B, st);
+    case 3: return launch_small_t<COV, 3>(a, B, st);
+    case 4: return launch_small_t<COV, 4>(a, B, st);
+    case 5: return launch_small_t<COV, 5>(a, B, st);
+    case 6: return launch_small_t<COV, 6>(a, B, st);
+  }
+  return set_error(GMMXX_ERR_UNSUPPORTED, "statistics width %d exceeds the SIMT window", a.FM);
+}
+
+int launch_em_small(int cov, const RowArgs& a, int B, cudaStream_t st) {
+  if (a.N == 0) return GMMXX_OK;
+  if (a.Kp != kBK) return set_error(GMMXX_ERR_UNSUPPORTED, "one-pass statistics need K <= %d", kBK);
+  switch (cov) {
+    case GMMXX_SPHERICAL: return launch_small_c<GMMXX_SPHERICAL>(a, B, st);
+    case GMMXX_DIAG: return launch_small_c<GMMXX_DIAG>(a, B, st);
+    case GMMXX_TIED: return launch_small_c<GMMXX_TIED>(a, B, st);
+    case GMMXX_FULL: return launch_small_c<GMMXX_FULL>(a, B, st);
   }
   return set_error(GMMXX_ERR_INVALID, "bad covariance type %d", cov);
 }

@@ -38,5 +38,8 @@ int launch_rows(int cov, int mode, const RowArgs& a, int B, cudaStream_t st);
 int launch_mstep(int cov, const RowArgs& a, int B, cudaStream_t st);
 // stats += sum of the M-step partials, ll += sum of the LSE partials (fixed order)
 int launch_stats_reduce(const RowArgs& a, int B, cudaStream_t st);
+// K <= 64: statistics and log-likelihood in one pass, then their fixed-order
+// reduction (replaces launch_rows(LSE) + launch_mstep + launch_stats_reduce)
+int launch_em_small(int cov, const RowArgs& a, int B, cudaStream_t st);
 
 }  // namespace gmmxx
