@@ -233,6 +233,60 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2
   m = nm;
 }
 
+// sum_n r_nk psi(x_n) for one row tile (R in s.R): n_k, the statistic of the
+// constant feature 0, as a column sum of R; the other FM - 1 features in
+// 64-wide chunks (thread: components 4 kg.., features 4 fg.. of a chunk)
+template <int COV, int NCH>
+__device__ __forceinline__ void mstep_tile(const RowArgs& a, const Smem& s, float (&macc)[NCH][4][4],
+                                           float (&nk)[4]) {
+  const int kg = threadIdx.x >> 4, fg = threadIdx.x & 15;
+  const int D = a.D, xst = D + 1;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < kBN * 64; e += kThreads) {
+      const int r = e >> 6, f = e & 63;
+      s.phim[e] = feat_m<COV>(s.xs + r * xst, s.q[r], 1 + c * 64 + f, D, a.FM, s.pairs);
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int r = 0; r < kBN; ++r) {
+      const float4 rv = *reinterpret_cast<const float4*>(s.R + r * kBK + kg * 4);
+      const float4 pv = *reinterpret_cast<const float4*>(s.phim + r * 64 + fg * 4);
+      const float ra[4] = {rv.x, rv.y, rv.z, rv.w};
+      const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+      if (c == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) nk[i] += ra[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) macc[c][i][j] = fmaf(ra[i], pa[j], macc[c][i][j]);
+    }
+  }
+}
+
+// one CTA's statistics into its partial slot st[Kp][FM] (component tile kt)
+template <int NCH>
+__device__ __forceinline__ void mstep_flush(const RowArgs& a, float* st, int kt, const float (&macc)[NCH][4][4],
+                                            const float (&nk)[4]) {
+  const int kg = threadIdx.x >> 4, fg = threadIdx.x & 15;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int k = kt * kBK + kg * 4 + i;
+    if (k >= a.K) continue;
+    if (fg == 0) st[(int64_t)k * a.FM] = nk[i];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int f = 1 + c * 64 + fg * 4 + j;
+        if (f < a.FM) st[(int64_t)k * a.FM + f] = macc[c][i][j];
+      }
+  }
+}
+
 template <int COV, int MODE>
 __global__ void __launch_bounds__(kThreads) rows_kernel(RowArgs a) {
   extern __shared__ __align__(16) char smem_raw[];
@@ -355,8 +409,7 @@ __global__ void __launch_bounds__(kThreads) mstep_kernel(RowArgs a) {
   const Smem s = carve<COV>(smem_raw, a.D, true);
   const int b = blockIdx.z, kt = blockIdx.y;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int kg = threadIdx.x >> 4, fg = threadIdx.x & 15;
-  const int D = a.D, xst = D + 1;
+  const int D = a.D;
   if (COV == GMMXX_TIED) {
     const float* pb = a.prec + (int64_t)b * D * D;
     for (int e = threadIdx.x; e < D * D; e += kThreads) s.prec[e] = pb[e];
@@ -374,6 +427,7 @@ __global__ void __launch_bounds__(kThreads) mstep_kernel(RowArgs a) {
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) macc[c][i][j] = 0.f;
+  float nk[4] = {0.f, 0.f, 0.f, 0.f};
 
   const int64_t rstart = (int64_t)blockIdx.x * a.rows_per_cta;
   const int64_t rend = min(rstart + a.rows_per_cta, a.N);
@@ -394,41 +448,10 @@ __global__ void __launch_bounds__(kThreads) mstep_kernel(RowArgs a) {
       for (int j = 0; j < 4; ++j) r[j] = ok ? expf(acc[i][j] - l) : 0.f;  // -inf -> 0
       *reinterpret_cast<float4*>(s.R + (ty * 4 + i) * kBK + tx * 4) = make_float4(r[0], r[1], r[2], r[3]);
     }
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      __syncthreads();
-      for (int e = threadIdx.x; e < kBN * 64; e += kThreads) {
-        const int r = e >> 6, f = e & 63;
-        s.phim[e] = feat_m<COV>(s.xs + r * xst, s.q[r], c * 64 + f, D, a.FM, s.pairs);
-      }
-      __syncthreads();
-#pragma unroll 4
-      for (int r = 0; r < kBN; ++r) {
-        const float4 rv = *reinterpret_cast<const float4*>(s.R + r * kBK + kg * 4);
-        const float4 pv = *reinterpret_cast<const float4*>(s.phim + r * 64 + fg * 4);
-        const float ra[4] = {rv.x, rv.y, rv.z, rv.w};
-        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) macc[c][i][j] = fmaf(ra[i], pa[j], macc[c][i][j]);
-      }
-    }
+    mstep_tile<COV, NCH>(a, s, macc, nk);
   }
   // one flush per CTA into its own partial slot (reduced in a fixed order later)
-  float* st = a.part + ((int64_t)b * a.part_blocks + blockIdx.x) * a.Kp * a.FM;
-#pragma unroll
-  for (int c = 0; c < NCH; ++c)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = kt * kBK + kg * 4 + i;
-      if (k >= a.K) continue;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int f = c * 64 + fg * 4 + j;
-        if (f < a.FM) st[(int64_t)k * a.FM + f] = macc[c][i][j];
-      }
-    }
+  mstep_flush<NCH>(a, a.part + ((int64_t)b * a.part_blocks + blockIdx.x) * a.Kp * a.FM, kt, macc, nk);
 }
 
 // One pass for K <= 64: every component of a row is in this CTA's tile, so
@@ -441,8 +464,7 @@ __global__ void __launch_bounds__(kThreads) em_small_kernel(RowArgs a) {
   const Smem s = carve<COV>(smem_raw, a.D, true);
   const int b = blockIdx.z;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int kg = threadIdx.x >> 4, fg = threadIdx.x & 15;
-  const int D = a.D, xst = D + 1;
+  const int D = a.D;
   if (COV == GMMXX_TIED) {
     const float* pb = a.prec + (int64_t)b * D * D;
     for (int e = threadIdx.x; e < D * D; e += kThreads) s.prec[e] = pb[e];
@@ -460,6 +482,7 @@ __global__ void __launch_bounds__(kThreads) em_small_kernel(RowArgs a) {
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) macc[c][i][j] = 0.f;
+  float nk[4] = {0.f, 0.f, 0.f, 0.f};
   double ll = 0.0;
 
   const int64_t rstart = (int64_t)blockIdx.x * a.rows_per_cta;
@@ -496,40 +519,9 @@ __global__ void __launch_bounds__(kThreads) em_small_kernel(RowArgs a) {
       for (int j = 0; j < 4; ++j) r[j] = ok ? expf(acc[i][j] - l) : 0.f;  // -inf -> 0
       *reinterpret_cast<float4*>(s.R + (ty * 4 + i) * kBK + tx * 4) = make_float4(r[0], r[1], r[2], r[3]);
     }
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      __syncthreads();
-      for (int e = threadIdx.x; e < kBN * 64; e += kThreads) {
-        const int r = e >> 6, f = e & 63;
-        s.phim[e] = feat_m<COV>(s.xs + r * xst, s.q[r], c * 64 + f, D, a.FM, s.pairs);
-      }
-      __syncthreads();
-#pragma unroll 4
-      for (int r = 0; r < kBN; ++r) {
-        const float4 rv = *reinterpret_cast<const float4*>(s.R + r * kBK + kg * 4);
-        const float4 pv = *reinterpret_cast<const float4*>(s.phim + r * 64 + fg * 4);
-        const float ra[4] = {rv.x, rv.y, rv.z, rv.w};
-        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) macc[c][i][j] = fmaf(ra[i], pa[j], macc[c][i][j]);
-      }
-    }
+    mstep_tile<COV, NCH>(a, s, macc, nk);
   }
-  float* st = a.part + ((int64_t)b * a.part_blocks + blockIdx.x) * a.Kp * a.FM;
-#pragma unroll
-  for (int c = 0; c < NCH; ++c)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = kg * 4 + i;
-      if (k >= a.K) continue;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int f = c * 64 + fg * 4 + j;
-        if (f < a.FM) st[(int64_t)k * a.FM + f] = macc[c][i][j];
-      }
-    }
+  mstep_flush<NCH>(a, a.part + ((int64_t)b * a.part_blocks + blockIdx.x) * a.Kp * a.FM, 0, macc, nk);
   if (a.ll_part != nullptr) {
     __shared__ double red[kThreads / 32];
     const double tot = block_sum<double>(ll, red);
@@ -665,7 +657,7 @@ static int launch_mstep_t(RowArgs a, int B, cudaStream_t st) {
 
 template <int COV>
 static int launch_mstep_c(const RowArgs& a, int B, cudaStream_t st) {
-  const int nch = (int)ceil_div(a.FM, 64);
+  const int nch = (int)ceil_div(a.FM - 1, 64);  // n_k is a column sum of R, outside the chunks
   switch (nch) {
     case 1: return launch_mstep_t<COV, 1>(a, B, st);
     case 2: return launch_mstep_t<COV, 2>(a, B, st);
@@ -710,7 +702,7 @@ static int launch_small_t(RowArgs a, int B, cudaStream_t st) {
 
 template <int COV>
 static int launch_small_c(const RowArgs& a, int B, cudaStream_t st) {
-  switch ((int)ceil_div(a.FM, 64)) {
+  switch ((int)ceil_div(a.FM - 1, 64)) {  // n_k is a column sum of R, outside the chunks
     case 1: return launch_small_t<COV, 1>(a, B, st);
     case 2: return launch_small_t<COV, 2>(a, B, st);
     case 3: return launch_small_t<COV, 3>(a, B, st);
