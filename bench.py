@@ -60,7 +60,7 @@ def launches_per_iteration(cfg, tc_path: bool) -> int:
     reduce), and for spherical K > 1024 the grouped passes: pack, G row-partial
     launches, combine, log-likelihood sum, G x (M-step launch + reduce)."""
     prep = 2 + (2 if cfg.cov_type in ("tied", "full") else 0)
-    stats = 3
+    stats = 2 if (not tc_path and cfg.K <= 64) else 3  # one-pass CUDA-core kernel + reduce for K <= 64
     if tc_path and cfg.cov_type == "spherical" and cfg.K > 1024:
         groups = (((cfg.K + 127) // 128) + 7) // 8
         stats = 3 + 3 * groups
@@ -188,7 +188,9 @@ def main():
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=0, help="override total N (smaller runs)")
-    ap.add_argument("--ref-rows", type=int, default=200_000)
+    ap.add_argument("--ref-rows", type=int, default=200_000, help="rows per step of --impl reference")
+    ap.add_argument("--cpu-rows", type=int, default=1_000_000,
+                    help="rows of the cpu_baseline sample (about 10 s of host work for config 1)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -361,7 +363,8 @@ def main():
                          "frac": achieved / peak, "traffic": traffic,
                          "kernel": ((("em_tc_diag_kernel" if cfg.cov_type == "diag" else "em_tc_kernel")
                                      + " (+ tc_pack_kernel, tc_reduce_kernel)") if tc_path
-                                    else "rows_kernel + mstep_kernel + stats_reduce_kernel"),
+                                    else ("em_small_kernel + stats_reduce_kernel" if cfg.K <= 64
+                                          else "rows_kernel + mstep_kernel + stats_reduce_kernel")),
                          "peak_source": f"{peaks['source']} bf16 {'sustained' if long_run else 'burst'}",
                          "algorithmic_flops_per_launch": flops, "launch_ms": acc_ms,
                          "hbm_frac": (n_local * cfg.B * D * torch.empty((), dtype=cfg.dtype).element_size()) /
@@ -372,7 +375,7 @@ def main():
         }
         if world == 1 and not args.no_cpu:
             try:
-                line["cpu_baseline"] = cpu_baseline(cfg, mix, (init_means, init_cov, init_w), args.ref_rows)
+                line["cpu_baseline"] = cpu_baseline(cfg, mix, (init_means, init_cov, init_w), args.cpu_rows)
             except Exception as exc:  # report, never fake
                 line["cpu_baseline"] = {"error": repr(exc)}
         print(json.dumps(line), flush=True)
