@@ -171,6 +171,63 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def run_infer(args, cfg, x, means, cov, weights):
+    """--infer: one inference call per step on the rows already in HBM, timed
+    with CUDA events on the launching stream (the output buffer of
+    predict_proba is allocated once).  Roofline: algorithmic logit FLOPs
+    against the bf16 peak for labels / score_samples, and the output bytes
+    against HBM for predict_proba (SURVEY 8d's bound for that call)."""
+    import torch
+
+    from gmmxx_b200 import engine
+
+    from gmmxx_b200 import _native as nat
+
+    B, N, D, K = cfg.B, x.shape[-2], cfg.D, cfg.K
+    dev = x.device
+    tc_path = nat.accumulate_path(engine.cov_code(cfg.cov_type), nat.BFLOAT16 if x.dtype == torch.bfloat16
+                                  else nat.FLOAT32, B, N, D, K) == 1
+    out = torch.empty((B, N, K), dtype=torch.float32, device=dev) if args.infer == "proba" else None
+    call = {"predict": lambda: engine.assign(cfg.cov_type, x, means, cov, weights),
+            "score": lambda: engine.score_samples(cfg.cov_type, x, means, cov, weights),
+            "proba": lambda: engine.predict_proba(cfg.cov_type, x, means, cov, weights, out=out)}[args.infer]
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in evs:
+        e0.record(stream)
+        call()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    rows = B * N
+    fe = {"spherical": D, "diag": 2 * D, "tied": D, "full": D + D * (D + 1) // 2}[cfg.cov_type]
+    flops = rows * 2.0 * K * fe  # the logits once (the algorithmic minimum, whatever the passes)
+    out_bytes = rows * {"predict": 8, "score": 4, "proba": 4 * K}[args.infer]
+    in_bytes = rows * D * x.element_size()
+    peaks = load_peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    gbs = (out_bytes + in_bytes) / (ms / 1e3) / 1e9
+    hbm = args.infer == "proba"
+    line = {
+        "metric": {"predict": "labels rows/s", "score": "score_samples rows/s", "proba": "predict_proba rows/s"}[
+            args.infer],
+        "value": rows / (ms / 1e3), "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(cfg, args),
+        "kernel": ("em_tc_diag_kernel, inference mode (tensor cores)" if cfg.cov_type == "diag" and tc_path
+                   else "rows_kernel (CUDA cores)"),
+        "roofline": {"bound": "hbm" if hbm else "tensor", "achieved": gbs if hbm else tflops,
+                     "peak": peaks["hbm_gbs"] if hbm else peaks["bf16"], "unit": "GB/s" if hbm else "TFLOP/s",
+                     "frac": (gbs / peaks["hbm_gbs"]) if hbm else (tflops / peaks["bf16"]),
+                     "peak_source": peaks["source"],
+                     "algorithmic_flops": flops, "bytes": out_bytes + in_bytes, "achieved_tflops": tflops},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(cfg, args):
     names = {0: "configs[0] spherical", 1: "configs[1] diag", 2: "configs[2] tied", 3: "configs[3] full",
              4: "configs[4] spherical large-K"}
@@ -193,6 +250,8 @@ def main():
                     help="rows of the cpu_baseline sample (about 10 s of host work for config 1)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--infer", choices=["predict", "score", "proba"], default=None,
+                    help="time an inference call (labels / score_samples / predict_proba) instead of EM")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -233,6 +292,11 @@ def main():
     means, cov, weights, _ = engine.initial_parameters(
         cfg.cov_type, x, cfg.K, torch.from_numpy(init_means), torch.from_numpy(init_cov),
         torch.from_numpy(init_w), 1e-6)
+    if args.infer:
+        if world > 1:
+            raise SystemExit("--infer runs on one GPU")
+        run_infer(args, cfg, x, means, cov, weights)
+        return
     ops = engine.CudaOps(cfg.cov_type, x, cfg.K)
     B, D, K = cfg.B, cfg.D, cfg.K
     stats = torch.zeros((B, K, ops.stat_width), dtype=torch.float32, device=dev)

@@ -104,6 +104,49 @@ RowArgs make_rows(int cov, int dt, const void* x, int64_t B, int64_t N, int64_t 
   return a;
 }
 
+// tensor-core launch block over the workspace buffers of layout L
+tc::TcLaunch make_tc(int cov, const void* x, int64_t N, int64_t D, int64_t K, const Layout& L, char* ws) {
+  tc::TcLaunch t{};
+  t.x = x;
+  t.N = N;
+  t.D = (int)D;
+  t.K = (int)K;
+  t.Kp_table = L.Kp;
+  t.Kp_part = (int64_t)L.tc_cluster * 128;  // per group for the grouped large-K path
+  t.F = stat_width(cov, (int)D);
+  t.cluster_size = L.tc_cluster;
+  t.nchunks = L.tc_chunks;
+  t.rowstat = L.tc_rowstat ? reinterpret_cast<float2*>(ws + L.tc_rowstat) : nullptr;
+  t.lse = L.tc_lse ? reinterpret_cast<float*>(ws + L.tc_lse) : nullptr;
+  t.wt = reinterpret_cast<const float*>(ws + L.wt);
+  t.cc = reinterpret_cast<const CompConst*>(ws + L.cc);
+  t.params = ws + L.tc_params;
+  t.consts = reinterpret_cast<float*>(ws + L.tc_consts);
+  t.part = reinterpret_cast<float*>(ws + L.tc_part);
+  t.part_ll = reinterpret_cast<double*>(ws + L.tc_part_ll);
+  t.status = reinterpret_cast<int*>(ws + L.status);
+  t.wait_ns = 2000000000ull;
+  return t;
+}
+
+// Inference on the diag tensor-core kernel (bf16 X, the EM kernel's shape
+// window): labels (mode 2), log-sum-exp (1) or responsibilities (3) in one
+// pass.  *done stays false when the call belongs to the CUDA-core kernels.
+int tc_infer(int cov, int dt, const void* x, int64_t N, int64_t D, int64_t K, const Layout& L, char* ws, int infer,
+             float* out_f, int64_t* out_i, cudaStream_t st, bool* done) {
+  *done = false;
+  const int km = kernel_mode();
+  if (cov != GMMXX_DIAG || dt != GMMXX_BFLOAT16 || L.tc_cluster == 0 || km == 1) return GMMXX_OK;
+  tc::TcLaunch t = make_tc(cov, x, N, D, K, L, ws);
+  t.infer = infer;
+  t.out_f = out_f;
+  t.out_i = out_i;
+  const int rc = tc::launch_em_tc(cov, t, st);
+  if (rc == GMMXX_ERR_UNSUPPORTED && km != 2) return GMMXX_OK;  // no co-resident cluster: CUDA cores
+  *done = true;
+  return rc;
+}
+
 int infer_common(int cov, int dt, const void* x, int64_t B, int64_t N, int64_t D, int64_t K, const float* means,
                  const float* covp, const float* weights, void* ws, size_t wsb, cudaStream_t st, Layout* L) {
   if (int rc = check_shape(cov, dt, B, N, D, K)) return rc;
@@ -200,25 +243,7 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
   if (mode == 2 && !tc_ok)
     return set_error(GMMXX_ERR_UNSUPPORTED, "tensor-core kernel required but the shape / dtype is outside its window");
   if (tc_ok && mode != 1) {
-    tc::TcLaunch t{};
-    t.x = x;
-    t.N = N;
-    t.D = (int)D;
-    t.K = (int)K;
-    t.Kp_table = L.Kp;
-    t.Kp_part = (int64_t)L.tc_cluster * 128;  // per group for the grouped large-K path
-    t.F = stat_width(cov_type, (int)D);
-    t.cluster_size = L.tc_cluster;
-    t.nchunks = L.tc_chunks;
-    t.rowstat = L.tc_rowstat ? reinterpret_cast<float2*>(ws + L.tc_rowstat) : nullptr;
-    t.lse = L.tc_lse ? reinterpret_cast<float*>(ws + L.tc_lse) : nullptr;
-    t.wt = reinterpret_cast<const float*>(ws + L.wt);
-    t.cc = reinterpret_cast<const CompConst*>(ws + L.cc);
-    t.params = ws + L.tc_params;
-    t.consts = reinterpret_cast<float*>(ws + L.tc_consts);
-    t.part = reinterpret_cast<float*>(ws + L.tc_part);
-    t.part_ll = reinterpret_cast<double*>(ws + L.tc_part_ll);
-    t.status = reinterpret_cast<int*>(ws + L.status);
+    tc::TcLaunch t = make_tc(cov_type, x, N, D, K, L, ws);
     t.stats = stats;
     t.ll = log_likelihood;
     {  // test hook: GMMXX_B200_TEST_STALL=1 makes the tensor-core kernel's bounded waits run out (100 ms)
@@ -284,6 +309,10 @@ int gmmxx_assign(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N,
   if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
     return rc;
   if (N > 0) GMMXX_REQUIRE(labels_out, "labels_out");
+  bool done = false;
+  const int rc = tc_infer(cov_type, x_dtype, x, N, D, K, L, static_cast<char*>(workspace), 2, nullptr, labels_out, st,
+                          &done);
+  if (done) return rc;
   RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, static_cast<char*>(workspace));
   a.labels = labels_out;
   return launch_rows(cov_type, MODE_ARGMAX, a, (int)B, st);
@@ -297,6 +326,10 @@ int gmmxx_logsumexp(int cov_type, int x_dtype, const void* x, int64_t B, int64_t
   if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
     return rc;
   if (N > 0) GMMXX_REQUIRE(lse_out, "lse_out");
+  bool done = false;
+  const int rc = tc_infer(cov_type, x_dtype, x, N, D, K, L, static_cast<char*>(workspace), 1, lse_out, nullptr, st,
+                          &done);
+  if (done) return rc;
   RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, static_cast<char*>(workspace));
   a.lse_out = lse_out;
   return launch_rows(cov_type, MODE_LSE, a, (int)B, st);
@@ -328,6 +361,9 @@ int gmmxx_predict_proba(int cov_type, int x_dtype, const void* x, int64_t B, int
     return rc;
   if (N > 0) GMMXX_REQUIRE(proba_out, "proba_out");
   char* ws = static_cast<char*>(workspace);
+  bool done = false;
+  const int rc = tc_infer(cov_type, x_dtype, x, N, D, K, L, ws, 3, proba_out, nullptr, st, &done);
+  if (done) return rc;
   RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
   a.lse_out = reinterpret_cast<float*>(ws + L.lse);
   if (int rc = launch_rows(cov_type, MODE_LSE, a, (int)B, st)) return rc;

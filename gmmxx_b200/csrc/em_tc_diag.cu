@@ -66,6 +66,8 @@ constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (
 constexpr int kMaxCluster = kMaxClusterDiag;
 
 enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpSoftmax0 = 6 };
+// EM statistics, or inference without the M-step (TcLaunch::infer)
+enum Mode { kModeEm = 0, kModeLse = 1, kModeArgmax = 2, kModeProba = 3 };
 constexpr int kThreads = (kWarpSoftmax0 + kSoftWarps) * 32;  // 22 warps, <= 88 registers each
 
 // shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
@@ -77,8 +79,8 @@ constexpr int kMSL = kMSH + kBlock;
 constexpr int kOnes = kMSL + kBlock;           // MN-major, column 0 = 1 (constant)
 constexpr int kR = kOnes + kBlock;             // R: two 64-component MN groups
 constexpr int kConsts = kR + 2 * kBlock;       // lz[128], c2[128]
-constexpr int kHalfX = kConsts + 2 * 128 * 4;  // [kSplit parts][128 rows] float2
-constexpr int kXch = kHalfX + kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
+constexpr int kHalfX = kConsts + 2 * 128 * 4;  // [2 slots][kSplit parts][128 rows] float2
+constexpr int kXch = kHalfX + 2 * kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
 __host__ __device__ constexpr int bars_off(int c) { return kXch + 2 * c * 128 * 8; }
 __host__ __device__ constexpr int red_off(int c) { return bars_off(c) + 192; }
 __host__ __device__ constexpr int smem_total(int c) { return bars_off(c) + 256; }
@@ -94,7 +96,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
 struct Bars {
   uint64_t params;
   uint64_t xfull;      // TMA: staging slot holds X(t)
-  uint64_t sempty;     // prep: staging slot read (4 warps)
+  uint64_t sempty;     // prep: staging slot read (128 threads)
   uint64_t mxfull;     // TMA: M-step stage holds X(t)
   uint64_t ffull;      // prep: E-step operand of tile t in tensor memory (4 warps)
   uint64_t mfull;      // prep: M-step stage holds [x | s_hi | s_lo] of tile t (4 warps)
@@ -125,8 +127,10 @@ __device__ __forceinline__ void square_split(uint32_t w, uint32_t& hi, uint32_t&
   lo = pack_bf16(s0 - bf16lo_to_f32(hi), s1 - bf16hi_to_f32(hi));
 }
 
+template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     em_tc_diag_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
+  constexpr bool kEm = kMode == kModeEm;
   extern __shared__ __align__(1024) char smem_raw[];
   char* sm = smem_raw;
   if ((smem_u32(smem_raw) & 1023u) != 0) {  // uniform across the grid: no CTA proceeds
@@ -151,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     mbar_init(&bars->params, 1);
     mbar_init(&bars->xfull, 1);
-    mbar_init(&bars->sempty, 4);
+    mbar_init(&bars->sempty, 128);
     mbar_init(&bars->mxfull, 1);
     mbar_init(&bars->sfull, 1);
     mbar_init(&bars->sfree, kSoftWarps);
@@ -232,8 +236,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(&bars->xfull, t & 1, abort, lim)) { ok = false; break; }
       uint32_t w[32];
       load_row(kStaging, w);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sempty);  // the TMA may refill the slot
       // the E-step of t-1 read the operand region: wait for its completion
       if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
       tmem_fence_after();
@@ -247,13 +249,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st16(tmem + lane_addr + kFCol + 64 + 16 * h, lo);
       }
       tmem_wait_st();
+      // the TMA may now refill the staging slot.  Every thread releases it
+      // itself, once its loaded words have been consumed (the tensor-memory
+      // stores above read them): an arrive right after the loads, or one lane's
+      // arrive after __syncwarp, let the next TMA copy (async proxy) overtake
+      // loads still in flight -- rows of the next tile then leaked into this
+      // one when the softmax ran slow (measured with predict_proba).
+      mbar_arrive(&bars->sempty);
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->ffull);
-      if (t >= 1 && !fill_mstage(t - 1)) { ok = false; break; }
+      if (kEm && t >= 1 && !fill_mstage(t - 1)) { ok = false; break; }
       if (*abort) { ok = false; break; }
     }
-    if (ok && T >= 1 && !fill_mstage(T - 1)) ok = false;
+    if (kEm && ok && T >= 1 && !fill_mstage(T - 1)) ok = false;
     if (!ok) set_abort(bars, a.status);
   } else if (warp == kWarpTma) {
     // ---------------- producer: weights once, then X tiles (staging slot and M-step stage) ----------------
@@ -281,9 +290,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(&bars->xfull, kBlock);
         tma_load_2d(sm + kStaging, &tmap, 0, row0(t), &bars->xfull);
         issued = t + 1;
-        if (t >= 1) ok = load_m(t - 1);
+        if (kEm && t >= 1) ok = load_m(t - 1);
       }
-      if (ok && T >= 1 && issued == T) ok = load_m(T - 1);
+      if (kEm && ok && T >= 1 && issued == T) ok = load_m(T - 1);
       if (!ok) set_abort(bars, a.status);
       // before the CTA can exit, every copy it started has landed (bounded,
       // also after an abort): the weights and the last load of each buffer
@@ -360,12 +369,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the prep's s_hi / s_lo), which M_hi(t+1) needs.  Queued behind E(t+2)
       // it would put an E-step, a TMA round trip and the stage refill into the
       // critical path of every tile.
-      if (ok && T > 0) ok = issue_e(0);
-      if (ok && T > 1) ok = issue_e(1);
-      for (int t = 0; ok && t < T; ++t) {
-        if (!issue_m(t, Hi{})) { ok = false; break; }
-        if (!issue_m(t, Lo{})) { ok = false; break; }
-        if (t + 2 < T && !issue_e(t + 2)) { ok = false; break; }
+      if constexpr (kEm) {
+        if (ok && T > 0) ok = issue_e(0);
+        if (ok && T > 1) ok = issue_e(1);
+        for (int t = 0; ok && t < T; ++t) {
+          if (!issue_m(t, Hi{})) { ok = false; break; }
+          if (!issue_m(t, Lo{})) { ok = false; break; }
+          if (t + 2 < T && !issue_e(t + 2)) { ok = false; break; }
+        }
+      } else {  // inference: E-steps only, each as soon as S is free
+        for (int t = 0; ok && t < T; ++t) ok = issue_e(t);
       }
       if (!ok) set_abort(bars, a.status);
       mma_commit(&bars->mdone);
@@ -401,114 +414,236 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&bars->rfull);
     };
     bool ok = true;
-    for (int t = 0; t < T; ++t) {
-      const int s = t & 1;
-      const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
-      const bool valid = grow < a.N;
-      if (!mbar_wait_warp(&bars->sfull, t & 1, abort, lim)) { ok = false; break; }
-      tmem_fence_after();
-      const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
-#pragma unroll
-      for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
-      tmem_wait_ld();
-      tmem_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sfree);
-      // logits (log2 units) min(lz - h S, c2), h = log2(e)/2, and this part's max
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int k4 = 0; k4 < kPart / 4; ++k4) {
-        const float4 vz = cz4[k4], vc = cc4[k4];
-        const float lz[4] = {vz.x, vz.y, vz.z, vz.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int k = 4 * k4 + j;
-          const float l = fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
-          p[k] = l;
-          mx[j] = fmaxf(mx[j], l);
+    if constexpr (kEm) {
+      for (int t = 0; t < T; ++t) {
+        const int s = t & 1;
+        const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
+        const bool valid = grow < a.N;
+        if (!mbar_wait_warp(&bars->sfull, t & 1, abort, lim)) { ok = false; break; }
+        tmem_fence_after();
+        const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
+  #pragma unroll
+        for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
+        tmem_wait_ld();
+        tmem_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->sfree);
+        // logits (log2 units) min(lz - h S, c2), h = log2(e)/2, and this part's max
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  #pragma unroll
+        for (int k4 = 0; k4 < kPart / 4; ++k4) {
+          const float4 vz = cz4[k4], vc = cc4[k4];
+          const float lz[4] = {vz.x, vz.y, vz.z, vz.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
+  #pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int k = 4 * k4 + j;
+            const float l = fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
+            p[k] = l;
+            mx[j] = fmaxf(mx[j], l);
+          }
         }
+        // residual part of the previous tile (the M-step's high part of t-1 ran meanwhile)
+        if (t >= 1) {
+          if (!mbar_wait_warp(&bars->rfree, 0u, abort, lim)) { ok = false; break; }  // M_hi(t-1)
+          store_r(lo);
+        }
+        const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        const float mref = (m == -INFINITY) ? 0.f : m;  // an all-padding part has p = 0
+        float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+  #pragma unroll
+        for (int k = 0; k < kPart; ++k) {
+          p[k] = ex2_approx(p[k] - mref);
+          sm4[k & 3] += p[k];
+        }
+        const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
+        // combine the parts of the row (slot t & 1: a part writes the slot of
+        // tile t+2 only after the barrier of tile t+1, which every other part
+        // passes after reading its entries of tile t)
+        float2* hxs = halfx + s * kSplit * 128;
+        hxs[qc * 128 + row] = make_float2(m, sum);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->hx[s]);
+        if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
+        float2 o[kSplit];
+  #pragma unroll
+        for (int q = 0; q < kSplit; ++q) o[q] = q == qc ? make_float2(m, sum) : hxs[q * 128 + row];
+        float mc = o[0].x;
+  #pragma unroll
+        for (int q = 1; q < kSplit; ++q) mc = fmaxf(mc, o[q].x);
+        // exponents <= 0 here; ex2.approx (relative error ~2^-22) flushes results
+        // below 2^-126, i.e. parts 2^126 times smaller than the row's largest.
+        // Every CTA owns at least one live component, so mc is finite.
+        float sc2 = 0.f;
+  #pragma unroll
+        for (int q = 0; q < kSplit; ++q) sc2 += o[q].y * ex2_approx(o[q].x - mc);
+        // exchange (max, sum) of this CTA's components with the cluster (part 0 sends)
+        if (qc == 0) {
+          if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
+  #pragma unroll
+          for (int q = 0; q < kMaxCluster; ++q)
+            if (q < nclus)
+              st_async_f2(map_shared(xch_mine + s * slot_stride, q), mc, sc2, map_shared(smem_u32(&bars->xch[s]), q));
+        }
+        if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
+        float2 e[kMaxCluster];
+  #pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q)
+          e[q] = q < nclus ? xch[(s * nclus + q) * 128 + row] : make_float2(-INFINITY, 0.f);
+        float M = e[0].x;
+  #pragma unroll
+        for (int q = 1; q < kMaxCluster; ++q) M = fmaxf(M, e[q].x);
+        float S = 0.f;
+  #pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q)
+          if (q < nclus) S += e[q].y * ex2_approx(e[q].x - M);
+        const float f = valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f;
+        // high part of tile t now (after the M-step's residual part of t-1);
+        // the residual words stay in registers for the next iteration
+        if (t >= 1 && !mbar_wait_warp(&bars->rfree, 1u, abort, lim)) { ok = false; break; }  // M_lo(t-1)
+  #pragma unroll
+        for (int c = 0; c < kPart / 8; ++c) {  // 8 components per 16-byte store
+          uint32_t hw[4];
+  #pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int k = 8 * c + 2 * i;
+            const float r0 = p[k] * f, r1 = p[k + 1] * f;
+            hw[i] = pack_bf16(r0, r1);
+            lo[4 * c + i] = pack_bf16(r0 - bf16lo_to_f32(hw[i]), r1 - bf16hi_to_f32(hw[i]));
+          }
+          *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)((rc0 + c) * 8))) =
+              make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->rfull);
+        if (valid && rank == 0 && qc == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
+        if (*abort) { ok = false; break; }
       }
-      // residual part of the previous tile (the M-step's high part of t-1 ran meanwhile)
-      if (t >= 1) {
-        if (!mbar_wait_warp(&bars->rfree, 0u, abort, lim)) { ok = false; break; }  // M_hi(t-1)
-        store_r(lo);
+      // the residual part of the last tile
+      if (ok && T >= 1) {
+        if (mbar_wait_warp(&bars->rfree, 0u, abort, lim)) store_r(lo);
+        else ok = false;
       }
-      const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      const float mref = (m == -INFINITY) ? 0.f : m;  // an all-padding part has p = 0
-      float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+    } else {
+      // inference: the logits and the row's cluster-wide reduction only
+      for (int t = 0; t < T; ++t) {
+        const int s = t & 1;
+        const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
+        const bool valid = grow < a.N;
+        if (!mbar_wait_warp(&bars->sfull, t & 1, abort, lim)) { ok = false; break; }
+        tmem_fence_after();
+        const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
 #pragma unroll
-      for (int k = 0; k < kPart; ++k) {
-        p[k] = ex2_approx(p[k] - mref);
-        sm4[k & 3] += p[k];
-      }
-      const float sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
-      // combine the parts of the row.  One buffer suffices: a part rewrites
-      // its entry for tile t+1 only after writing R_lo(t), which waits for
-      // M_hi(t), which waited for every other part's R_hi(t) -- and each part
-      // read this entry before writing R_hi(t).
-      halfx[qc * 128 + row] = make_float2(m, sum);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->hx[s]);
-      if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
-      float2 o[kSplit];
+        for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
+        tmem_wait_ld();
+        tmem_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->sfree);
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int q = 0; q < kSplit; ++q) o[q] = q == qc ? make_float2(m, sum) : halfx[q * 128 + row];
-      float mc = o[0].x;
+        for (int k4 = 0; k4 < kPart / 4; ++k4) {
+          const float4 vz = cz4[k4], vc = cc4[k4];
+          const float lz[4] = {vz.x, vz.y, vz.z, vz.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
 #pragma unroll
-      for (int q = 1; q < kSplit; ++q) mc = fmaxf(mc, o[q].x);
-      // exponents <= 0 here; ex2.approx (relative error ~2^-22) flushes results
-      // below 2^-126, i.e. parts 2^126 times smaller than the row's largest.
-      // Every CTA owns at least one live component, so mc is finite.
-      float sc2 = 0.f;
+          for (int j = 0; j < 4; ++j) {
+            const int k = 4 * k4 + j;
+            const float l = fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
+            p[k] = l;
+            mx[j] = fmaxf(mx[j], l);
+          }
+        }
+        float2* hxs = halfx + s * kSplit * 128;
+        const int comp0 = (int)rank * kKC + k0;  // global index of p[0]
+        float m = 0.f, sum = 0.f;
+        float2 mine;
+        if constexpr (kMode == kModeArgmax) {
+          // this part's largest logit and its first component (increasing k)
+          float bv = -INFINITY;
+          int bi = 0x7fffffff;
 #pragma unroll
-      for (int q = 0; q < kSplit; ++q) sc2 += o[q].y * ex2_approx(o[q].x - mc);
-      // exchange (max, sum) of this CTA's components with the cluster (part 0 sends)
-      if (qc == 0) {
-        if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
+          for (int k = 0; k < kPart; ++k)
+            if (p[k] > bv) { bv = p[k]; bi = comp0 + k; }
+          mine = make_float2(bv, __int_as_float(bi));
+        } else {
+          m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+          const float mref = (m == -INFINITY) ? 0.f : m;
+          float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int k = 0; k < kPart; ++k) {
+            p[k] = ex2_approx(p[k] - mref);
+            sm4[k & 3] += p[k];
+          }
+          sum = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
+          mine = make_float2(m, sum);
+        }
+        // combine the parts of the row (slot t & 1, as in the EM loop)
+        hxs[qc * 128 + row] = mine;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->hx[s]);
+        if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
+        float2 o[kSplit];
+#pragma unroll
+        for (int q = 0; q < kSplit; ++q) o[q] = q == qc ? mine : hxs[q * 128 + row];
+        float2 cta;
+        if constexpr (kMode == kModeArgmax) {
+          cta = o[0];  // parts in increasing component order: strictly larger wins
+#pragma unroll
+          for (int q = 1; q < kSplit; ++q)
+            if (o[q].x > cta.x) cta = o[q];
+        } else {
+          float mc = o[0].x;
+#pragma unroll
+          for (int q = 1; q < kSplit; ++q) mc = fmaxf(mc, o[q].x);
+          float sc2 = 0.f;
+#pragma unroll
+          for (int q = 0; q < kSplit; ++q) sc2 += o[q].y * ex2_approx(o[q].x - mc);
+          cta = make_float2(mc, sc2);
+        }
+        if (qc == 0) {
+          if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
+#pragma unroll
+          for (int q = 0; q < kMaxCluster; ++q)
+            if (q < nclus)
+              st_async_f2(map_shared(xch_mine + s * slot_stride, q), cta.x, cta.y, map_shared(smem_u32(&bars->xch[s]), q));
+        }
+        if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
+        float2 e[kMaxCluster];
 #pragma unroll
         for (int q = 0; q < kMaxCluster; ++q)
-          if (q < nclus)
-            st_async_f2(map_shared(xch_mine + s * slot_stride, q), mc, sc2, map_shared(smem_u32(&bars->xch[s]), q));
-      }
-      if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort, lim)) { ok = false; break; }
-      float2 e[kMaxCluster];
+          e[q] = q < nclus ? xch[(s * nclus + q) * 128 + row] : make_float2(-INFINITY, 0.f);
+        if constexpr (kMode == kModeArgmax) {
+          float2 best = e[0];  // ranks in increasing component order: strictly larger wins
 #pragma unroll
-      for (int q = 0; q < kMaxCluster; ++q)
-        e[q] = q < nclus ? xch[(s * nclus + q) * 128 + row] : make_float2(-INFINITY, 0.f);
-      float M = e[0].x;
+          for (int q = 1; q < kMaxCluster; ++q)
+            if (q < nclus && e[q].x > best.x) best = e[q];
+          if (valid && rank == 0 && qc == 0) a.out_i[grow] = (int64_t)__float_as_int(best.y);
+        } else {
+          float M = e[0].x;
 #pragma unroll
-      for (int q = 1; q < kMaxCluster; ++q) M = fmaxf(M, e[q].x);
-      float S = 0.f;
+          for (int q = 1; q < kMaxCluster; ++q) M = fmaxf(M, e[q].x);
+          float S = 0.f;
 #pragma unroll
-      for (int q = 0; q < kMaxCluster; ++q)
-        if (q < nclus) S += e[q].y * ex2_approx(e[q].x - M);
-      const float f = valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f;
-      // high part of tile t now (after the M-step's residual part of t-1);
-      // the residual words stay in registers for the next iteration
-      if (t >= 1 && !mbar_wait_warp(&bars->rfree, 1u, abort, lim)) { ok = false; break; }  // M_lo(t-1)
+          for (int q = 0; q < kMaxCluster; ++q)
+            if (q < nclus) S += e[q].y * ex2_approx(e[q].x - M);
+          if constexpr (kMode == kModeLse) {
+            if (valid && rank == 0 && qc == 0) a.out_f[grow] = (M + log2f(S)) * kLn2;
+          } else if (valid) {  // responsibilities of this part's components, fp32 [N][K]
+            const float f = ex2_approx(m - M) * __frcp_rn(S);
+            float* orow = a.out_f + grow * (int64_t)a.K + comp0;
+            if (a.out_vec && comp0 + kPart <= a.K) {
 #pragma unroll
-      for (int c = 0; c < kPart / 8; ++c) {  // 8 components per 16-byte store
-        uint32_t hw[4];
+              for (int c = 0; c < kPart / 4; ++c)
+                reinterpret_cast<float4*>(orow)[c] =
+                    make_float4(p[4 * c] * f, p[4 * c + 1] * f, p[4 * c + 2] * f, p[4 * c + 3] * f);
+            } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int k = 8 * c + 2 * i;
-          const float r0 = p[k] * f, r1 = p[k + 1] * f;
-          hw[i] = pack_bf16(r0, r1);
-          lo[4 * c + i] = pack_bf16(r0 - bf16lo_to_f32(hw[i]), r1 - bf16hi_to_f32(hw[i]));
+              for (int k = 0; k < kPart; ++k)
+                if (comp0 + k < a.K) orow[k] = p[k] * f;
+            }
+          }
         }
-        *reinterpret_cast<uint4*>(rg + sw128((uint32_t)row, (uint32_t)((rc0 + c) * 8))) =
-            make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        if (*abort) { ok = false; break; }
       }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->rfull);
-      if (valid && rank == 0 && qc == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
-      if (*abort) { ok = false; break; }
-    }
-    // the residual part of the last tile
-    if (ok && T >= 1) {
-      if (mbar_wait_warp(&bars->rfree, 0u, abort, lim)) store_r(lo);
-      else ok = false;
     }
     if (!ok) set_abort(bars, a.status);
     // ---------------- epilogue: statistics partials (all softmax warps) ----------------
@@ -519,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // columns, part 0 also n_k.
     if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 2 * lim)) set_abort(bars, a.status);
     tmem_fence_after();
-    {
+    if constexpr (kEm) {
       static_assert(kSplit == 4, "epilogue column split");
       const int comp = (int)rank * kKC + row;
       float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
@@ -549,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     tmem_fence_before();
-    if (qc == 0) {
+    if (kEm && qc == 0) {
       double* red = reinterpret_cast<double*>(sm + red_off(nclus));
       double v = ll_acc;
 #pragma unroll
@@ -567,17 +702,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // no CTA exits while a peer may still write into its shared memory
 }
 
-}  // namespace
-
-int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st) {
-  if (L.D != 64 || L.cluster_size < 1 || L.cluster_size > kMaxCluster)
-    return set_error(GMMXX_ERR_UNSUPPORTED, "diag tensor-core kernel: D = 64, K <= %d", 128 * kMaxCluster);
-  if (int rc = launch_tc_pack(GMMXX_DIAG, 1, L, st)) return rc;
-  CUtensorMap tmap;
-  if (int rc = make_x_tensor_map(L, &tmap)) return rc;
+template <int kMode>
+static int launch_mode(const TcLaunch& L, const CUtensorMap& tmap, cudaStream_t st, int* ncl_out) {
+  auto kern = em_tc_diag_kernel<kMode>;
   const int smem = smem_total(L.cluster_size);
   int ncl = 0;
-  if (int rc = clustered_launch((const void*)em_tc_diag_kernel, kThreads, smem, L, &ncl)) return rc;
+  if (int rc = clustered_launch((const void*)kern, kThreads, smem, L, &ncl)) return rc;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -602,8 +732,38 @@ int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st) {
   args.status = L.status;
   args.wait_ns = L.wait_ns ? L.wait_ns : 2000000000ull;
   args.test_stall = L.test_stall;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, em_tc_diag_kernel, tmap, args);
+  args.K = L.K;
+  args.out_f = L.out_f;
+  args.out_i = L.out_i;
+  args.out_vec = ((reinterpret_cast<uintptr_t>(L.out_f) & 15u) == 0 && (L.K & 3) == 0) ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_diag_kernel launch: %s", cudaGetErrorString(e));
+  *ncl_out = ncl;
+  return GMMXX_OK;
+}
+
+}  // namespace
+
+int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st) {
+  if (L.D != 64 || L.cluster_size < 1 || L.cluster_size > kMaxCluster)
+    return set_error(GMMXX_ERR_UNSUPPORTED, "diag tensor-core kernel: D = 64, K <= %d", 128 * kMaxCluster);
+  if (L.infer < 0 || L.infer > 3) return set_error(GMMXX_ERR_INVALID, "diag tensor-core kernel: mode %d", L.infer);
+  if ((L.infer == kModeLse || L.infer == kModeProba) && L.out_f == nullptr)
+    return set_error(GMMXX_ERR_INVALID, "diag tensor-core kernel: no output buffer");
+  if (L.infer == kModeArgmax && L.out_i == nullptr)
+    return set_error(GMMXX_ERR_INVALID, "diag tensor-core kernel: no label buffer");
+  if (int rc = launch_tc_pack(GMMXX_DIAG, 1, L, st)) return rc;
+  CUtensorMap tmap;
+  if (int rc = make_x_tensor_map(L, &tmap)) return rc;
+  int ncl = 0;
+  int rc = GMMXX_OK;
+  switch (L.infer) {
+    case kModeEm: rc = launch_mode<kModeEm>(L, tmap, st, &ncl); break;
+    case kModeLse: rc = launch_mode<kModeLse>(L, tmap, st, &ncl); break;
+    case kModeArgmax: rc = launch_mode<kModeArgmax>(L, tmap, st, &ncl); break;
+    default: rc = launch_mode<kModeProba>(L, tmap, st, &ncl); break;
+  }
+  if (rc != GMMXX_OK || L.infer != kModeEm) return rc;
   return launch_tc_reduce(L, ncl, st);
 }
 

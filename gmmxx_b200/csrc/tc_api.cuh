@@ -29,6 +29,11 @@ struct TcArgs {
   float2* rowstat;      // per-row (max, scaled sum) over this group (log2 units)
   uint64_t wait_ns;     // limit of every bounded wait (diag kernel)
   int test_stall;       // test hook (diag kernel): the producer issues no X loads
+  // inference modes of the diag kernel (TcLaunch::infer != 0)
+  int K;                // real component count (row stride of out_f for predict_proba)
+  float* out_f;         // [N] log-sum-exp (natural log) or [N][K] responsibilities
+  int64_t* out_i;       // [N] labels
+  int out_vec;          // out_f 16-byte aligned and K % 4 == 0: 16-byte stores allowed
 };
 
 struct TcLaunch {
@@ -53,6 +58,12 @@ struct TcLaunch {
   float* lse;        // [N]         (grouped large-K path)
   uint64_t wait_ns;  // bounded-wait limit (0: 2 s)
   int test_stall;    // GMMXX_B200_TEST_STALL=1: make the diag kernel's waits run out
+  // diag kernel only: 0 = EM statistics; inference without the M-step:
+  // 1 = per-row log-sum-exp into out_f, 2 = labels into out_i,
+  // 3 = responsibilities exp(logit - lse) into out_f [N][K]
+  int infer;
+  float* out_f;
+  int64_t* out_i;
 };
 
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st);

@@ -401,6 +401,21 @@ def _infer_args(cov_type, x, means, cov, weights):
     return covc, x, means, cov, weights, ws, (b, n, d, k)
 
 
+def _check_tc_infer(covc, x, ws, dims) -> None:
+    """After an inference call that ran on the diag tensor-core kernel (bf16
+    X in its shape window): read the workspace status word (one stream sync)
+    so that an expired bounded wait raises instead of leaving stale output."""
+    b, n, d, k = dims
+    if covc != nat.DIAG or x.dtype != torch.bfloat16 or nat.accumulate_path(covc, nat.BFLOAT16, b, n, d, k) != 1:
+        return
+    status = ctypes_int()
+    nat.call("gmmxx_workspace_status", ws.data_ptr(), status.ref(), _stream_ptr(x.device))
+    if status.value == nat.ERR_TIMEOUT:
+        raise nat.GmmxxError(status.value, "a bounded device-side wait expired in the inference kernel")
+    if status.value == nat.ERR_UNSUPPORTED:
+        raise nat.GmmxxError(status.value, "the inference kernel rejected its launch configuration on the device")
+
+
 def assign(cov_type, x, means, cov, weights) -> torch.Tensor:
     """(B, N) int64 labels (torch_fallback.py:780-965)."""
     covc, x, means, cov, weights, ws, (b, n, d, k) = _infer_args(cov_type, x, means, cov, weights)
@@ -409,6 +424,7 @@ def assign(cov_type, x, means, cov, weights) -> torch.Tensor:
         nat.call("gmmxx_assign", covc, _X_DTYPES[x.dtype], x.data_ptr(), b, n, d, k, means.data_ptr(),
                  cov.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
                  _stream_ptr(x.device))
+        _check_tc_infer(covc, x, ws, (b, n, d, k))
     return out
 
 
@@ -420,6 +436,7 @@ def score_samples(cov_type, x, means, cov, weights) -> torch.Tensor:
         nat.call("gmmxx_logsumexp", covc, _X_DTYPES[x.dtype], x.data_ptr(), b, n, d, k, means.data_ptr(),
                  cov.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
                  _stream_ptr(x.device))
+        _check_tc_infer(covc, x, ws, (b, n, d, k))
     return out
 
 
@@ -448,6 +465,7 @@ def predict_proba(cov_type, x, means, cov, weights, out: Optional[torch.Tensor] 
         nat.call("gmmxx_predict_proba", covc, _X_DTYPES[x.dtype], x.data_ptr(), b, n, d, k, means.data_ptr(),
                  cov.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
                  _stream_ptr(x.device))
+        _check_tc_infer(covc, x, ws, (b, n, d, k))
     return out
 
 

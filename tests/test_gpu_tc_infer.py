@@ -1,0 +1,104 @@
+"""Inference on the diag tensor-core kernel (bf16 X, D = 64, K <= 512, one
+pass per call): labels, score_samples and predict_proba against the numpy
+oracle of the reference's chunked torch functions
+(torch_fallback.py:824-871, 1011-1056, 1178-1237) and against the
+exact-fp32 CUDA-core kernels on the same inputs.
+
+Tolerances (bf16 X is exact; the logits carry fp32-equivalent weights and
+fp32 tensor-core accumulation): log-sum-exp within 2e-4 relative + 2e-3
+absolute of the oracle, responsibilities within 1e-4 absolute, labels equal
+on at least 99.9 % of rows (rows whose two best components tie to fp32
+rounding may flip)."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(seed, n, d, k):
+    rng = np.random.default_rng(seed)
+    mu = rng.normal(0, 3.0, (k, d))
+    var = np.exp(rng.uniform(np.log(0.1), np.log(4.0), (k, d)))
+    w = rng.dirichlet(np.full(k, 0.5))
+    z = rng.choice(k, n, p=w)
+    x = (mu[z] + np.sqrt(var[z]) * rng.standard_normal((n, d))).astype(np.float32)
+    xb = torch.from_numpy(x).to(torch.bfloat16)[None]
+    means = (mu + 0.2 * rng.standard_normal(mu.shape)).astype(np.float32)[None]
+    cov = (var * rng.uniform(0.8, 1.25, var.shape)).astype(np.float32)[None]
+    wts = (w / w.sum()).astype(np.float32)[None]
+    return xb, means, cov, wts
+
+
+def _infer(dev, xb, means, cov, wts, kernel):
+    from gmmxx_b200 import _native as nat
+    from gmmxx_b200 import engine
+
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    os.environ["GMMXX_B200_KERNEL"] = kernel
+    try:
+        x = xb.to(dev)
+        b, n, d = x.shape
+        path = nat.accumulate_path(nat.DIAG, nat.BFLOAT16, b, n, d, means.shape[1])
+        args = ("diag", x, t(means), t(cov), t(wts))
+        out = (engine.assign(*args).cpu().numpy(), engine.score_samples(*args).cpu().numpy(),
+               engine.predict_proba(*args).cpu().numpy())
+        torch.cuda.synchronize()
+        return path, out
+    finally:
+        os.environ.pop("GMMXX_B200_KERNEL", None)
+
+
+@pytest.mark.parametrize("n,k", [
+    (200_000, 512),   # config-1 shape, cluster of 4
+    (70_001, 300),    # ragged N, padded components, cluster of 3
+    (66_000, 333),    # K % 4 != 0: scalar stores of responsibilities
+    (65_536, 40),     # single-CTA cluster
+])
+def test_tc_inference_matches_oracle(cuda_device, n, k):
+    xb, means, cov, wts = _case(11 + k, n, 64, k)
+    path, (lab, lse, proba) = _infer(cuda_device, xb, means, cov, wts, "tc")
+    assert path == 1
+    x = xb.float().numpy()
+    ref_lab = oracle.assign("diag", x, means, cov, wts)
+    ref_lse = oracle.score_samples("diag", x, means, cov, wts)
+    assert lab.shape == ref_lab.shape and lab.dtype == np.int64
+    assert (lab == ref_lab).mean() >= 0.999
+    np.testing.assert_allclose(lse, ref_lse, rtol=2e-4, atol=2e-3)
+    assert proba.shape == (1, n, k)
+    # row sums are 1 and rows agree with the oracle's exp(logit - lse)
+    np.testing.assert_allclose(proba.sum(-1), 1.0, atol=1e-4)
+    sl = slice(0, 4096)
+    ref_p = oracle.predict_proba("diag", x[:, sl], means, cov, wts)
+    np.testing.assert_allclose(proba[:, sl], ref_p, atol=1e-4)
+
+
+def test_tc_inference_matches_cuda_cores(cuda_device):
+    xb, means, cov, wts = _case(5, 131_072, 64, 512)
+    p_tc, (lab_tc, lse_tc, pr_tc) = _infer(cuda_device, xb, means, cov, wts, "tc")
+    p_simt, (lab_s, lse_s, pr_s) = _infer(cuda_device, xb, means, cov, wts, "simt")
+    assert p_tc == 1 and p_simt == 0
+    assert (lab_tc == lab_s).mean() >= 0.999
+    np.testing.assert_allclose(lse_tc, lse_s, rtol=2e-4, atol=2e-3)
+    np.testing.assert_allclose(pr_tc, pr_s, atol=1e-4)
+
+
+def test_tc_inference_labels_first_of_equal_components(cuda_device):
+    """Two identical components: the argmax keeps the first (the reference's
+    strict '>' merge, torch_fallback.py:814-817) within a row part, across
+    parts of one CTA and across cluster ranks."""
+    xb, means, cov, wts = _case(3, 65_536, 64, 256)
+    pairs = ((5, 6), (40, 40 + 64), (20, 20 + 128))
+    for a, b in pairs:
+        means[0, b] = means[0, a]
+        cov[0, b] = cov[0, a]
+        wts[0, a] = wts[0, b] = 0.1
+    _, (lab, _, _) = _infer(cuda_device, xb, means, cov, wts, "tc")
+    for a, b in pairs:
+        assert (lab == a).any()
+        assert not (lab == b).any()
