@@ -218,6 +218,7 @@ def run_infer(args, cfg, x, means, cov, weights):
         "ms_per_step": ms, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
         "config": workload_config(cfg, args),
         "kernel": ("em_tc_diag_kernel, inference mode (tensor cores)" if cfg.cov_type == "diag" and tc_path
+                   else "em_tc_kernel, per-row inference passes (tensor cores)" if tc_path
                    else "rows_kernel (CUDA cores)"),
         "roofline": {"bound": "hbm" if hbm else "tensor", "achieved": gbs if hbm else tflops,
                      "peak": peaks["hbm_gbs"] if hbm else peaks["bf16"], "unit": "GB/s" if hbm else "TFLOP/s",

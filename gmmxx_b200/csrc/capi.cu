@@ -117,7 +117,8 @@ tc::TcLaunch make_tc(int cov, const void* x, int64_t N, int64_t D, int64_t K, co
   t.cluster_size = L.tc_cluster;
   t.nchunks = L.tc_chunks;
   t.rowstat = L.tc_rowstat ? reinterpret_cast<float2*>(ws + L.tc_rowstat) : nullptr;
-  t.lse = L.tc_lse ? reinterpret_cast<float*>(ws + L.tc_lse) : nullptr;
+  // the grouped path's per-row buffer, else the CUDA-core path's (N floats)
+  t.lse = reinterpret_cast<float*>(ws + (L.tc_lse ? L.tc_lse : L.lse));
   t.wt = reinterpret_cast<const float*>(ws + L.wt);
   t.cc = reinterpret_cast<const CompConst*>(ws + L.cc);
   t.params = ws + L.tc_params;
@@ -129,14 +130,16 @@ tc::TcLaunch make_tc(int cov, const void* x, int64_t N, int64_t D, int64_t K, co
   return t;
 }
 
-// Inference on the diag tensor-core kernel (bf16 X, the EM kernel's shape
-// window): labels (mode 2), log-sum-exp (1) or responsibilities (3) in one
-// pass.  *done stays false when the call belongs to the CUDA-core kernels.
+// Inference on the tensor-core kernels (bf16 X, the EM kernels' shape
+// windows): labels (mode 2), log-sum-exp (1) or responsibilities (3); diag
+// in one pass, spherical in per-row passes per 1024-component group.  *done
+// stays false when the call belongs to the CUDA-core kernels.
 int tc_infer(int cov, int dt, const void* x, int64_t N, int64_t D, int64_t K, const Layout& L, char* ws, int infer,
              float* out_f, int64_t* out_i, cudaStream_t st, bool* done) {
   *done = false;
   const int km = kernel_mode();
-  if (cov != GMMXX_DIAG || dt != GMMXX_BFLOAT16 || L.tc_cluster == 0 || km == 1) return GMMXX_OK;
+  if ((cov != GMMXX_DIAG && cov != GMMXX_SPHERICAL) || dt != GMMXX_BFLOAT16 || L.tc_cluster == 0 || km == 1)
+    return GMMXX_OK;
   tc::TcLaunch t = make_tc(cov, x, N, D, K, L, ws);
   t.infer = infer;
   t.out_f = out_f;

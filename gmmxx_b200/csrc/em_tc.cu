@@ -70,7 +70,12 @@ enum Warp { kWarpTma = 0, kWarpMma = 1, kWarpPrep0 = 2, kWarpSoftmax0 = 4 };
 // components, tc_lse_combine_kernel folds the groups into the row's
 // log-sum-exp, and kModeExtLse turns that into responsibilities and the
 // M-step statistics of the group's components.
-enum Mode { kModeFull = 0, kModeRowStat = 1, kModeExtLse = 2 };
+//
+// Inference (no M-step): kModeArgmax writes each row's (max logit, first
+// component) over the group (TcArgs::row_out chooses rowstat or the label),
+// kModeProba writes the responsibilities 2^(l - lse) of the group's
+// components as fp32 rows of K, from the log-sum-exp of a row-statistics pass.
+enum Mode { kModeFull = 0, kModeRowStat = 1, kModeExtLse = 2, kModeArgmax = 3, kModeProba = 4 };
 
 // Shared-memory carve-up (byte offsets from a 1024-aligned base).
 //   diag      : weights (a_j, v_j) | stages{X, SH} x2 | SL (single) | aux (constant)
@@ -141,6 +146,8 @@ template <int COV, int DB, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     em_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
   static_assert(MODE == kModeFull || COV == GMMXX_SPHERICAL, "grouped passes are spherical only");
+  // passes without an M-step: the stage is free after the E-step and the softmax
+  constexpr bool kEOnly = MODE == kModeRowStat || MODE == kModeArgmax || MODE == kModeProba;
   using C = Cfg<COV, DB>;
   // The dynamic block is the kernel's only shared memory, declared 1024-byte
   // aligned (the 128-byte swizzle atoms need it).  All shared pointers derive
@@ -219,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t >= 2 && !mbar_wait(&bars->fempty[s], ((t >> 1) - 1) & 1, abort)) { set_abort(bars, a.status); break; }
         // without an M-step the stage is free once the E-step read it; the
         // softmax must also have read the stage's |x|^2 entries (qbuf)
-        if (MODE == kModeRowStat && t >= 2 && !mbar_wait(&bars->sfree[s], ((t >> 1) - 1) & 1, abort)) {
+        if (kEOnly && t >= 2 && !mbar_wait(&bars->sfree[s], ((t >> 1) - 1) & 1, abort)) {
           set_abort(bars, a.status);
           break;
         }
@@ -317,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       using Hi = std::integral_constant<int, 0>;
       using Lo = std::integral_constant<int, 1>;
-      if constexpr (MODE == kModeRowStat) {
+      if constexpr (kEOnly) {
         for (int t = 0; ok && t < T; ++t) {
           if (!issue_e_main(t)) { ok = false; break; }
           mma_commit(&bars->fempty[t & 1]);  // no M-step: the stage is free after E(t)
@@ -470,6 +477,69 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      if constexpr (MODE == kModeArgmax) {
+        // this half's largest logit and its first component, then the row's
+        // over both halves and the cluster; halves and ranks are in increasing
+        // component order and only a strictly larger logit replaces the best
+        const int comp0 = chunk * kKC + k0;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int k = 0; k < kHalf; ++k)
+          if (p[k] > bv) { bv = p[k]; bi = comp0 + k; }
+        float2* hxs = halfx + s * 2 * 128;
+        hxs[hf * 128 + row] = make_float2(bv, __int_as_float(bi));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->hx[s]);
+        if (!mbar_wait_warp(&bars->hx[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        float2 best = hxs[row];
+        const float2 h1 = hxs[128 + row];
+        if (h1.x > best.x) best = h1;
+        if (hf == 0) {
+          if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[s], (uint32_t)(nclus * 128 * 8));
+#pragma unroll
+          for (int q = 0; q < C::kMaxCluster; ++q)
+            if (q < nclus)
+              st_async_f2(map_shared(xch_mine + s * slot_stride, q), best.x, best.y,
+                          map_shared(smem_u32(&bars->xch[s]), q));
+        }
+        if (!mbar_wait_warp(&bars->xch[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
+        float2 g = xch[(s * nclus) * 128 + row];
+#pragma unroll
+        for (int q = 1; q < C::kMaxCluster; ++q)
+          if (q < nclus) {
+            const float2 e = xch[(s * nclus + q) * 128 + row];
+            if (e.x > g.x) g = e;
+          }
+        if (valid && rank == 0 && hf == 0) {
+          if (a.row_out == 3) a.out_i[grow] = (int64_t)__float_as_int(g.y);
+          else a.rowstat[grow] = g;
+        }
+        if (*abort) break;
+        continue;
+      }
+      if constexpr (MODE == kModeProba) {
+        // responsibilities of this half's components from the row's
+        // log-sum-exp over all K (log2 units), written as fp32 rows of K
+        if (valid) {
+          const float lse = a.lse_in[grow];
+          const int comp0 = chunk * kKC + k0;
+          float* orow = a.out_f + grow * (int64_t)a.K + comp0;
+          if (a.out_vec && comp0 + kHalf <= a.K) {
+#pragma unroll
+            for (int c = 0; c < kHalf / 4; ++c)
+              reinterpret_cast<float4*>(orow)[c] =
+                  make_float4(ex2_approx(p[4 * c] - lse), ex2_approx(p[4 * c + 1] - lse),
+                              ex2_approx(p[4 * c + 2] - lse), ex2_approx(p[4 * c + 3] - lse));
+          } else {
+#pragma unroll
+            for (int k = 0; k < kHalf; ++k)
+              if (comp0 + k < a.K) orow[k] = ex2_approx(p[k] - lse);
+          }
+        }
+        if (*abort) break;
+        continue;
+      }
       float M = 0.f, S = 1.f, f = 0.f;
       if constexpr (MODE == kModeExtLse) {
         // responsibilities from the row's log-sum-exp over all K (log2 units)
@@ -521,7 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (q < nclus) S += e[q].y * exp2f(e[q].x - M);
       if constexpr (MODE == kModeRowStat) {
         // the row's (max, scaled sum) over this group's components; no R, no M-step
-        if (valid && rank == 0 && hf == 0) a.rowstat[grow] = make_float2(M, S);
+        if (valid && rank == 0 && hf == 0) {
+          if (a.row_out == 0) a.rowstat[grow] = make_float2(M, S);
+          else a.out_f[grow] = a.row_out == 1 ? (M + log2f(S)) * kLn2 : M + log2f(S);
+        }
         if (*abort) break;
         continue;
       }
@@ -567,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(&bars->mdone, 0, nullptr, 4000000000ull)) set_abort(bars, a.status);
       tmem_fence_after();
     }
-    if (hf == 0 && MODE != kModeRowStat) {
+    if (hf == 0 && !kEOnly) {
       const int comp = (int)rank * kKC + row;  // this thread's TMEM lane = component
       float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
       for (int c0 = 0; c0 < C::kFdm; c0 += 16) {
@@ -665,7 +738,8 @@ __global__ void tc_reduce_kernel(const float* part, const double* part_ll, int n
 // Grouped large-K path: each row's log-sum-exp over all groups (log2 units)
 // from the per-group (max, scaled sum), and one fixed-order log-likelihood
 // partial per block.
-__global__ void tc_lse_combine_kernel(const float2* rowstat, int groups, int64_t N, float* lse, double* ll_part) {
+__global__ void tc_lse_combine_kernel(const float2* rowstat, int groups, int64_t N, float* lse, double* ll_part,
+                                      float scale = 1.f) {
   double acc = 0.0;
   for (int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; n < N; n += (int64_t)gridDim.x * blockDim.x) {
     float M = -INFINITY;
@@ -676,9 +750,10 @@ __global__ void tc_lse_combine_kernel(const float2* rowstat, int groups, int64_t
       S += e.y * exp2f(e.x - M);
     }
     const float l2 = M + log2f(S);
-    lse[n] = l2;
+    lse[n] = scale == 1.f ? l2 : l2 * scale;
     acc += (double)l2 * (double)kLn2;
   }
+  if (ll_part == nullptr) return;
   __shared__ double red[32];
   acc = warp_sum_d(acc);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
@@ -687,6 +762,19 @@ __global__ void tc_lse_combine_kernel(const float2* rowstat, int groups, int64_t
     double s = 0.0;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
     ll_part[blockIdx.x] = s;
+  }
+}
+
+// Grouped inference: each row's label from the per-group (max logit, first
+// component), groups in increasing component order, strictly larger wins.
+__global__ void tc_argmax_combine_kernel(const float2* rowstat, int groups, int64_t N, int64_t* labels) {
+  for (int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; n < N; n += (int64_t)gridDim.x * blockDim.x) {
+    float2 best = rowstat[n];
+    for (int g = 1; g < groups; ++g) {
+      const float2 e = rowstat[(int64_t)g * N + n];
+      if (e.x > best.x) best = e;
+    }
+    labels[n] = (int64_t)__float_as_int(best.y);
   }
 }
 
@@ -786,7 +874,7 @@ int clustered_launch(const void* kern, int threads, int smem, const TcLaunch& L,
 // One clustered launch of em_tc_kernel over chunks [chunk0, chunk0 + csize).
 template <int COV, int DB, int MODE>
 static int launch_mode(const TcLaunch& L, int chunk0, int csize, const float* lse_in, float2* rowstat, int* ncl_out,
-                       cudaStream_t st) {
+                       cudaStream_t st, int row_out = 0) {
   using C = Cfg<COV, DB>;
   // the dynamic block is the kernel's only shared memory: <= 227 KB per CTA
   static_assert(C::total(C::kMaxCluster) <= 232448, "shared memory budget");
@@ -823,6 +911,11 @@ static int launch_mode(const TcLaunch& L, int chunk0, int csize, const float* ls
   args.chunk0 = chunk0;
   args.lse_in = lse_in;
   args.rowstat = rowstat;
+  args.K = L.K;
+  args.out_f = L.out_f;
+  args.out_i = L.out_i;
+  args.out_vec = ((reinterpret_cast<uintptr_t>(L.out_f) & 15u) == 0 && (L.K & 3) == 0) ? 1 : 0;
+  args.row_out = row_out;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_kernel launch: %s", cudaGetErrorString(e));
   *ncl_out = ncl;
@@ -873,8 +966,64 @@ static int launch_grouped(const TcLaunch& L, cudaStream_t st) {
   return GMMXX_OK;
 }
 
+// Spherical inference (TcLaunch::infer = 1 log-sum-exp, 2 labels, 3
+// responsibilities) in groups of up to 8 chunks: per-row passes without an
+// M-step, folded over the groups by the combine kernels.  One group writes
+// its rows' results directly (the label, the natural-log log-sum-exp, or
+// the log2 log-sum-exp that the responsibilities pass reads from L.lse).
+template <int DB>
+static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
+  if (L.infer < 1 || L.infer > 3) return set_error(GMMXX_ERR_INVALID, "tensor-core inference mode %d", L.infer);
+  if ((L.infer == 2 && L.out_i == nullptr) || (L.infer != 2 && L.out_f == nullptr))
+    return set_error(GMMXX_ERR_INVALID, "tensor-core inference: no output buffer");
+  const int groups = (L.nchunks + kMaxClusterSph - 1) / kMaxClusterSph;
+  if (groups > 1 && L.rowstat == nullptr) return set_error(GMMXX_ERR_WORKSPACE, "grouped pass buffers missing");
+  if (L.infer == 3 && L.lse == nullptr) return set_error(GMMXX_ERR_WORKSPACE, "per-row log-sum-exp buffer missing");
+  if (int rc = launch_tc_pack(GMMXX_SPHERICAL, DB, L, st)) return rc;
+  auto csz = [&](int g) { return std::min(kMaxClusterSph, L.nchunks - g * kMaxClusterSph); };
+  const int nb = std::min<int>(kMaxClusters, 148);
+  int ncl = 0;
+  if (L.infer == 2) {  // labels
+    if (groups == 1) return launch_mode<GMMXX_SPHERICAL, DB, kModeArgmax>(L, 0, csz(0), nullptr, nullptr, &ncl, st, 3);
+    for (int g = 0; g < groups; ++g)
+      if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeArgmax>(L, g * kMaxClusterSph, csz(g), nullptr,
+                                                                  L.rowstat + (int64_t)g * L.N, &ncl, st))
+        return rc;
+    tc_argmax_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.out_i);
+    return check_launch("tc_argmax_combine_kernel");
+  }
+  // each row's log-sum-exp over all K: natural log into out_f (score_samples),
+  // or log2 units into L.lse for the responsibilities pass
+  if (groups == 1) {
+    if (L.infer == 1) return launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(L, 0, csz(0), nullptr, nullptr, &ncl, st, 1);
+    TcLaunch Lq = L;
+    Lq.out_f = L.lse;
+    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(Lq, 0, csz(0), nullptr, nullptr, &ncl, st, 2)) return rc;
+  } else {
+    for (int g = 0; g < groups; ++g)
+      if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(L, g * kMaxClusterSph, csz(g), nullptr,
+                                                                   L.rowstat + (int64_t)g * L.N, &ncl, st))
+        return rc;
+    if (L.infer == 1) {
+      tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.out_f, nullptr, kLn2);
+      return check_launch("tc_lse_combine_kernel");
+    }
+    tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.lse, nullptr, 1.f);
+    if (int rc = check_launch("tc_lse_combine_kernel")) return rc;
+  }
+  for (int g = 0; g < groups; ++g)
+    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeProba>(L, g * kMaxClusterSph, csz(g), L.lse, nullptr, &ncl, st))
+      return rc;
+  return GMMXX_OK;
+}
+
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st) {
   if (cov == GMMXX_DIAG && L.D == 64 && L.cluster_size <= kMaxClusterDiag) return launch_em_tc_diag(L, st);
+  if (L.infer != 0) {
+    if (cov == GMMXX_SPHERICAL && L.D == 64) return launch_sph_infer<1>(L, st);
+    if (cov == GMMXX_SPHERICAL && L.D == 128) return launch_sph_infer<2>(L, st);
+    return set_error(GMMXX_ERR_UNSUPPORTED, "no tensor-core inference kernel for this shape");
+  }
   if (cov == GMMXX_SPHERICAL && L.nchunks > kMaxClusterSph) {
     if (L.rowstat == nullptr || L.lse == nullptr) return set_error(GMMXX_ERR_WORKSPACE, "grouped pass buffers missing");
     if (L.D == 64) return launch_grouped<1>(L, st);

@@ -34,6 +34,11 @@ struct TcArgs {
   float* out_f;         // [N] log-sum-exp (natural log) or [N][K] responsibilities
   int64_t* out_i;       // [N] labels
   int out_vec;          // out_f 16-byte aligned and K % 4 == 0: 16-byte stores allowed
+  // spherical per-row passes (row statistics / argmax): where the row's
+  // result goes -- 0: rowstat[row] (per-group partial), 1: out_f[row] =
+  // natural-log log-sum-exp, 2: out_f[row] = log-sum-exp in log2 units,
+  // 3: out_i[row] = label
+  int row_out;
 };
 
 struct TcLaunch {
@@ -55,7 +60,7 @@ struct TcLaunch {
   float* stats;
   double* ll;
   float2* rowstat;   // [groups][N] (grouped large-K path)
-  float* lse;        // [N]         (grouped large-K path)
+  float* lse;        // [N]         per-row log-sum-exp, log2 units (grouped path; spherical predict_proba)
   uint64_t wait_ns;  // bounded-wait limit (0: 2 s)
   int test_stall;    // GMMXX_B200_TEST_STALL=1: make the diag kernel's waits run out
   // diag kernel only: 0 = EM statistics; inference without the M-step:

@@ -402,11 +402,13 @@ def _infer_args(cov_type, x, means, cov, weights):
 
 
 def _check_tc_infer(covc, x, ws, dims) -> None:
-    """After an inference call that ran on the diag tensor-core kernel (bf16
-    X in its shape window): read the workspace status word (one stream sync)
-    so that an expired bounded wait raises instead of leaving stale output."""
+    """After an inference call that ran on a tensor-core kernel (diag or
+    spherical, bf16 X in its shape window): read the workspace status word
+    (one stream sync) so that an expired bounded wait raises instead of
+    leaving stale output."""
     b, n, d, k = dims
-    if covc != nat.DIAG or x.dtype != torch.bfloat16 or nat.accumulate_path(covc, nat.BFLOAT16, b, n, d, k) != 1:
+    if covc not in (nat.DIAG, nat.SPHERICAL) or x.dtype != torch.bfloat16 or \
+            nat.accumulate_path(covc, nat.BFLOAT16, b, n, d, k) != 1:
         return
     status = ctypes_int()
     nat.call("gmmxx_workspace_status", ws.data_ptr(), status.ref(), _stream_ptr(x.device))

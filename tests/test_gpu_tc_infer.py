@@ -1,8 +1,9 @@
-"""Inference on the diag tensor-core kernel (bf16 X, D = 64, K <= 512, one
-pass per call): labels, score_samples and predict_proba against the numpy
-oracle of the reference's chunked torch functions
-(torch_fallback.py:824-871, 1011-1056, 1178-1237) and against the
-exact-fp32 CUDA-core kernels on the same inputs.
+"""Inference on the tensor-core kernels (bf16 X): the diag kernel (D = 64,
+K <= 512, one pass per call) and the spherical kernel (D = 64 / 128, per-row
+passes per group of 1024 components): labels, score_samples and
+predict_proba against the numpy oracle of the reference's chunked torch
+functions (torch_fallback.py:780-821, 824-871, 983-1056, 1133-1237) and
+against the exact-fp32 CUDA-core kernels on the same inputs.
 
 Tolerances (bf16 X is exact; the logits carry fp32-equivalent weights and
 fp32 tensor-core accumulation): log-sum-exp within 2e-4 relative + 2e-3
@@ -21,21 +22,27 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-def _case(seed, n, d, k):
+def _case(seed, n, d, k, cov_type="diag"):
     rng = np.random.default_rng(seed)
-    mu = rng.normal(0, 3.0, (k, d))
-    var = np.exp(rng.uniform(np.log(0.1), np.log(4.0), (k, d)))
+    mu = rng.normal(0, 3.0 if cov_type == "diag" else 2.0, (k, d))
+    if cov_type == "diag":
+        var = np.exp(rng.uniform(np.log(0.1), np.log(4.0), (k, d)))
+    else:
+        var = np.repeat(rng.uniform(0.3, 1.5, (k, 1)) ** 2, d, 1)
     w = rng.dirichlet(np.full(k, 0.5))
     z = rng.choice(k, n, p=w)
     x = (mu[z] + np.sqrt(var[z]) * rng.standard_normal((n, d))).astype(np.float32)
     xb = torch.from_numpy(x).to(torch.bfloat16)[None]
     means = (mu + 0.2 * rng.standard_normal(mu.shape)).astype(np.float32)[None]
-    cov = (var * rng.uniform(0.8, 1.25, var.shape)).astype(np.float32)[None]
+    if cov_type == "diag":
+        cov = (var * rng.uniform(0.8, 1.25, var.shape)).astype(np.float32)[None]
+    else:
+        cov = (var[:, 0] * rng.uniform(0.8, 1.25, k)).astype(np.float32)[None]
     wts = (w / w.sum()).astype(np.float32)[None]
     return xb, means, cov, wts
 
 
-def _infer(dev, xb, means, cov, wts, kernel):
+def _infer(dev, xb, means, cov, wts, kernel, cov_type="diag"):
     from gmmxx_b200 import _native as nat
     from gmmxx_b200 import engine
 
@@ -44,8 +51,9 @@ def _infer(dev, xb, means, cov, wts, kernel):
     try:
         x = xb.to(dev)
         b, n, d = x.shape
-        path = nat.accumulate_path(nat.DIAG, nat.BFLOAT16, b, n, d, means.shape[1])
-        args = ("diag", x, t(means), t(cov), t(wts))
+        code = nat.DIAG if cov_type == "diag" else nat.SPHERICAL
+        path = nat.accumulate_path(code, nat.BFLOAT16, b, n, d, means.shape[1])
+        args = (cov_type, x, t(means), t(cov), t(wts))
         out = (engine.assign(*args).cpu().numpy(), engine.score_samples(*args).cpu().numpy(),
                engine.predict_proba(*args).cpu().numpy())
         torch.cuda.synchronize()
@@ -99,6 +107,59 @@ def test_tc_inference_labels_first_of_equal_components(cuda_device):
         cov[0, b] = cov[0, a]
         wts[0, a] = wts[0, b] = 0.1
     _, (lab, _, _) = _infer(cuda_device, xb, means, cov, wts, "tc")
+    for a, b in pairs:
+        assert (lab == a).any()
+        assert not (lab == b).any()
+
+
+@pytest.mark.parametrize("n,d,k", [
+    (100_000, 128, 256),   # one group of 2 chunks
+    (65_536, 64, 64),      # one CTA
+    (70_001, 128, 1024),   # one group of 8 chunks, ragged N
+    (66_000, 128, 2304),   # three groups (8, 8, 2 chunks): combine kernels
+    (65_536, 64, 1100),    # two groups, K % 4 == 0 but the last chunk padded
+])
+def test_tc_spherical_inference_matches_oracle(cuda_device, n, d, k):
+    xb, means, cov, wts = _case(21 + k + d, n, d, k, "spherical")
+    path, (lab, lse, proba) = _infer(cuda_device, xb, means, cov, wts, "tc", "spherical")
+    assert path == 1
+    x = xb.float().numpy()
+    ref_lab = oracle.assign("spherical", x, means, cov, wts)
+    ref_lse = oracle.score_samples("spherical", x, means, cov, wts)
+    assert lab.dtype == np.int64 and (lab == ref_lab).mean() >= 0.999
+    np.testing.assert_allclose(lse, ref_lse, rtol=2e-4, atol=2e-3)
+    assert proba.shape == (1, n, k)
+    np.testing.assert_allclose(proba.sum(-1), 1.0, atol=1e-4)
+    sl = slice(0, 2048)
+    np.testing.assert_allclose(proba[:, sl], oracle.predict_proba("spherical", x[:, sl], means, cov, wts), atol=1e-4)
+
+
+def test_tc_spherical_inference_matches_cuda_cores(cuda_device):
+    xb, means, cov, wts = _case(8, 65_536, 128, 2304, "spherical")
+    p_tc, (lab_tc, lse_tc, pr_tc) = _infer(cuda_device, xb, means, cov, wts, "tc", "spherical")
+    p_s, (lab_s, lse_s, pr_s) = _infer(cuda_device, xb, means, cov, wts, "simt", "spherical")
+    assert p_tc == 1 and p_s == 0
+    assert (lab_tc == lab_s).mean() >= 0.999
+    np.testing.assert_allclose(lse_tc, lse_s, rtol=2e-4, atol=2e-3)
+    np.testing.assert_allclose(pr_tc, pr_s, atol=1e-4)
+
+
+def test_tc_spherical_labels_first_of_equal_components(cuda_device):
+    """Identical components across halves, cluster ranks and groups: the
+    first one wins (torch_fallback.py:814-817)."""
+    xb, means, cov, wts = _case(4, 65_536, 64, 2304, "spherical")
+    counts = np.bincount(oracle.assign("spherical", xb.float().numpy(), means, cov, wts)[0], minlength=2304)
+    # the most populated component of a range, duplicated `offset` later
+    spans = ((0, 64, 64), (128, 256, 128), (256, 512, 1024), (1024, 1280, 512))
+    pairs = []
+    for lo, hi, offset in spans:
+        a = lo + int(np.argmax(counts[lo:hi]))
+        pairs.append((a, a + offset))
+    for a, b in pairs:
+        means[0, b] = means[0, a]
+        cov[0, b] = cov[0, a]
+        wts[0, b] = wts[0, a]
+    _, (lab, _, _) = _infer(cuda_device, xb, means, cov, wts, "tc", "spherical")
     for a, b in pairs:
         assert (lab == a).any()
         assert not (lab == b).any()
