@@ -56,7 +56,7 @@ def algorithmic_flops(cov: str, n: int, d: int, k: int) -> float:
 def launches_per_iteration(cfg, tc_path: bool) -> int:
     """Kernels of this library launched per EM iteration: prep_weights +
     prep_table (+ 2 Cholesky kernels for tied / full), the statistics kernels,
-    finalize.  Statistics: 3 (pack, tensor-core kernel, reduce; or rows, mstep,
+    finalize (per component, then per problem).  Statistics: 3 (pack, tensor-core kernel, reduce; or rows, mstep,
     reduce), and for spherical K > 1024 the grouped passes: pack, G row-partial
     launches, combine, log-likelihood sum, G x (M-step launch + reduce)."""
     prep = 2 + (2 if cfg.cov_type in ("tied", "full") else 0)
@@ -64,7 +64,7 @@ def launches_per_iteration(cfg, tc_path: bool) -> int:
     if tc_path and cfg.cov_type == "spherical" and cfg.K > 1024:
         groups = (((cfg.K + 127) // 128) + 7) // 8
         stats = 3 + 3 * groups
-    return prep + stats + 1
+    return prep + stats + 2
 
 
 def load_peaks():

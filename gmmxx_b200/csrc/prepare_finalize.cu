@@ -230,65 +230,82 @@ __global__ void prep_table_kernel(int K, int D, int64_t Kp, const float* means, 
 }
 
 // ---------------------------------------------------------------------------
-// finalize: one CTA per problem
+// finalize: one warp per component, then one CTA per problem
 // ---------------------------------------------------------------------------
+// M-step finalize, per component: one warp per component k (lanes over the
+// feature index), the same element arithmetic as the reference's finalize
+// (torch_fallback.py:2293-2305, 2654-2666, 3145-3162).  Weights are written
+// unnormalised; finalize_kernel renormalises them.
+template <int COV>
+__global__ void finalize_comp_kernel(int K, int D, int64_t n_total, const float* stats, float reg, float mw,
+                                     float* means, float* cov, float* weights) {
+  const int b = blockIdx.y;
+  const int k = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (k >= K) return;
+  const int FM = stat_width(COV, D);
+  const float* s = stats + ((int64_t)b * K + k) * FM;
+  const float nk = s[0];
+  const bool active = nk > mw;
+  const float nks = fmaxf(nk, mw);
+  float* mu = means + ((int64_t)b * K + k) * D;
+  if (active)
+    for (int d = lane; d < D; d += 32) mu[d] = s[1 + d] / nks;
+  if (COV == GMMXX_SPHERICAL) {
+    if (active && lane == 0) {
+      float msq = 0.f;  // sequential over d, as the means were formed
+      for (int d = 0; d < D; ++d) {
+        const float m = s[1 + d] / nks;
+        msq = fmaf(m, m, msq);
+      }
+      float v = fmaxf(s[1 + D] - nk * msq, 0.f) / (nks * (float)D);
+      cov[(int64_t)b * K + k] = fmaxf(v, reg);
+    }
+  } else if (COV == GMMXX_DIAG) {
+    if (active) {
+      float* vp = cov + ((int64_t)b * K + k) * D;
+      for (int d = lane; d < D; d += 32) {
+        const float m = s[1 + d] / nks;
+        vp[d] = fmaxf(s[1 + D + d] / nks - m * m, reg);
+      }
+    }
+  } else if (COV == GMMXX_FULL) {
+    if (active) {
+      float* cp = cov + ((int64_t)b * K + k) * D * D;
+      for (int i = 0; i < D; ++i) {
+        const float mi = s[1 + i] / nks;
+        const int p0 = i * D - i * (i - 1) / 2;  // packed index of (i, i)
+        for (int j = i + lane; j < D; j += 32) {
+          const float mj = s[1 + j] / nks;
+          float c = (s[1 + D + p0 + (j - i)] - nk * (mi * mj)) / nks;
+          c = 0.5f * (c + c);
+          if (i == j) c = c + reg;
+          cp[i * D + j] = c;
+          cp[j * D + i] = c;
+        }
+      }
+    }
+  }
+  if (lane == 0) weights[(int64_t)b * K + k] = fmaxf(nk / (float)n_total, mw);
+}
+
+// Per problem: weights renormalised, the tied covariance (from X^T X and
+// the new means), the lower bound.
 template <int COV>
 __global__ void finalize_kernel(int K, int D, int64_t n_total, int64_t B, const float* stats,
-                                const double* ll, const float* xx, float reg, float mw, float* means,
+                                const double* ll, const float* xx, float reg, float* means,
                                 float* cov, float* weights, float* lb_out) {
   __shared__ float red[32];
   const int b = blockIdx.x;
   const int FM = stat_width(COV, D);
   const float* st = stats + (int64_t)b * K * FM;
-  float* mub = means + (int64_t)b * K * D;
+  const float* mub = means + (int64_t)b * K * D;
   const float nf = (float)n_total;
   float wpart = 0.f;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    const float* s = st + (int64_t)k * FM;
-    const float nk = s[0];
-    const bool active = nk > mw;
-    const float nks = fmaxf(nk, mw);
-    float* mu = mub + (int64_t)k * D;
-    if (active)
-      for (int d = 0; d < D; ++d) mu[d] = s[1 + d] / nks;
-    if (COV == GMMXX_SPHERICAL) {
-      if (active) {
-        float msq = 0.f;
-        for (int d = 0; d < D; ++d) msq = fmaf(mu[d], mu[d], msq);
-        float v = fmaxf(s[1 + D] - nk * msq, 0.f) / (nks * (float)D);
-        v = fmaxf(v, reg);
-        cov[(int64_t)b * K + k] = v;
-      }
-    } else if (COV == GMMXX_DIAG) {
-      if (active) {
-        float* vp = cov + ((int64_t)b * K + k) * D;
-        for (int d = 0; d < D; ++d) {
-          const float second = s[1 + D + d] / nks;
-          vp[d] = fmaxf(second - mu[d] * mu[d], reg);
-        }
-      }
-    } else if (COV == GMMXX_FULL) {
-      if (active) {
-        float* cp = cov + ((int64_t)b * K + k) * D * D;
-        int p = 0;
-        for (int i = 0; i < D; ++i)
-          for (int j = i; j < D; ++j, ++p) {
-            float c = (s[1 + D + p] - nk * (mu[i] * mu[j])) / nks;
-            c = 0.5f * (c + c);
-            if (i == j) c = c + reg;
-            cp[i * D + j] = c;
-            cp[j * D + i] = c;
-          }
-      }
-    }
-    const float w = fmaxf(nk / nf, mw);
-    weights[(int64_t)b * K + k] = w;
-    wpart += w;
-  }
+  for (int k = threadIdx.x; k < K; k += blockDim.x) wpart += weights[(int64_t)b * K + k];
   const float wsum = block_sum<float>(wpart, red);
   for (int k = threadIdx.x; k < K; k += blockDim.x) weights[(int64_t)b * K + k] /= wsum;
   if (COV == GMMXX_TIED) {
-    __syncthreads();
     const float* xb = xx + (int64_t)b * D * D;
     float* cb = cov + (int64_t)b * D * D;
     for (int e = threadIdx.x; e < D * D; e += blockDim.x) {
@@ -365,18 +382,34 @@ int launch_prepare(int cov, int64_t B, int64_t D, int64_t K, float* means, float
 int launch_finalize(int cov, int64_t B, int64_t D, int64_t K, int64_t n_total, const float* stats,
                     const double* ll, const float* xx, float reg, float mw, float* means, float* covp,
                     float* weights, float* lb_out, cudaStream_t st) {
+  const dim3 cgrid((unsigned)ceil_div(K, 8), (unsigned)B);
   switch (cov) {
     case GMMXX_SPHERICAL:
-      finalize_kernel<GMMXX_SPHERICAL><<<(unsigned)B, 256, 0, st>>>((int)K, (int)D, n_total, B, stats, ll, xx, reg, mw, means, covp, weights, lb_out);
+      finalize_comp_kernel<GMMXX_SPHERICAL><<<cgrid, 256, 0, st>>>((int)K, (int)D, n_total, stats, reg, mw, means, covp, weights);
       break;
     case GMMXX_DIAG:
-      finalize_kernel<GMMXX_DIAG><<<(unsigned)B, 256, 0, st>>>((int)K, (int)D, n_total, B, stats, ll, xx, reg, mw, means, covp, weights, lb_out);
+      finalize_comp_kernel<GMMXX_DIAG><<<cgrid, 256, 0, st>>>((int)K, (int)D, n_total, stats, reg, mw, means, covp, weights);
       break;
     case GMMXX_TIED:
-      finalize_kernel<GMMXX_TIED><<<(unsigned)B, 256, 0, st>>>((int)K, (int)D, n_total, B, stats, ll, xx, reg, mw, means, covp, weights, lb_out);
+      finalize_comp_kernel<GMMXX_TIED><<<cgrid, 256, 0, st>>>((int)K, (int)D, n_total, stats, reg, mw, means, covp, weights);
       break;
     default:
-      finalize_kernel<GMMXX_FULL><<<(unsigned)B, 256, 0, st>>>((int)K, (int)D, n_total, B, stats, ll, xx, reg, mw, means, covp, weights, lb_out);
+      finalize_comp_kernel<GMMXX_FULL><<<cgrid, 256, 0, st>>>((int)K, (int)D, n_total, stats, reg, mw, means, covp, weights);
+      break;
+  }
+  if (int rc = check_launch("finalize_comp_kernel")) return rc;
+  switch (cov) {
+    case GMMXX_SPHERICAL:
+      finalize_kernel<GMMXX_SPHERICAL><<<(unsigned)B, 256, 0, st>>>((int)K, (int)D, n_total, B, stats, ll, xx, reg, means, covp, weights, lb_out);
+      break;
+    case GMMXX_DIAG:
+      finalize_kernel<GMMXX_DIAG><<<(unsigned)B, 256, 0, st>>>((int)K, (int)D, n_total, B, stats, ll, xx, reg, means, covp, weights, lb_out);
+      break;
+    case GMMXX_TIED:
+      finalize_kernel<GMMXX_TIED><<<(unsigned)B, 256, 0, st>>>((int)K, (int)D, n_total, B, stats, ll, xx, reg, means, covp, weights, lb_out);
+      break;
+    default:
+      finalize_kernel<GMMXX_FULL><<<(unsigned)B, 256, 0, st>>>((int)K, (int)D, n_total, B, stats, ll, xx, reg, means, covp, weights, lb_out);
       break;
   }
   return check_launch("finalize_kernel");
