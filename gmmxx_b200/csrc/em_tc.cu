@@ -1,6 +1,8 @@
 // em_tc.cu -- fused soft-EM statistics kernel on the 5th-generation tensor
 // cores (tcgen05 + TMEM + TMA) for bf16 X with spherical covariance
-// (D = 64 / 128, K <= 1024), B == 1, plus the host pieces every tensor-core
+// (D = 64 / 128; K <= 1024 in one pass, K <= 16384 in groups of 1024
+// components), B == 1, with E-step-only passes for inference (labels,
+// score_samples, predict_proba); plus the host pieces every tensor-core
 // kernel shares: the per-iteration weight-image packer, the tensor map of X,
 // the clustered launch and the fixed-order reduction of the partials.  The
 // diagonal-covariance kernel is em_tc_diag.cu.
@@ -53,7 +55,6 @@ constexpr int kBlock = 16384;     // one [128][64] bf16 swizzled block
 constexpr int kAuxBytes = 4096;   // [16][128] K-major aux operand (1, |x|^2 hi / lo)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (log2 units)
 
 // 2^x on the SFU (ex2.approx.ftz: ~2^-22 relative error, subnormal results flushed)
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -77,26 +78,29 @@ enum Warp { kWarpTma = 0, kWarpMma = 1, kWarpPrep0 = 2, kWarpSoftmax0 = 4 };
 // components as fp32 rows of K, from the log-sum-exp of a row-statistics pass.
 enum Mode { kModeFull = 0, kModeRowStat = 1, kModeExtLse = 2, kModeArgmax = 3, kModeProba = 4 };
 
-// Shared-memory carve-up (byte offsets from a 1024-aligned base).
-//   diag      : weights (a_j, v_j) | stages{X, SH} x2 | SL (single) | aux (constant)
-//   spherical : weights (a_j)      | stages{X, aux} x2
-//   then R (two 64-component MN groups), constants, q, exchange slots, barriers.
+// Weight images of both covariance types (built by tc_pack_kernel; the
+// diagonal kernel em_tc_diag.cu reads the diag ones), and the shared-memory
+// carve-up of em_tc_kernel (spherical), in byte offsets from a 1024-aligned
+// base: weights (a_j) | stages {X, aux} x2 | R (two 64-component MN groups) |
+// constants | q | row-half slots | exchange slots | barriers.
 template <int COV, int DB>
 struct Cfg {
   static constexpr int D = 64 * DB;
   static constexpr bool kDiag = (COV == GMMXX_DIAG);
-  static constexpr int kMaxCluster = kDiag ? kMaxClusterDiag : 8;  // cluster ranks (128 components each)
+  // weight blocks: a_j (x coefficient), for diag also v_j (x^2 coefficient)
   static constexpr int kParamBlocks = kDiag ? 2 * kNS * DB : kNS * DB;
   static constexpr int kParams = 0;
+  __host__ __device__ static constexpr int a_blk(int j, int db) { return kParams + (j * DB + db) * kBlock; }
+  __host__ __device__ static constexpr int v_blk(int j, int db) { return kParams + ((kNS + j) * DB + db) * kBlock; }
+  // em_tc_kernel (spherical)
+  static constexpr int kMaxCluster = 8;  // cluster ranks (128 components each)
   static constexpr int kStage0 = kParams + kParamBlocks * kBlock;
-  static constexpr int kStageBytes = kDiag ? 2 * DB * kBlock : DB * kBlock + kAuxBytes;
-  static constexpr int kSL = kStage0 + 2 * kStageBytes;               // diag only
-  static constexpr int kAuxConst = kSL + (kDiag ? DB * kBlock : 0);   // diag only
-  static constexpr int kR = kAuxConst + (kDiag ? kAuxBytes : 0);
+  static constexpr int kStageBytes = DB * kBlock + kAuxBytes;
+  static constexpr int kR = kStage0 + 2 * kStageBytes;
   static constexpr int kConsts = kR + 2 * kBlock;  // mpm[128], h[128], c2[128]
-  static constexpr int kQ = kConsts + 3 * 128 * 4; // q[2][128] (spherical)
-  static constexpr int kHalfX = kQ + (kDiag ? 0 : 2 * 128 * 4);  // [2 halves][128 rows] float2
-  static constexpr int kXch = kHalfX + 2 * 2 * 128 * 8;  // halfx: [tile parity][half][row] float2
+  static constexpr int kQ = kConsts + 3 * 128 * 4; // q[2][128]
+  static constexpr int kHalfX = kQ + 2 * 128 * 4;  // [tile parity][half][row] float2
+  static constexpr int kXch = kHalfX + 2 * 2 * 128 * 8;
   __host__ __device__ static constexpr int xch_bytes(int C) { return 2 * C * 128 * 8; }
   __host__ __device__ static constexpr int bars(int C) { return kXch + xch_bytes(C); }
   // barriers (< 192 B) and the epilogue's 4-double reduction slot share the last 256 B
@@ -104,25 +108,16 @@ struct Cfg {
   __host__ __device__ static constexpr int total(int C) { return bars(C) + 256; }
   // feature blocks of stage s (byte offsets)
   __host__ __device__ static constexpr int x_blk(int s, int db) { return kStage0 + s * kStageBytes + db * kBlock; }
-  __host__ __device__ static constexpr int sh_blk(int s, int db) { return kStage0 + s * kStageBytes + (DB + db) * kBlock; }
-  __host__ __device__ static constexpr int sl_blk(int db) { return kSL + db * kBlock; }
-  __host__ __device__ static constexpr int aux(int s) {
-    return kDiag ? kAuxConst : kStage0 + s * kStageBytes + DB * kBlock;
-  }
-  // weight blocks: a_j (x coefficient), v_j (x^2 coefficient, diag)
-  __host__ __device__ static constexpr int a_blk(int j, int db) { return kParams + (j * DB + db) * kBlock; }
-  __host__ __device__ static constexpr int v_blk(int j, int db) { return kParams + ((kNS + j) * DB + db) * kBlock; }
-  // M-step accumulator columns: [x (D) | x^2 (D, diag) | aux (16)]
-  static constexpr int kAuxCol = kDiag ? 2 * D : D;
+  __host__ __device__ static constexpr int aux(int s) { return kStage0 + s * kStageBytes + DB * kBlock; }
+  // M-step accumulator columns: [x (D) | aux (16)]
+  static constexpr int kAuxCol = D;
   static constexpr int kFdm = kAuxCol + 16;
 };
 
 struct Bars {  // lives in dynamic shared memory; see Cfg::bars / Cfg::red
   uint64_t params;
   uint64_t xfull[2];   // TMA: X tile landed
-  uint64_t fmain[2];   // prep: SH (diag) / |x|^2 (spherical) ready
-  uint64_t fl;         // prep: SL ready (diag)
-  uint64_t slfree;     // MMA: M-step high part done reading SL (diag)
+  uint64_t fmain[2];   // prep: |x|^2 (aux operand and q) ready
   uint64_t fempty[2];  // MMA: stage free for the next TMA
   uint64_t sfull[2];   // MMA: S tile complete
   uint64_t sfree[2];   // softmax: S tile consumed
@@ -145,7 +140,9 @@ __device__ __forceinline__ void set_abort(Bars* b, int* status) {
 template <int COV, int DB, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     em_tc_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
-  static_assert(MODE == kModeFull || COV == GMMXX_SPHERICAL, "grouped passes are spherical only");
+  // diagonal covariance has its own kernel (em_tc_diag.cu); Cfg<DIAG> only
+  // describes the weight images that tc_pack_kernel builds for it
+  static_assert(COV == GMMXX_SPHERICAL, "em_tc_kernel is the spherical kernel");
   // passes without an M-step: the stage is free after the E-step and the softmax
   constexpr bool kEOnly = MODE == kModeRowStat || MODE == kModeArgmax || MODE == kModeProba;
   using C = Cfg<COV, DB>;
@@ -186,8 +183,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->xch[i], 1);
       mbar_init(&bars->hx[i], 8);
     }
-    mbar_init(&bars->fl, 2);
-    mbar_init(&bars->slfree, 1);
     mbar_init(&bars->rfull, 8);
     mbar_init(&bars->rfree, 1);
     mbar_init(&bars->mdone, 1);
@@ -198,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // constants of this CTA's component chunk; constant rows of the aux operand(s)
   const int chunk = a.chunk0 + (int)rank;  // this CTA's 128-component chunk of K
   for (int i = tid; i < 3 * 128; i += kThreads) c_mpm[i] = a.consts[(int64_t)chunk * 3 * 128 + i];
-  for (int s = 0; s < (C::kDiag ? 1 : 2); ++s) {
+  for (int s = 0; s < 2; ++s) {
     char* aux = sm + C::aux(s);
     for (int i = tid; i < 16 * 128; i += kThreads) {
       const int n = i >> 7, r = i & 127;
@@ -239,9 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer (one thread) ----------------
     if (lane == 0) {
       const uint32_t id_e = idesc_bf16(128, kKC, 0, 0);
-      const uint32_t id_m = idesc_bf16(128, 64, 1, 1);
-      // x | s_hi (diag) or the DB column blocks of x (spherical) in one instruction
-      const uint32_t id_m2 = idesc_bf16(128, C::kDiag ? 128 : 64 * DB, 1, 1);
+      // the DB column blocks of x in one instruction
+      const uint32_t id_m2 = idesc_bf16(128, 64 * DB, 1, 1);
       const uint32_t id_aux = idesc_bf16(128, 16, 1, 0);
       const uint32_t base = smem_u32(sm);
       const uint32_t r_base = base + C::kR;
@@ -256,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc = 1;
         }
       };
-      // E-step, main part: x . a_j (+ s_hi . v_j for diag) into S[t & 1]
+      // E-step: x . a_j into S[t & 1]
       auto issue_e_main = [&](int t) -> bool {
         const int s = t & 1;
         if (!mbar_wait(&bars->fmain[s], (t >> 1) & 1, abort)) return false;
@@ -267,32 +261,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int db = 0; db < DB; ++db) {
 #pragma unroll
           for (int j = 0; j < kNS; ++j) block_mma(d, base + C::x_blk(s, db), base + C::a_blk(j, db), acc);
-          if (C::kDiag) {
-#pragma unroll
-            for (int j = 0; j < kNS; ++j) block_mma(d, base + C::sh_blk(s, db), base + C::v_blk(j, db), acc);
-          }
-        }
-        if (!C::kDiag) mma_commit(&bars->sfull[s]);
-        return true;
-      };
-      // E-step, residual part (diag): s_lo . v_0 + s_lo . v_1, then S[t & 1] is complete
-      auto issue_e_lo = [&](int t) -> bool {
-        const int s = t & 1;
-        if (!mbar_wait(&bars->fl, t & 1, abort)) return false;
-        tmem_fence_after();
-        const uint32_t d = tmem + (uint32_t)(s * kKC);
-        uint32_t acc = 1;
-        for (int db = 0; db < DB; ++db) {
-          block_mma(d, base + C::sl_blk(db), base + C::v_blk(0, db), acc);
-          block_mma(d, base + C::sl_blk(db), base + C::v_blk(1, db), acc);
         }
         mma_commit(&bars->sfull[s]);
         return true;
       };
       // M-step of tile t with R part PART (0 = high bf16 terms, 1 = residual).
-      // The feature blocks of a stage are adjacent 16 KB blocks ([x | s_hi] for
-      // diag, the DB column blocks of x for spherical), so one MN-major
-      // instruction of N = 128 covers them; PART is a template argument so
+      // The DB column blocks of x are adjacent 16 KB blocks of the stage, so
+      // one MN-major instruction covers them; PART is a template argument so
       // that the issue sequence carries no branches between instructions.
       auto issue_m = [&](int t, auto part_tag) -> bool {
         constexpr int part = decltype(part_tag)::value;
@@ -305,20 +280,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // 32 B / 2048 B per 4 steps (K-major aux)
         const uint64_t r0 = desc_mnmajor(r_base, kBlock);
         const uint64_t x0 = desc_mnmajor(base + C::x_blk(s, 0), kBlock);
-        const uint64_t sl0 = C::kDiag ? desc_mnmajor(base + C::sl_blk(0), kBlock) : 0;
         const uint64_t aux0 = desc_kmajor(base + C::aux(s));
-        static_assert(C::kDiag ? C::sh_blk(0, 0) == C::x_blk(0, 0) + kBlock : true, "x and s_hi blocks adjacent");
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // 16 rows per instruction
           const uint64_t step = (uint64_t)(ks * 128);  // 2048 B >> 4
           const uint64_t ra = r0 + step;
           const uint32_t acc = ks == 0 ? acc0 : 1u;
-          mma_bf16(tmem + kDmCol, ra, x0 + step, id_m2, acc);  // [x | s_hi] (diag) or x (spherical)
-          if constexpr (C::kDiag && part == 0) mma_bf16(tmem + kDmCol + C::D, ra, sl0 + step, id_m, 1u);
+          mma_bf16(tmem + kDmCol, ra, x0 + step, id_m2, acc);  // x
           mma_bf16(tmem + kDmCol + C::kAuxCol, ra, aux0 + (uint64_t)((ks >> 2) * 128 + (ks & 3) * 2), id_aux, acc);
         }
         mma_commit(&bars->rfree);
-        if constexpr (C::kDiag && part == 0) mma_commit(&bars->slfree);
         if constexpr (part == 1) mma_commit(&bars->fempty[s]);
         return true;
       };
@@ -330,12 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(&bars->fempty[t & 1]);  // no M-step: the stage is free after E(t)
         }
       } else {
-        if (ok && T > 0) ok = issue_e_main(0) && (!C::kDiag || issue_e_lo(0));
+        if (ok && T > 0) ok = issue_e_main(0);
         for (int t = 0; ok && t < T; ++t) {
-          const bool more = t + 1 < T;
-          if (more && !issue_e_main(t + 1)) { ok = false; break; }
+          if (t + 1 < T && !issue_e_main(t + 1)) { ok = false; break; }
           if (!issue_m(t, Hi{})) { ok = false; break; }
-          if (C::kDiag && more && !issue_e_lo(t + 1)) { ok = false; break; }
           if (!issue_m(t, Lo{})) { ok = false; break; }
         }
       }
@@ -348,79 +317,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < T; ++t) {
       const int s = t & 1;
       if (!mbar_wait_warp(&bars->xfull[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
-      if (C::kDiag) {
-        // x^2 = s_hi + s_lo exactly (bf16 x has 8 significant bits).  One pass
-        // writes SH (double-buffered) and keeps the s_lo words in registers
-        // until the single SL buffer is free.  The buffers share one swizzled
-        // layout, so the map is elementwise.
-        static_assert(!C::kDiag || DB == 1, "diag tensor-core path is D = 64");
-        constexpr int kPer = kBlock / 16 / 64;  // 16-byte chunks per prep thread
-        uint4 lo4[kPer];
-        const uint4* xs = reinterpret_cast<const uint4*>(sm + C::x_blk(s, 0));
-        uint4* sh = reinterpret_cast<uint4*>(sm + C::sh_blk(s, 0));
+      // |x|^2 per row (two threads per row), three bf16 terms q_0 + q_1 + q_2
+      // (24 significant bits) into the aux operand
+      char* aux = sm + C::aux(s);
+      const int r = ptid >> 1, hf = ptid & 1;
+      for (int rr = r; rr < kBM; rr += 32) {
+        float acc = 0.f;
+        for (int db = 0; db < DB; ++db)
+          for (int c = hf * 4; c < hf * 4 + 4; ++c) {
+            const uint4 v = *reinterpret_cast<const uint4*>(sm + C::x_blk(s, db) + rr * 128 + c * 16);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int i4 = 0; i4 < kPer; ++i4) {
-          const int c = ptid + 64 * i4;
-          const uint4 v = xs[c];
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-          uint32_t hi[4], lo[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
-            const float s0 = x0 * x0, s1 = x1 * x1;  // exact in fp32
-            hi[i] = pack_bf16(s0, s1);
-            lo[i] = pack_bf16(s0 - bf16lo_to_f32(hi[i]), s1 - bf16hi_to_f32(hi[i]));
-          }
-          sh[c] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          lo4[i4] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->fmain[s]);
-        // SL is single-buffered: wait until the previous tile's M-step high part read it
-        if (t >= 1 && !mbar_wait_warp(&bars->slfree, (t - 1) & 1, abort)) { set_abort(bars, a.status); break; }
-        uint4* sl = reinterpret_cast<uint4*>(sm + C::sl_blk(0));
-#pragma unroll
-        for (int i4 = 0; i4 < kPer; ++i4) sl[ptid + 64 * i4] = lo4[i4];
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->fl);
-        if (*abort) break;
-      } else {
-        // |x|^2 per row (two threads per row), three bf16 terms q_0 + q_1 + q_2
-        // (24 significant bits) into the aux operand
-        char* aux = sm + C::aux(s);
-        const int r = ptid >> 1, hf = ptid & 1;
-        for (int rr = r; rr < kBM; rr += 32) {
-          float acc = 0.f;
-          for (int db = 0; db < DB; ++db)
-            for (int c = hf * 4; c < hf * 4 + 4; ++c) {
-              const uint4 v = *reinterpret_cast<const uint4*>(sm + C::x_blk(s, db) + rr * 128 + c * 16);
-              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
-                acc = fmaf(x0, x0, acc);
-                acc = fmaf(x1, x1, acc);
-              }
-            }
-          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-          if (hf == 0) {
-            qbuf[s * 128 + rr] = acc;
-            char* blk = aux + (rr >> 6) * 2048;
-            float rem = acc;
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-              const __nv_bfloat16 qj = __float2bfloat16(rem);
-              *reinterpret_cast<__nv_bfloat16*>(blk + sw128(1 + j, rr & 63)) = qj;
-              rem -= __bfloat162float(qj);
+            for (int i = 0; i < 4; ++i) {
+              const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
+              acc = fmaf(x0, x0, acc);
+              acc = fmaf(x1, x1, acc);
             }
           }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        if (hf == 0) {
+          qbuf[s * 128 + rr] = acc;
+          char* blk = aux + (rr >> 6) * 2048;
+          float rem = acc;
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            const __nv_bfloat16 qj = __float2bfloat16(rem);
+            *reinterpret_cast<__nv_bfloat16*>(blk + sw128(1 + j, rr & 63)) = qj;
+            rem -= __bfloat162float(qj);
+          }
         }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->fmain[s]);
       }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->fmain[s]);
     }
   } else {
     // ---------------- softmax: 8 warps, two per TMEM lane quarter ----------------
@@ -448,29 +377,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC + k0);
       tmem_ld32(sc, p);
       tmem_ld32(sc + 32, p + 32);
-      float qn = 0.f;
-      if (!C::kDiag) {  // |x|^2 of this row (signalled by the prep warps before S was issued)
-        if (!mbar_wait_warp(&bars->fmain[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
-        qn = qbuf[s * 128 + row];
-      }
+      // |x|^2 of this row (signalled by the prep warps before S was issued)
+      if (!mbar_wait_warp(&bars->fmain[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
+      const float qn = qbuf[s * 128 + row];
       tmem_wait_ld();
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->sfree[s]);  // S(t) and this row's |x|^2 consumed
-      // logits (log2 units) and this half's row max; four independent chains.
-      // Diag components all have distance scale s = 1, so h = log2(e) / 2 is a
-      // constant and only mpm and c2 are read from shared memory.
+      // logits (log2 units) c2 - h max(|x|^2 + S + mpm, 0) and this half's row
+      // max; four independent chains
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int k4 = 0; k4 < kHalf / 4; ++k4) {
         const float4 vm = cm4[k4], vc = cc4[k4];
-        const float4 vh = C::kDiag ? make_float4(kHalfLog2e, kHalfLog2e, kHalfLog2e, kHalfLog2e) : ch4[k4];
+        const float4 vh = ch4[k4];
         const float mm[4] = {vm.x, vm.y, vm.z, vm.w}, hh[4] = {vh.x, vh.y, vh.z, vh.w},
                     cc[4] = {vc.x, vc.y, vc.z, vc.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int k = 4 * k4 + j;
-          const float dist = C::kDiag ? fmaxf(p[k] + mm[j], 0.f) : fmaxf(p[k] + (mm[j] + qn), 0.f);
+          const float dist = fmaxf(p[k] + (mm[j] + qn), 0.f);
           const float l = fmaf(-hh[j], dist, cc[j]);
           p[k] = l;
           mx[j] = fmaxf(mx[j], l);
@@ -650,9 +576,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 16 && c0 + j < C::kFdm; ++j) {
           const int col = c0 + j;
           if (col < C::D) out[1 + col] = v[j];                                  // sum r x
-          else if (C::kDiag && col < 2 * C::D) out[1 + col] = v[j];             // sum r x^2
           else if (col == C::kAuxCol) out[0] = v[j];                            // n_k
-          else if (!C::kDiag && col == C::kAuxCol + 1) out[1 + C::D] = v[j] + v[j + 1] + v[j + 2];  // sum r |x|^2
+          else if (col == C::kAuxCol + 1) out[1 + C::D] = v[j] + v[j + 1] + v[j + 2];  // sum r |x|^2
         }
       }
       tmem_fence_before();
