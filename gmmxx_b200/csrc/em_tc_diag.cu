@@ -108,6 +108,8 @@ struct Bars {
   uint64_t xch[2];     // cluster exchange of (row max, row sum)
   uint64_t hx[2];      // every part of the row wrote its (max, sum) (16 warps)
   uint64_t mdone;      // MMA: all MMAs complete
+  uint64_t pfull;      // predict_proba: the tile's rows staged in shared memory (16 warps)
+  uint64_t pfree;      // predict_proba: the staged rows stored to global memory (16 warps)
   uint32_t tmem_base;
   int abort;
 };
@@ -169,6 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->rfull, kSoftWarps);
     mbar_init(&bars->rfree, 1);
     mbar_init(&bars->mdone, 1);
+    mbar_init(&bars->pfull, kSoftWarps);
+    mbar_init(&bars->pfree, kSoftWarps);
     bars->abort = 0;
     fence_barrier_init();
   }
@@ -627,19 +631,50 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (q < nclus) S += e[q].y * ex2_approx(e[q].x - M);
           if constexpr (kMode == kModeLse) {
             if (valid && rank == 0 && qc == 0) a.out_f[grow] = (M + log2f(S)) * kLn2;
-          } else if (valid) {  // responsibilities of this part's components, fp32 [N][K]
+          } else if (a.out_vec) {
+            // responsibilities, fp32 [N][K]: the tile's rows are staged in the
+            // (here unused) M-step stage, [128 rows][128 components] with the
+            // 16-byte chunks of a row permuted by row & 7, then every warp
+            // stores 8 whole rows of this CTA's components as 512-byte runs
+            const float f = valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f;
+            float* stg = reinterpret_cast<float*>(sm + kMX);
+            if (t >= 1 && !mbar_wait_warp(&bars->pfree, (t - 1) & 1, abort, lim)) { ok = false; break; }
+#pragma unroll
+            for (int c = 0; c < kPart / 4; ++c) {
+              const int pos = ((k0 >> 2) + c) ^ (row & 7);
+              *reinterpret_cast<float4*>(stg + row * kKC + pos * 4) =
+                  make_float4(p[4 * c] * f, p[4 * c + 1] * f, p[4 * c + 2] * f, p[4 * c + 3] * f);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->pfull);
+            if (!mbar_wait_warp(&bars->pfull, t & 1, abort, lim)) { ok = false; break; }
+            const int sw = warp - kWarpSoftmax0;
+            const int comp = (int)rank * kKC + 4 * lane;
+#pragma unroll 2
+            for (int i = 0; i < kBM / kSoftWarps; ++i) {
+              const int r = sw * (kBM / kSoftWarps) + i;
+              const int64_t gr = (cid + (int64_t)t * ncl) * kBM + r;
+              const float4 v = *reinterpret_cast<const float4*>(stg + r * kKC + ((lane ^ (r & 7)) * 4));
+              if (gr < a.N) {
+                float* o = a.out_f + gr * (int64_t)a.K + comp;
+                if (comp + 3 < a.K) {
+                  *reinterpret_cast<float4*>(o) = v;
+                } else {
+                  if (comp < a.K) o[0] = v.x;
+                  if (comp + 1 < a.K) o[1] = v.y;
+                  if (comp + 2 < a.K) o[2] = v.z;
+                }
+              }
+            }
+            // the staged values went into the stores above: the stage is free
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->pfree);
+          } else if (valid) {  // unaligned output or K % 4 != 0: this thread's components
             const float f = ex2_approx(m - M) * __frcp_rn(S);
             float* orow = a.out_f + grow * (int64_t)a.K + comp0;
-            if (a.out_vec && comp0 + kPart <= a.K) {
 #pragma unroll
-              for (int c = 0; c < kPart / 4; ++c)
-                reinterpret_cast<float4*>(orow)[c] =
-                    make_float4(p[4 * c] * f, p[4 * c + 1] * f, p[4 * c + 2] * f, p[4 * c + 3] * f);
-            } else {
-#pragma unroll
-              for (int k = 0; k < kPart; ++k)
-                if (comp0 + k < a.K) orow[k] = p[k] * f;
-            }
+            for (int k = 0; k < kPart; ++k)
+              if (comp0 + k < a.K) orow[k] = p[k] * f;
           }
         }
         if (*abort) { ok = false; break; }
