@@ -163,3 +163,26 @@ def test_tc_spherical_labels_first_of_equal_components(cuda_device):
     for a, b in pairs:
         assert (lab == a).any()
         assert not (lab == b).any()
+
+
+@pytest.mark.parametrize("cov_type,d,k", [("diag", 64, 512), ("spherical", 128, 1100)])
+def test_tc_predict_proba_unaligned_output(cuda_device, cov_type, d, k):
+    """predict_proba into a caller buffer that starts 4 bytes off a 16-byte
+    boundary: the kernels take their per-element store path (the host checks
+    the alignment before allowing 16-byte stores) and agree with an aligned
+    call bit for bit."""
+    from gmmxx_b200 import engine
+
+    xb, means, cov, wts = _case(31, 65_536, d, k, cov_type)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    x = xb.to(cuda_device)
+    args = (cov_type, x, t(means), t(cov), t(wts))
+    n = x.shape[1]
+    buf = torch.full((n * k + 1,), -1.0, dtype=torch.float32, device=cuda_device)
+    out = buf[1:].view(1, n, k)
+    assert out.data_ptr() % 16 != 0
+    got = engine.predict_proba(*args, out=out)
+    ref = engine.predict_proba(*args)
+    torch.cuda.synchronize()
+    assert buf[0].item() == -1.0  # nothing written before the view
+    assert torch.equal(got, ref)
