@@ -1,5 +1,7 @@
 // em_tc_diag.cu -- fused soft-EM statistics for diagonal covariance on the
-// 5th-generation tensor cores, bf16 X, D = 64, K <= 512, B == 1.
+// 5th-generation tensor cores, bf16 X, D = 64, K <= 512, B == 1; the same
+// kernel without the M-step computes labels, per-row log-sum-exp or the
+// responsibilities (the inference modes, see Mode below).
 //
 // A thread-block cluster of C = ceil(K / 128) CTAs works on one 128-row tile
 // of X at a time; CTA `rank` owns components [128 rank, 128 rank + 128) whose
@@ -20,11 +22,12 @@
 //             one N = 208 instruction per 16 rows and R part (the four
 //             operand groups sit 16 KB apart; the last is a constant ones block)
 //
-// The E-step of tile t+1 therefore depends only on X(t+1) and on the E-step
-// of tile t (tensor-memory operand), never on the M-step buffers, and the
-// softmax warps are software-pipelined: the residual part r_lo of tile t-1
-// is written after the logits of tile t, so the wait for the M-step's high
-// part overlaps useful work.
+// The E-step of tile t+1 therefore depends only on X(t+1), on the E-step of
+// tile t (the tensor-memory operand) and on the softmax having loaded S(t)
+// (one logit slot), never on the M-step buffers; and the softmax warps are
+// software-pipelined: the residual part r_lo of tile t-1 is written after
+// the logits of tile t, so the wait for the M-step's high part overlaps
+// useful work.
 //
 // Precision as in em_tc.cu: X exact in bf16, x^2 split exactly into two bf16
 // terms, weights into three (24 significant bits), r into two; products exact,
@@ -74,6 +77,7 @@ constexpr int kThreads = (kWarpSoftmax0 + kSoftWarps) * 32;  // 22 warps, <= 88 
 constexpr int kParams = 0;                     // a_0 a_1 a_2 | v_0 v_1 v_2 (16 KB each)
 constexpr int kStaging = kParams + 2 * kNS * kBlock;  // X staging slot
 constexpr int kMX = kStaging + kBlock;         // M-step stage: x | s_hi | s_lo | ones
+                                               // (predict_proba: the tile's fp32 rows)
 constexpr int kMSH = kMX + kBlock;
 constexpr int kMSL = kMSH + kBlock;
 constexpr int kOnes = kMSL + kBlock;           // MN-major, column 0 = 1 (constant)
