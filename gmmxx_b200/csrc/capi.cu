@@ -132,7 +132,7 @@ tc::TcLaunch make_tc(int cov, const void* x, int64_t N, int64_t D, int64_t K, co
 
 // Inference on the tensor-core kernels (bf16 X, the EM kernels' shape
 // windows): labels (mode 2), log-sum-exp (1) or responsibilities (3); diag
-// in one pass, spherical in per-row passes per 1024-component group.  *done
+// in one pass, spherical in per-row passes per group of components.  *done
 // stays false when the call belongs to the CUDA-core kernels.
 int tc_infer(int cov, int dt, const void* x, int64_t N, int64_t D, int64_t K, const Layout& L, char* ws, int infer,
              float* out_f, int64_t* out_i, cudaStream_t st, bool* done) {

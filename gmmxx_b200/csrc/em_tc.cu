@@ -1,6 +1,6 @@
 // em_tc.cu -- fused soft-EM statistics kernel on the 5th-generation tensor
 // cores (tcgen05 + TMEM + TMA) for bf16 X with spherical covariance
-// (D = 64 / 128; K <= 1024 in one pass, K <= 16384 in groups of 1024
+// (D = 64 / 128; K <= 1024 in one pass, K <= 16384 in groups of 512
 // components), B == 1, with E-step-only passes for inference (labels,
 // score_samples, predict_proba); plus the host pieces every tensor-core
 // kernel shares: the per-iteration weight-image packer, the tensor map of X,
@@ -66,7 +66,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
 enum Warp { kWarpTma = 0, kWarpMma = 1, kWarpPrep0 = 2, kWarpSoftmax0 = 4 };
 
 // Launch modes.  kModeFull: the whole of K in one cluster (K <= 1024).
-// Large K runs as groups of 8 chunks (1024 components) in two passes:
+// Large K runs as groups of kGroupChunks chunks (512 components) in two passes:
 // kModeRowStat writes each row's (max, scaled sum) over the group's
 // components, tc_lse_combine_kernel folds the groups into the row's
 // log-sum-exp, and kModeExtLse turns that into responsibilities and the
@@ -856,18 +856,19 @@ static int launch_t(const TcLaunch& L, cudaStream_t st) {
   return launch_tc_reduce(L, ncl, st);
 }
 
-// Spherical K > 1024: groups of 8 chunks (1024 components).  Pass 1 writes
+// Spherical K > 1024: groups of kGroupChunks chunks (512 components).  Pass 1 writes
 // each row's (max, sum) per group; the combine folds them into the row's
 // log-sum-exp and the log-likelihood; pass 2 forms the responsibilities of
 // each group's components from it and accumulates their statistics.
 template <int DB>
 static int launch_grouped(const TcLaunch& L, cudaStream_t st) {
   if (int rc = launch_tc_pack(GMMXX_SPHERICAL, DB, L, st)) return rc;
-  const int groups = (L.nchunks + kMaxClusterSph - 1) / kMaxClusterSph;
+  const int gc = tc_group_chunks(L.K);
+  const int groups = (L.nchunks + gc - 1) / gc;
   int ncl = 0;
   for (int g = 0; g < groups; ++g) {
-    const int csize = std::min(kMaxClusterSph, L.nchunks - g * kMaxClusterSph);
-    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(L, g * kMaxClusterSph, csize, nullptr,
+    const int csize = std::min(gc, L.nchunks - g * gc);
+    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(L, g * gc, csize, nullptr,
                                                                  L.rowstat + (int64_t)g * L.N, &ncl, st))
       return rc;
   }
@@ -877,13 +878,13 @@ static int launch_grouped(const TcLaunch& L, cudaStream_t st) {
   tc_ll_sum_kernel<<<1, 32, 0, st>>>(L.part_ll, nb, L.ll);
   if (int rc = check_launch("tc_ll_sum_kernel")) return rc;
   for (int g = 0; g < groups; ++g) {
-    const int csize = std::min(kMaxClusterSph, L.nchunks - g * kMaxClusterSph);
-    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeExtLse>(L, g * kMaxClusterSph, csize, L.lse, nullptr, &ncl, st))
+    const int csize = std::min(gc, L.nchunks - g * gc);
+    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeExtLse>(L, g * gc, csize, L.lse, nullptr, &ncl, st))
       return rc;
     TcLaunch Lg = L;  // statistics rows of this group's components
-    const int k0 = g * kMaxClusterSph * kKC;
+    const int k0 = g * gc * kKC;
     Lg.stats = L.stats + (int64_t)k0 * L.F;
-    Lg.K = std::min(kMaxClusterSph * kKC, L.K - k0);
+    Lg.K = std::min(gc * kKC, L.K - k0);
     Lg.Kp_part = (int64_t)csize * kKC;
     Lg.ll = nullptr;
     if (int rc = launch_tc_reduce(Lg, ncl, st)) return rc;
@@ -901,17 +902,18 @@ static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
   if (L.infer < 1 || L.infer > 3) return set_error(GMMXX_ERR_INVALID, "tensor-core inference mode %d", L.infer);
   if ((L.infer == 2 && L.out_i == nullptr) || (L.infer != 2 && L.out_f == nullptr))
     return set_error(GMMXX_ERR_INVALID, "tensor-core inference: no output buffer");
-  const int groups = (L.nchunks + kMaxClusterSph - 1) / kMaxClusterSph;
+  const int gc = tc_group_chunks(L.K);
+  const int groups = (L.nchunks + gc - 1) / gc;
   if (groups > 1 && L.rowstat == nullptr) return set_error(GMMXX_ERR_WORKSPACE, "grouped pass buffers missing");
   if (L.infer == 3 && L.lse == nullptr) return set_error(GMMXX_ERR_WORKSPACE, "per-row log-sum-exp buffer missing");
   if (int rc = launch_tc_pack(GMMXX_SPHERICAL, DB, L, st)) return rc;
-  auto csz = [&](int g) { return std::min(kMaxClusterSph, L.nchunks - g * kMaxClusterSph); };
+  auto csz = [&](int g) { return std::min(gc, L.nchunks - g * gc); };
   const int nb = std::min<int>(kMaxClusters, 148);
   int ncl = 0;
   if (L.infer == 2) {  // labels
     if (groups == 1) return launch_mode<GMMXX_SPHERICAL, DB, kModeArgmax>(L, 0, csz(0), nullptr, nullptr, &ncl, st, 3);
     for (int g = 0; g < groups; ++g)
-      if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeArgmax>(L, g * kMaxClusterSph, csz(g), nullptr,
+      if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeArgmax>(L, g * gc, csz(g), nullptr,
                                                                   L.rowstat + (int64_t)g * L.N, &ncl, st))
         return rc;
     tc_argmax_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.out_i);
@@ -926,7 +928,7 @@ static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
     if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(Lq, 0, csz(0), nullptr, nullptr, &ncl, st, 2)) return rc;
   } else {
     for (int g = 0; g < groups; ++g)
-      if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(L, g * kMaxClusterSph, csz(g), nullptr,
+      if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeRowStat>(L, g * gc, csz(g), nullptr,
                                                                    L.rowstat + (int64_t)g * L.N, &ncl, st))
         return rc;
     if (L.infer == 1) {
@@ -937,7 +939,7 @@ static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
     if (int rc = check_launch("tc_lse_combine_kernel")) return rc;
   }
   for (int g = 0; g < groups; ++g)
-    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeProba>(L, g * kMaxClusterSph, csz(g), L.lse, nullptr, &ncl, st))
+    if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeProba>(L, g * gc, csz(g), L.lse, nullptr, &ncl, st))
       return rc;
   return GMMXX_OK;
 }

@@ -65,23 +65,32 @@ __host__ __device__ inline int stat_width(int cov, int D) {
   }
 }
 
-// Tensor-core path window (em_tc.cu): bf16 X, B == 1, N >= 64K,
-// diag D == 64 with K <= 512, spherical D in {64, 128} with K <= 1024.
+// Tensor-core path window (em_tc.cu, em_tc_diag.cu): bf16 X, B == 1,
+// N >= 64K, diag D == 64 with K <= 512, spherical D in {64, 128} with
+// K <= 16384 (one pass up to 1024 components, else two passes per group).
 constexpr int kTcMaxClusters = 160;
 constexpr int kMaxClusterDiag = 4;
-constexpr int kMaxClusterSph = 8;      // spherical: up to 8 CTAs (1024 components) per cluster
-constexpr int kMaxComponentsSph = 16384;  // larger K runs as groups of 1024 components
+constexpr int kMaxClusterSph = 8;      // spherical one-pass: up to 8 CTAs (1024 components) per cluster
+constexpr int kMaxComponentsSph = 16384;
+// Spherical K > 1024: groups of 4 chunks (512 components).  Clusters of 4
+// co-reside 33 at a time (132 SMs) against 15 of 8 (120 SMs), for the same
+// work per CTA; the price is twice the passes over X, which HBM absorbs.
+constexpr int kGroupChunks = 4;
 __host__ __device__ inline bool tc_eligible(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   if (B != 1 || N < 65536) return false;
   if (cov == GMMXX_DIAG) return D == 64 && K <= 128 * kMaxClusterDiag;
   if (cov == GMMXX_SPHERICAL) return (D == 64 || D == 128) && K <= kMaxComponentsSph;
   return false;
 }
-// 128-component groups of one tensor-core launch: all of K up to 8 chunks,
-// else groups of 8 chunks (spherical large K)
-__host__ __device__ inline int tc_groups(int64_t K) {
+// 128-component chunks per group of one tensor-core launch: all of K up to
+// 8 chunks (one pass), else kGroupChunks (spherical large K, two passes)
+__host__ __device__ inline int tc_group_chunks(int64_t K) {
   const int nch = (int)((K + 127) / 128);
-  return (nch + kMaxClusterSph - 1) / kMaxClusterSph;
+  return nch <= kMaxClusterSph ? nch : kGroupChunks;
+}
+__host__ __device__ inline int tc_groups(int64_t K) {
+  const int nch = (int)((K + 127) / 128), gc = tc_group_chunks(K);
+  return (nch + gc - 1) / gc;
 }
 // three bf16 terms per weight: a_j (and v_j for diag)
 __host__ __device__ inline int tc_param_blocks(int cov, int D) { return (cov == GMMXX_DIAG ? 6 : 3) * (D / 64); }
@@ -162,7 +171,7 @@ inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   if (tc_eligible(cov, B, N, D, K)) {
     const int nch = (int)((K + 127) / 128);
     const int G = tc_groups(K);
-    const int C = G > 1 ? kMaxClusterSph : nch;
+    const int C = tc_group_chunks(K);
     L.tc_cluster = C;
     L.tc_chunks = nch;
     L.tc_params = off; off += al((int64_t)nch * tc_param_blocks(cov, (int)D) * 16384);

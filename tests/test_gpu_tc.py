@@ -1,6 +1,6 @@
 """Tensor-core (tcgen05) EM kernel parity: bf16 X, diag D=64 (K <= 512) /
 spherical D in {64, 128} (K <= 1024 in one cluster of 1-8 CTAs, larger K as
-groups of 1024 components in two passes), against the numpy oracle and
+groups of 512 components in two passes), against the numpy oracle and
 against the exact-fp32 CUDA-core kernels on the same inputs.
 bf16-input tolerances: parameters within 1e-4 (relative, atol 1e-4, or within
 the fp32 oracle's own error), mean log-likelihood within 1e-3 relative."""
@@ -141,7 +141,7 @@ def _stats_one_step(cov, xb, init, icov, iw, k, dev):
 
 
 def test_tc_grouped_statistics_single_step(cuda_device):
-    """Large-K spherical (two-pass, groups of 1024): the statistics and the
+    """Large-K spherical (two-pass, groups of 512): the statistics and the
     log-likelihood of one accumulate call equal the CUDA-core ones."""
     xb, init, icov, iw = _data(13, 65_536, 128, 2304, "spherical")
     out = _stats_one_step("spherical", xb, init, icov, iw, 2304, cuda_device)
@@ -152,7 +152,7 @@ def test_tc_grouped_statistics_single_step(cuda_device):
 
 
 def test_tc_grouped_config4_shape_matches_simt(cuda_device):
-    """Config-4 shape (spherical, D = 128, K = 8192: 8 groups) on 65,536 rows.
+    """Config-4 shape (spherical, D = 128, K = 8192: 16 groups) on 65,536 rows.
 
     With ~8 rows per component many components hold a single row, whose
     variance is a cancellation (sum r|x|^2 - n |mu|^2 = 0 up to rounding) that
