@@ -603,6 +603,22 @@ static int sm_count() {
   return cached;
 }
 
+// Row blocks of a (row blocks, component tiles, B) statistics grid: as many
+// as fill one wave of co-resident CTAs (a partly filled second or third
+// wave would cost a whole wave), at most the partial slots the workspace
+// reserves (mstep_blocks) and at most one per row tile.
+template <typename KernelT>
+static int64_t wave_blocks(KernelT k, int64_t smem, int64_t ktiles, int64_t B, int64_t nblk_max, int64_t tiles) {
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kThreads, (size_t)smem) != cudaSuccess || occ < 1) {
+    cudaGetLastError();
+    occ = 1;
+  }
+  int64_t nblk = (int64_t)sm_count() * occ / (ktiles * B);
+  nblk = std::min(std::max<int64_t>(nblk, 1), nblk_max);
+  return std::min(nblk, std::max<int64_t>(tiles, 1));
+}
+
 template <typename KernelT>
 static int prep_smem(KernelT k, int64_t bytes) {
   if (bytes > 48 * 1024) {
@@ -640,14 +656,14 @@ int launch_rows(int cov, int mode, const RowArgs& a, int B, cudaStream_t st) {
 }
 
 template <int COV, int NCH>
-static int launch_mstep_t(RowArgs a, int B, cudaStream_t st) {
+static int launch_mstep_t(RowArgs& a, int B, cudaStream_t st) {
   const int64_t sm = smem_bytes(COV, a.D, true);
   auto k = mstep_kernel<COV, NCH>;
   if (int rc = prep_smem(k, sm)) return rc;
   const int ktiles = (int)(a.Kp / kBK);
   const int64_t tiles = ceil_div(a.N, kBN);
   const int64_t nblk_max = mstep_blocks(B, a.N, a.Kp);  // partial slots reserved in the workspace
-  a.rows_per_cta = ceil_div(tiles, nblk_max) * kBN;
+  a.rows_per_cta = ceil_div(tiles, wave_blocks(k, sm, ktiles, B, nblk_max, tiles)) * kBN;
   const int64_t nblk = ceil_div(a.N, a.rows_per_cta);
   a.part_blocks = nblk_max;
   dim3 grid((unsigned)nblk, (unsigned)ktiles, (unsigned)B);
@@ -656,7 +672,7 @@ static int launch_mstep_t(RowArgs a, int B, cudaStream_t st) {
 }
 
 template <int COV>
-static int launch_mstep_c(const RowArgs& a, int B, cudaStream_t st) {
+static int launch_mstep_c(RowArgs& a, int B, cudaStream_t st) {
   const int nch = (int)ceil_div(a.FM - 1, 64);  // n_k is a column sum of R, outside the chunks
   switch (nch) {
     case 1: return launch_mstep_t<COV, 1>(a, B, st);
@@ -669,7 +685,7 @@ static int launch_mstep_c(const RowArgs& a, int B, cudaStream_t st) {
   return set_error(GMMXX_ERR_UNSUPPORTED, "statistics width %d exceeds the SIMT window", a.FM);
 }
 
-int launch_mstep(int cov, const RowArgs& a, int B, cudaStream_t st) {
+int launch_mstep(int cov, RowArgs& a, int B, cudaStream_t st) {
   if (a.N == 0) return GMMXX_OK;
   switch (cov) {
     case GMMXX_SPHERICAL: return launch_mstep_c<GMMXX_SPHERICAL>(a, B, st);
@@ -687,7 +703,7 @@ static int launch_small_t(RowArgs a, int B, cudaStream_t st) {
   if (int rc = prep_smem(k, sm)) return rc;
   const int64_t tiles = ceil_div(a.N, kBN);
   const int64_t nblk_max = mstep_blocks(B, a.N, a.Kp);
-  a.rows_per_cta = ceil_div(tiles, nblk_max) * kBN;
+  a.rows_per_cta = ceil_div(tiles, wave_blocks(k, sm, 1, B, nblk_max, tiles)) * kBN;
   const int64_t nblk = ceil_div(a.N, a.rows_per_cta);
   a.part_blocks = nblk_max;
   dim3 grid((unsigned)nblk, 1u, (unsigned)B);
@@ -729,7 +745,9 @@ int launch_stats_reduce(const RowArgs& a, int B, cudaStream_t st) {
   if (a.N == 0) return GMMXX_OK;
   const int64_t tiles = ceil_div(a.N, kBN);
   const int64_t nblk_max = mstep_blocks(B, a.N, a.Kp);
-  const int64_t nblk = ceil_div(a.N, ceil_div(tiles, nblk_max) * kBN);  // slots the M-step filled
+  // slots the M-step filled (launch_mstep recorded its rows per CTA)
+  const int64_t rpc = a.rows_per_cta > 0 ? a.rows_per_cta : ceil_div(tiles, nblk_max) * kBN;
+  const int64_t nblk = ceil_div(a.N, rpc);
   const int64_t n = (int64_t)B * a.K * a.FM;
   // partial slots are strided by nblk_max; only the first nblk are written
   stats_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(

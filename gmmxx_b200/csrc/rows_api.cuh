@@ -35,7 +35,8 @@ struct RowArgs {
 enum { MODE_LSE = 0, MODE_ARGMAX = 1, MODE_RESP = 2 };
 
 int launch_rows(int cov, int mode, const RowArgs& a, int B, cudaStream_t st);
-int launch_mstep(int cov, const RowArgs& a, int B, cudaStream_t st);
+// records the grid it chose in a.rows_per_cta (read by launch_stats_reduce)
+int launch_mstep(int cov, RowArgs& a, int B, cudaStream_t st);
 // stats += sum of the M-step partials, ll += sum of the LSE partials (fixed order)
 int launch_stats_reduce(const RowArgs& a, int B, cudaStream_t st);
 // K <= 64: statistics and log-likelihood in one pass, then their fixed-order
