@@ -14,7 +14,6 @@ through the GPU each iteration (gmmxx_b200.large_n), as in the reference
 
 from __future__ import annotations
 
-import contextlib
 import math
 import warnings
 from typing import Any, Optional

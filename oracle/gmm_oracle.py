@@ -18,7 +18,7 @@ recorded from the reference (``tests/golden/make_golden.py``).
 from __future__ import annotations
 
 import math
-from typing import Dict, Optional, Tuple
+from typing import Dict, Tuple
 
 import numpy as np
 

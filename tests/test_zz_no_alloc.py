@@ -7,7 +7,6 @@ different models, and it must refuse shapes whose table does not fit.
 This file is collected last on purpose: it exercises the shared built-in
 array after every other test has run, and must also pass on its own."""
 
-import ctypes
 
 import numpy as np
 import pytest
