@@ -176,7 +176,7 @@ def run_infer(args, cfg, x, means, cov, weights):
     with CUDA events on the launching stream (the output buffer of
     predict_proba is allocated once).  Roofline: algorithmic logit FLOPs
     against the bf16 peak for labels / score_samples, and the output bytes
-    against HBM for predict_proba (SURVEY 8d's bound for that call)."""
+    against HBM for predict_proba (its output of K floats per row bounds it)."""
     import torch
 
     from gmmxx_b200 import engine
