@@ -98,3 +98,20 @@ def test_accumulate_path_selection(lib, monkeypatch):
     assert nat.accumulate_path(nat.DIAG, nat.BFLOAT16, 1, 50_000_000, 64, 512) == 0
     with pytest.raises(nat.GmmxxError):
         nat.accumulate_path(7, nat.BFLOAT16, 1, 10, 4, 4)
+
+
+def test_large_k_spherical_workspace_has_per_group_row_partials(lib):
+    """Spherical K > 1024 runs in groups of 512 components (4 chunks): the
+    workspace grows by 8 B per row per group (the (max, sum) row partials),
+    plus the per-row log-sum-exp buffers, over the fixed-size tables."""
+    k, d = 8192, 128
+    n1, n2 = 1 << 20, 1 << 21
+    slope = (_native.workspace_bytes(_native.SPHERICAL, 1, n2, d, k) -
+             _native.workspace_bytes(_native.SPHERICAL, 1, n1, d, k)) / (n2 - n1)
+    groups = k // 512
+    per_row = 8 * groups + 4 + 4 + 8 / 64  # row partials, tc log-sum-exp, CUDA-core lse, LL partials
+    assert abs(slope - per_row) < 0.01
+    # one-pass window (K <= 1024): no per-group partials
+    slope1 = (_native.workspace_bytes(_native.SPHERICAL, 1, n2, d, 1024) -
+              _native.workspace_bytes(_native.SPHERICAL, 1, n1, d, 1024)) / (n2 - n1)
+    assert abs(slope1 - (4 + 8 / 64)) < 0.01
