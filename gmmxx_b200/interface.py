@@ -416,3 +416,99 @@ class GMMXX:
             setattr(self, name, value)
         self._reset_fit_state()
         return self
+
+    # --- save / load ------------------------------------------------------------
+
+    _STATE_FORMAT = "gmmxx_b200.GMMXX"
+    _STATE_VERSION = 1
+
+    def state_dict(self) -> dict:
+        """The fitted model as plain Python values and CPU tensors.
+
+        The reference keeps a fit only in memory (its fitted attributes are
+        set in gmmxx/interface.py:369-396 and nothing writes them out); this is
+        an addition.  The dict holds the constructor parameters, the batched
+        parameters (``means`` (B, K, D), ``covariances`` in the layout of the
+        covariance type, ``weights`` (B, K)), the fit labels when they were
+        computed and the fit record (``lower_bound``, history, iteration
+        count, init source).  ``torch.save`` writes it and
+        ``torch.load(..., weights_only=True)`` reads it back.
+        """
+        self._require_trained()
+        params = self.get_params()
+        params["dtype"] = None if self.dtype is None else str(self.dtype).split(".")[-1]
+        params["device"] = str(self.device)
+        cpu = lambda t: None if t is None else t.detach().to("cpu").clone()
+        return {
+            "format": self._STATE_FORMAT,
+            "version": self._STATE_VERSION,
+            "params": params,
+            "batch_size": self._batch_size,
+            "means": cpu(self.means_b),
+            "covariances": cpu(self.variances_b),
+            "weights": cpu(self.weights_b),
+            "labels": cpu(self.cluster_ids_b),
+            "fit_info": dict(self.fit_info_ or {}),
+        }
+
+    def load_state_dict(self, state: dict) -> "GMMXX":
+        """Restore a model written by :meth:`state_dict`.  The constructor
+        parameters are taken from the state except ``device``, which stays the
+        one this estimator was built with; the parameter tensors move there.
+        Raises ``ValueError`` on a state of another format or version, or whose
+        tensors do not have the shapes its covariance type needs."""
+        if not isinstance(state, dict) or state.get("format") != self._STATE_FORMAT:
+            raise ValueError("not a gmmxx_b200.GMMXX state")
+        if state.get("version") != self._STATE_VERSION:
+            raise ValueError(f"unsupported GMMXX state version {state.get('version')!r}")
+        params = dict(state["params"])
+        params.pop("device", None)
+        if params.get("dtype") is not None:
+            params["dtype"] = getattr(torch, params["dtype"])
+        backend = params.pop("backend", "auto")
+        means, cov, weights, labels = state["means"], state["covariances"], state["weights"], state["labels"]
+        batch_size = state["batch_size"]
+        for name, t in (("means", means), ("covariances", cov), ("weights", weights)):
+            if not torch.is_tensor(t) or not t.dtype.is_floating_point:
+                raise ValueError(f"state entry {name!r} must be a floating point tensor")
+        if means.ndim != 3:
+            raise ValueError("state means must have shape (B, K, D)")
+        b, k, d = means.shape
+        if (batch_size is None and b != 1) or (batch_size is not None and batch_size != b):
+            raise ValueError("state batch_size does not match the parameter tensors")
+        cov_type = _normalize_covariance_type(params["covariance_type"])
+        shapes = {"spherical": (b, k), "diag": (b, k, d), "tied": (b, d, d), "full": (b, k, d, d)}
+        if tuple(cov.shape) != shapes[cov_type]:
+            raise ValueError(f"state covariances must have shape {shapes[cov_type]} for {cov_type} covariance")
+        if tuple(weights.shape) != (b, k):
+            raise ValueError(f"state weights must have shape {(b, k)}")
+        if labels is not None and (not torch.is_tensor(labels) or labels.ndim != 2 or labels.shape[0] != b):
+            raise ValueError("state labels must have shape (B, N)")
+        if params.get("n_components") != k or params.get("d") not in (None, d):
+            raise ValueError("state parameters do not match the parameter tensors")
+        self.set_params(backend=backend, **params)
+        info = dict(state.get("fit_info") or {})
+        for key in ("lower_bound", "lower_bound_history", "n_iter", "init_source"):
+            if key not in info:
+                raise ValueError(f"state fit_info lacks {key!r}")
+        dev = lambda t: t.to(device=self.device, dtype=torch.float32).contiguous()
+        self._set_fit_result(labels_b=None if labels is None else labels.to(self.device, torch.int64),
+                             means_b=dev(means), variances_b=dev(cov), weights_b=dev(weights), info=info,
+                             batch_size=batch_size)
+        self.d = d
+        return self
+
+    def save(self, path) -> None:
+        """Write :meth:`state_dict` to ``path`` with ``torch.save``."""
+        torch.save(self.state_dict(), path)
+
+    @classmethod
+    def load(cls, path, device: Optional[torch.device] = None) -> "GMMXX":
+        """Read a model written by :meth:`save`; ``device`` (default: the one it
+        was fitted on) is where its parameters are placed."""
+        state = torch.load(path, map_location="cpu", weights_only=True)
+        if not isinstance(state, dict) or "params" not in state:
+            raise ValueError("not a gmmxx_b200.GMMXX state")
+        params = state["params"]
+        model = cls(k=params["n_components"], device=params["device"] if device is None else device)
+        return model.load_state_dict(state)

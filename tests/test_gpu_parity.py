@@ -180,6 +180,24 @@ def test_estimator_end_to_end(cuda_device):
         assert g.score(xt) == pytest.approx(float(s.mean()))
 
 
+def test_saved_model_predicts_identically(cuda_device, tmp_path):
+    """A fitted estimator written with save() and read with load() gives the
+    same labels, log-likelihoods and responsibilities bit for bit."""
+    from gmmxx_b200 import GMMXX
+
+    x, _ = _mixture(4, 2, 3000, 8, 6)
+    xt = torch.from_numpy(x).to(cuda_device)
+    for cov in ("spherical", "diag", "tied", "full"):
+        g = GMMXX(k=6, niter=5, covariance_type=cov, backend="cuda", seed=2).fit(xt)
+        g.save(tmp_path / f"{cov}.pt")
+        r = GMMXX.load(tmp_path / f"{cov}.pt")
+        assert r.device == g.device and r.covariance_type == cov
+        assert torch.equal(r.means_, g.means_) and torch.equal(r.labels_, g.labels_)
+        assert torch.equal(r.predict(xt), g.predict(xt))
+        assert torch.equal(r.score_samples(xt), g.score_samples(xt))
+        assert torch.equal(r.predict_proba(xt), g.predict_proba(xt))
+
+
 def test_streamed_fit_matches_resident_fit(cuda_device):
     from gmmxx_b200 import engine, large_n
 
