@@ -73,6 +73,9 @@ _SIGNATURES = {
     "gmmxx_accumulate_path": (_I32, [_I32, _I32, _I64, _I64, _I64, _I64, _P]),
     "gmmxx_em_prepare": (_I32, [_I32, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _SZ, _P]),
     "gmmxx_em_accumulate": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P, _P, _P]),
+    "gmmxx_topk_scratch_bytes": (_SZ, [_I64, _I64, _I64]),
+    "gmmxx_em_accumulate_topk": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P, _SZ, _P, _P,
+                                        _P]),
     "gmmxx_em_finalize": (_I32, [_I32, _I64, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _P, _P, _P, _P]),
     "gmmxx_xx_total": (_I32, [_I32, _P, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "gmmxx_assign": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
@@ -146,3 +149,7 @@ def accumulate_path(cov: int, xdt: int, b: int, n: int, d: int, k: int) -> int:
 
 def workspace_bytes(cov: int, b: int, n: int, d: int, k: int) -> int:
     return int(load().gmmxx_workspace_bytes(cov, b, n, d, k))
+
+
+def topk_scratch_bytes(b: int, n: int, top_k: int) -> int:
+    return int(load().gmmxx_topk_scratch_bytes(b, n, top_k))

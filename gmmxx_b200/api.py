@@ -6,7 +6,9 @@ the reference (gmmxx/torch_fallback.py:3339-3513).  Arguments that only steer
 the reference's Triton / chunking heuristics (``chunk_size_N``,
 ``chunk_size_K``, ``kmeans_*``, ``use_triton``) are accepted and validated but
 do not change the result: the engine streams rows and components itself.
-``approx_top_k`` (approximate top-k EM) is not part of this engine and raises.
+``approx_top_k`` in [1, K - 1] runs approximate top-k EM (each row's
+responsibilities restricted to its top_k components, as the reference's
+torch_fallback.py:667-767); None or >= K is exact EM.
 
 Inference functions mirror the reference's ``*_torch_native_chunked``
 functions (torch_fallback.py:780-1345) without the torch-specific suffix.
@@ -34,8 +36,8 @@ def _validate(x, n_components, max_iters, chunk_size_N, chunk_size_K, min_weight
         raise ValueError("chunk_size_N and chunk_size_K must be positive")
     if min_weight <= 0.0:
         raise ValueError("min_weight must be positive")
-    if approx_top_k is not None and int(approx_top_k) < int(n_components):
-        raise NotImplementedError("approximate top-k EM is not implemented by the gmmxx_b200 engine")
+    if approx_top_k is not None and int(approx_top_k) <= 0:
+        raise ValueError("approx_top_k must be positive or None")
 
 
 def _fit(cov_type, x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
@@ -44,7 +46,8 @@ def _fit(cov_type, x, n_components, max_iters, tol, init_means, init_variances, 
     return engine.em_fit(
         cov_type, x, n_components, max_iters=max_iters, tol=tol, init_means=init_means,
         init_variances=init_variances, init_weights=init_weights, init_params=init_params,
-        reg_covar=reg_covar, min_weight=min_weight, compute_labels=compute_labels, verbose=verbose)
+        reg_covar=reg_covar, min_weight=min_weight, compute_labels=compute_labels, verbose=verbose,
+        approx_top_k=approx_top_k)
 
 
 def batch_gmm_Spherical(

@@ -277,6 +277,50 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
   return launch_stats_reduce(a, (int)B, st);
 }
 
+size_t gmmxx_topk_scratch_bytes(int64_t B, int64_t N, int64_t top_k) {
+  if (B <= 0 || N < 0 || top_k <= 0) return 0;
+  return (size_t)topk_scratch_bytes(B, N, top_k);
+}
+
+int gmmxx_em_accumulate_topk(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,
+                             int64_t top_k, void* workspace, size_t workspace_bytes, void* scratch,
+                             size_t scratch_bytes, float* stats, double* log_likelihood, void* stream) {
+  if (int rc = check_shape(cov_type, x_dtype, B, N, D, K)) return rc;
+  GMMXX_REQUIRE(stats, "stats");
+  GMMXX_REQUIRE(log_likelihood, "log_likelihood");
+  if (top_k < 1 || top_k >= K)
+    return set_error(GMMXX_ERR_INVALID, "top_k=%lld must be in [1, K - 1] (K=%lld)", (long long)top_k, (long long)K);
+  if (top_k > kMaxTopK)
+    return set_error(GMMXX_ERR_UNSUPPORTED, "top_k=%lld exceeds the engine window (top_k <= %d)", (long long)top_k,
+                     kMaxTopK);
+  const Layout L = make_layout(cov_type, B, N, D, K);
+  if (int rc = check_ws(workspace, workspace_bytes, L)) return rc;
+  if (N == 0) return GMMXX_OK;
+  GMMXX_REQUIRE(x, "x");
+  GMMXX_REQUIRE(scratch, "scratch");
+  if ((reinterpret_cast<uintptr_t>(scratch) & 15) != 0) return set_error(GMMXX_ERR_INVALID, "scratch must be 16-byte aligned");
+  const int64_t need = topk_scratch_bytes(B, N, top_k);
+  if ((int64_t)scratch_bytes < need)
+    return set_error(GMMXX_ERR_WORKSPACE, "scratch of %zu bytes is smaller than the %lld bytes required",
+                     scratch_bytes, (long long)need);
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
+  a.top_k = (int)top_k;
+  a.topk_idx = static_cast<int32_t*>(scratch);
+  a.topk_r = reinterpret_cast<float*>(static_cast<char*>(scratch) + need / 2);
+  a.ll_part = reinterpret_cast<double*>(ws + L.llpart);
+  a.ll = log_likelihood;
+  if (cov_type == GMMXX_TIED) a.q_out = reinterpret_cast<float*>(ws + L.qrow);
+  if (int rc = launch_topk_rows(cov_type, a, (int)B, st)) return rc;
+  a.q_in = a.q_out;  // x^T P x for the M-step's row loads
+  a.q_out = nullptr;
+  a.stats = stats;
+  a.part = reinterpret_cast<float*>(ws + L.mpart);
+  if (int rc = launch_topk_mstep(cov_type, a, (int)B, st)) return rc;
+  return launch_stats_reduce(a, (int)B, st);
+}
+
 int gmmxx_em_finalize(int cov_type, int64_t B, int64_t D, int64_t K, int64_t n_total, const float* stats,
                       const double* log_likelihood, const float* xx_total, float reg_covar, float min_weight,
                       float* means, float* cov, float* weights, float* lower_bound_out, void* stream) {

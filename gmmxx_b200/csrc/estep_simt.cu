@@ -20,6 +20,9 @@
 //   em_small_kernel  K <= 64 (one component tile): the two passes above in
 //                 one -- logits, the row's logsumexp, r and the statistics per
 //                 row tile, the log-likelihood summed per CTA.
+//   topk_rows_kernel / topk_mstep_kernel  approximate top-k EM: each row's
+//                 top_k components and responsibilities, then the statistics
+//                 from those lists.
 #include "rows_api.cuh"
 
 #include <float.h>
@@ -529,6 +532,164 @@ __global__ void __launch_bounds__(kThreads) em_small_kernel(RowArgs a) {
   }
 }
 
+// Approximate top-k EM (torch_fallback.py:667-767 _topk_logits_for_chunk /
+// _accumulate_topk_stats; _cuda.py:783-889): a row's responsibilities are
+// the softmax of its top_k logits, zero for every other component.
+//
+// Selection pass, grid (row tiles, B): the logits of each 64-component tile
+// go through shared memory, and one thread per row merges them into the
+// row's list, sorted by logit (descending) with the lower component index
+// first among equal logits (a candidate enters only when strictly larger than
+// the list's last entry, and moves up only past strictly smaller entries).
+// After the last tile: the list's log-sum-exp (summed per CTA into the
+// log-likelihood partials, as rows_kernel<MODE_LSE> does), and the lists of
+// (component, r = exp(logit - lse)) to scratch.
+__host__ __device__ inline int64_t topk_rows_smem(int cov, int D, int top_k) {
+  return smem_bytes(cov, D, false) + (int64_t)kBN * (kBK + 1) * 4 + (int64_t)top_k * kBN * 8;
+}
+
+template <int COV>
+__global__ void __launch_bounds__(kThreads) topk_rows_kernel(RowArgs a) {
+  extern __shared__ __align__(16) char smem_raw[];
+  const Smem s = carve<COV>(smem_raw, a.D, false);
+  float* lt = reinterpret_cast<float*>(smem_raw + smem_bytes(COV, a.D, false));  // [kBN][kBK + 1]
+  const int T = a.top_k;
+  float* lv = lt + kBN * (kBK + 1);                       // [T][kBN] list logits
+  int* li = reinterpret_cast<int*>(lv + T * kBN);         // [T][kBN] list components
+  const int b = blockIdx.y;
+  const int64_t row0 = (int64_t)blockIdx.x * kBN;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  if (COV == GMMXX_TIED) {
+    const float* pb = a.prec + (int64_t)b * a.D * a.D;
+    for (int e = threadIdx.x; e < a.D * a.D; e += kThreads) s.prec[e] = pb[e];
+  }
+  if (COV == GMMXX_FULL) {
+    for (int i = threadIdx.x; i < a.D; i += kThreads) {
+      int p = i * a.D - i * (i - 1) / 2;
+      for (int j = i; j < a.D; ++j) s.pairs[p++] = (uint16_t)(i | (j << 8));
+    }
+  }
+  for (int e = threadIdx.x; e < T * kBN; e += kThreads) {
+    lv[e] = -INFINITY;
+    li[e] = -1;
+  }
+  __syncthreads();
+  load_rows<COV>(a, s, b, row0);
+
+  const int ktiles = (int)(a.Kp / kBK);
+  float acc[4][4];
+  for (int kt = 0; kt < ktiles; ++kt) {
+    tile_dots<COV>(a, s, b, kt, acc);
+    to_logits(a, s, b, kt, acc);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) lt[(ty * 4 + i) * (kBK + 1) + tx * 4 + j] = acc[i][j];
+    __syncthreads();
+    if (threadIdx.x < kBN) {
+      const int r = threadIdx.x;
+      const int kn = min(kBK, a.K - kt * kBK);
+      float vmin = lv[(T - 1) * kBN + r];
+      for (int c = 0; c < kn; ++c) {
+        const float v = lt[r * (kBK + 1) + c];
+        if (!(v > vmin)) continue;
+        int t = T - 1;
+        while (t > 0 && v > lv[(t - 1) * kBN + r]) {
+          lv[t * kBN + r] = lv[(t - 1) * kBN + r];
+          li[t * kBN + r] = li[(t - 1) * kBN + r];
+          --t;
+        }
+        lv[t * kBN + r] = v;
+        li[t * kBN + r] = kt * kBK + c;
+        vmin = lv[(T - 1) * kBN + r];
+      }
+    }
+    __syncthreads();  // the next tile's logits overwrite lt
+  }
+
+  double part = 0.0;
+  if (threadIdx.x < kBN) {
+    const int r = threadIdx.x;
+    const int64_t row = row0 + r;
+    if (row < a.N) {
+      const float m = lv[r];
+      float sm = 0.f;
+      if (m != -INFINITY) {
+        for (int t = 0; t < T; ++t) sm += expf(lv[t * kBN + r] - m);
+      }
+      const float l = (m == -INFINITY) ? -INFINITY : m + logf(sm);
+      const int64_t o = ((int64_t)b * a.N + row) * T;
+      for (int t = 0; t < T; ++t) {
+        a.topk_idx[o + t] = li[t * kBN + r];
+        a.topk_r[o + t] = (m == -INFINITY) ? 0.f : expf(lv[t * kBN + r] - l);
+      }
+      part = (double)l;
+    }
+  }
+  if (a.ll_part != nullptr) {
+    __shared__ double red[kThreads / 32];
+    const double tot = block_sum<double>(part, red);
+    if (threadIdx.x == 0) a.ll_part[(int64_t)b * gridDim.x + blockIdx.x] = tot;
+  }
+}
+
+// M-step over the top-k lists, grid (row blocks, component tiles, B) like
+// mstep_kernel: a row tile's R block (64 rows x this CTA's 64 components) is
+// filled from the lists instead of recomputed logits, and tiles where no row
+// has a listed component in this slice are skipped.
+template <int COV, int NCH>
+__global__ void __launch_bounds__(kThreads) topk_mstep_kernel(RowArgs a) {
+  extern __shared__ __align__(16) char smem_raw[];
+  const Smem s = carve<COV>(smem_raw, a.D, true);
+  const int b = blockIdx.z, kt = blockIdx.y;
+  const int D = a.D, T = a.top_k;
+  if (COV == GMMXX_TIED) {
+    const float* pb = a.prec + (int64_t)b * D * D;
+    for (int e = threadIdx.x; e < D * D; e += kThreads) s.prec[e] = pb[e];
+  }
+  if (COV == GMMXX_FULL) {
+    for (int i = threadIdx.x; i < D; i += kThreads) {
+      int p = i * D - i * (i - 1) / 2;
+      for (int j = i; j < D; ++j) s.pairs[p++] = (uint16_t)(i | (j << 8));
+    }
+  }
+  float macc[NCH][4][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) macc[c][i][j] = 0.f;
+  float nk[4] = {0.f, 0.f, 0.f, 0.f};
+
+  const int64_t rstart = (int64_t)blockIdx.x * a.rows_per_cta;
+  const int64_t rend = min(rstart + a.rows_per_cta, a.N);
+  const int k0 = kt * kBK;
+  for (int64_t row0 = rstart; row0 < rend; row0 += kBN) {
+    __syncthreads();  // the previous tile's reads of R are done
+    for (int e = threadIdx.x; e < kBN * kBK; e += kThreads) s.R[e] = 0.f;
+    __syncthreads();
+    int has = 0;
+    if (threadIdx.x < kBN) {
+      const int64_t row = row0 + threadIdx.x;
+      if (row < rend) {
+        const int64_t o = ((int64_t)b * a.N + row) * T;
+        for (int t = 0; t < T; ++t) {
+          const int c = a.topk_idx[o + t] - k0;  // -1 entries fall outside every slice
+          if (c >= 0 && c < kBK) {
+            s.R[threadIdx.x * kBK + c] = a.topk_r[o + t];
+            has = 1;
+          }
+        }
+      }
+    }
+    if (__syncthreads_or(has) == 0) continue;
+    load_rows<COV>(a, s, b, row0);
+    mstep_tile<COV, NCH>(a, s, macc, nk);
+  }
+  mstep_flush<NCH>(a, a.part + ((int64_t)b * a.part_blocks + blockIdx.x) * a.Kp * a.FM, kt, macc, nk);
+}
+
 __global__ void stats_reduce_kernel(const float* part, int64_t nblk, int64_t stride, int64_t Kp, int K, int FM,
                                     int B, float* stats, const double* ll_part, int64_t nll, double* ll) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -737,6 +898,69 @@ int launch_em_small(int cov, const RowArgs& a, int B, cudaStream_t st) {
     case GMMXX_DIAG: return launch_small_c<GMMXX_DIAG>(a, B, st);
     case GMMXX_TIED: return launch_small_c<GMMXX_TIED>(a, B, st);
     case GMMXX_FULL: return launch_small_c<GMMXX_FULL>(a, B, st);
+  }
+  return set_error(GMMXX_ERR_INVALID, "bad covariance type %d", cov);
+}
+
+template <int COV>
+static int launch_topk_rows_t(const RowArgs& a, int B, cudaStream_t st) {
+  const int64_t sm = topk_rows_smem(COV, a.D, a.top_k);
+  auto k = topk_rows_kernel<COV>;
+  if (int rc = prep_smem(k, sm)) return rc;
+  dim3 grid((unsigned)ceil_div(a.N, kBN), (unsigned)B);  // the LSE pass's grid: same partial layout
+  k<<<grid, kThreads, sm, st>>>(a);
+  return check_launch("topk_rows_kernel");
+}
+
+int launch_topk_rows(int cov, const RowArgs& a, int B, cudaStream_t st) {
+  if (a.N == 0) return GMMXX_OK;
+  if (a.top_k < 1 || a.top_k > kMaxTopK || a.top_k >= a.K)
+    return set_error(GMMXX_ERR_INVALID, "top_k=%d outside [1, min(K - 1, %d)]", a.top_k, kMaxTopK);
+  switch (cov) {
+    case GMMXX_SPHERICAL: return launch_topk_rows_t<GMMXX_SPHERICAL>(a, B, st);
+    case GMMXX_DIAG: return launch_topk_rows_t<GMMXX_DIAG>(a, B, st);
+    case GMMXX_TIED: return launch_topk_rows_t<GMMXX_TIED>(a, B, st);
+    case GMMXX_FULL: return launch_topk_rows_t<GMMXX_FULL>(a, B, st);
+  }
+  return set_error(GMMXX_ERR_INVALID, "bad covariance type %d", cov);
+}
+
+template <int COV, int NCH>
+static int launch_topk_mstep_t(RowArgs& a, int B, cudaStream_t st) {
+  const int64_t sm = smem_bytes(COV, a.D, true);
+  auto k = topk_mstep_kernel<COV, NCH>;
+  if (int rc = prep_smem(k, sm)) return rc;
+  const int ktiles = (int)(a.Kp / kBK);
+  const int64_t tiles = ceil_div(a.N, kBN);
+  const int64_t nblk_max = mstep_blocks(B, a.N, a.Kp);
+  a.rows_per_cta = ceil_div(tiles, wave_blocks(k, sm, ktiles, B, nblk_max, tiles)) * kBN;
+  const int64_t nblk = ceil_div(a.N, a.rows_per_cta);
+  a.part_blocks = nblk_max;
+  dim3 grid((unsigned)nblk, (unsigned)ktiles, (unsigned)B);
+  k<<<grid, kThreads, sm, st>>>(a);
+  return check_launch("topk_mstep_kernel");
+}
+
+template <int COV>
+static int launch_topk_mstep_c(RowArgs& a, int B, cudaStream_t st) {
+  switch ((int)ceil_div(a.FM - 1, 64)) {  // n_k is a column sum of R, outside the chunks
+    case 1: return launch_topk_mstep_t<COV, 1>(a, B, st);
+    case 2: return launch_topk_mstep_t<COV, 2>(a, B, st);
+    case 3: return launch_topk_mstep_t<COV, 3>(a, B, st);
+    case 4: return launch_topk_mstep_t<COV, 4>(a, B, st);
+    case 5: return launch_topk_mstep_t<COV, 5>(a, B, st);
+    case 6: return launch_topk_mstep_t<COV, 6>(a, B, st);
+  }
+  return set_error(GMMXX_ERR_UNSUPPORTED, "statistics width %d exceeds the SIMT window", a.FM);
+}
+
+int launch_topk_mstep(int cov, RowArgs& a, int B, cudaStream_t st) {
+  if (a.N == 0) return GMMXX_OK;
+  switch (cov) {
+    case GMMXX_SPHERICAL: return launch_topk_mstep_c<GMMXX_SPHERICAL>(a, B, st);
+    case GMMXX_DIAG: return launch_topk_mstep_c<GMMXX_DIAG>(a, B, st);
+    case GMMXX_TIED: return launch_topk_mstep_c<GMMXX_TIED>(a, B, st);
+    case GMMXX_FULL: return launch_topk_mstep_c<GMMXX_FULL>(a, B, st);
   }
   return set_error(GMMXX_ERR_INVALID, "bad covariance type %d", cov);
 }

@@ -30,7 +30,19 @@ struct RowArgs {
   // instead of being recomputed for every component tile (may be null)
   float* q_out;         // [B][N]
   const float* q_in;    // [B][N]
+  // approximate top-k EM: per row, its top_k components and their
+  // responsibilities, written by the selection pass and read by the M-step
+  int top_k;
+  int32_t* topk_idx;    // [B][N][top_k] (-1: no entry)
+  float* topk_r;        // [B][N][top_k]
 };
+
+// largest top_k of the approximate EM passes (the selection pass keeps each
+// row's sorted list in shared memory)
+constexpr int kMaxTopK = 64;
+__host__ __device__ inline int64_t topk_scratch_bytes(int64_t B, int64_t N, int64_t top_k) {
+  return 2 * round_up(B * N * top_k * 4, 256);
+}
 
 enum { MODE_LSE = 0, MODE_ARGMAX = 1, MODE_RESP = 2 };
 
@@ -42,5 +54,10 @@ int launch_stats_reduce(const RowArgs& a, int B, cudaStream_t st);
 // K <= 64: statistics and log-likelihood in one pass, then their fixed-order
 // reduction (replaces launch_rows(LSE) + launch_mstep + launch_stats_reduce)
 int launch_em_small(int cov, const RowArgs& a, int B, cudaStream_t st);
+// approximate top-k EM: the selection pass (top_k lists, log-likelihood
+// partials as the LSE pass writes them) and the M-step over the lists; then
+// launch_stats_reduce as for exact EM
+int launch_topk_rows(int cov, const RowArgs& a, int B, cudaStream_t st);
+int launch_topk_mstep(int cov, RowArgs& a, int B, cudaStream_t st);
 
 }  // namespace gmmxx

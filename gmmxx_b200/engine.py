@@ -31,6 +31,27 @@ _X_DTYPES = {torch.float32: nat.FLOAT32, torch.bfloat16: nat.BFLOAT16, torch.flo
 
 MIN_WEIGHT_DEFAULT = 1e-8
 
+# largest approx_top_k the engine's selection kernel keeps per row
+MAX_APPROX_TOP_K = 64
+
+
+def resolve_approx_top_k(approx_top_k: Optional[int], n_components: int) -> Optional[int]:
+    """``approx_top_k`` as the EM loops use it (the reference's
+    _resolve_approx_top_k, torch_fallback.py:599-607): None or >= K means exact
+    EM, <= 0 is an error.  Values above MAX_APPROX_TOP_K (below K) are outside
+    the engine's window."""
+    if approx_top_k is None:
+        return None
+    top_k = int(approx_top_k)
+    if top_k <= 0:
+        raise ValueError("approx_top_k must be positive or None")
+    if top_k >= n_components:
+        return None
+    if top_k > MAX_APPROX_TOP_K:
+        raise nat.UnsupportedShape(nat.ERR_UNSUPPORTED,
+                                   f"approx_top_k={top_k} exceeds the engine window (<= {MAX_APPROX_TOP_K})")
+    return top_k
+
 
 def cov_code(cov_type: str) -> int:
     try:
@@ -195,7 +216,7 @@ class CudaOps:
     """The four per-iteration kernels of one fit, bound to one device buffer
     of rows.  ``em_loop`` drives any object with this interface."""
 
-    def __init__(self, cov_type: str, x: torch.Tensor, k: int):
+    def __init__(self, cov_type: str, x: torch.Tensor, k: int, top_k: Optional[int] = None):
         self.cov_type = cov_type
         self.covc = cov_code(cov_type)
         self.x = x
@@ -206,6 +227,12 @@ class CudaOps:
         self.stream = _stream_ptr(x.device)
         self.stat_width = nat.stat_width(self.covc, self.d)
         self.ws = _WS.get(x.device, nat.workspace_bytes(self.covc, self.b, self.n, self.d, k))
+        # approximate top-k EM: the per-row lists between its two passes
+        self.top_k = top_k
+        self.scratch = None
+        if top_k is not None:
+            self.scratch = torch.empty(nat.topk_scratch_bytes(self.b, self.n, top_k), dtype=torch.uint8,
+                                       device=x.device)
 
     def xx_total(self, xx: torch.Tensor) -> None:
         nat.call("gmmxx_xx_total", self.xdt, self.x.data_ptr(), self.b, self.n, self.d, xx.data_ptr(),
@@ -217,6 +244,11 @@ class CudaOps:
                  self.stream)
 
     def accumulate(self, stats, ll) -> None:
+        if self.top_k is not None:
+            nat.call("gmmxx_em_accumulate_topk", self.covc, self.xdt, self.x.data_ptr(), self.b, self.n, self.d,
+                     self.k, self.top_k, self.ws.data_ptr(), self.ws.numel(), self.scratch.data_ptr(),
+                     self.scratch.numel(), stats.data_ptr(), ll.data_ptr(), self.stream)
+            return
         nat.call("gmmxx_em_accumulate", self.covc, self.xdt, self.x.data_ptr(), self.b, self.n, self.d, self.k,
                  self.ws.data_ptr(), self.ws.numel(), stats.data_ptr(), ll.data_ptr(), self.stream)
 
@@ -323,10 +355,13 @@ def em_fit(
     compute_labels: bool = True,
     verbose: bool = False,
     comm: Optional[Comm] = None,
+    approx_top_k: Optional[int] = None,
 ):
     """Soft EM on the CUDA engine.  ``x`` (B, N_local, D) is this rank's row
     shard when ``comm`` is given (the fit is over the union of all shards;
-    returned labels are the local shard's)."""
+    returned labels are the local shard's).  ``approx_top_k`` in [1, K - 1]
+    runs approximate top-k EM (each row's responsibilities restricted to its
+    top_k components; torch_fallback.py:667-767)."""
     cov_code(cov_type)
     x = check_x(x)
     b, n_local, d = x.shape
@@ -348,12 +383,15 @@ def em_fit(
             raise ValueError("x must contain at least one sample")
         means, cov, weights, source = initial_parameters(
             cov_type, x, n_components, init_means, init_variances, init_weights, reg_covar, init_params)
-        ops = CudaOps(cov_type, x, means.shape[1])
+        top_k = resolve_approx_top_k(approx_top_k, means.shape[1])
+        ops = CudaOps(cov_type, x, means.shape[1], top_k)
         n_iter, hist, elapsed = em_loop(ops, cov_type, means, cov, weights, n_total=n_total, max_iters=max_iters,
                                         tol=tol, reg_covar=reg_covar, min_weight=min_weight, verbose=verbose,
                                         comm=comm)
         labels = assign(cov_type, x, means, cov, weights) if compute_labels else None
-    info = fit_info(n_iter, hist, source, elapsed, gpus=1 if comm is None else comm.world_size)
+    info = fit_info(n_iter, hist, source, elapsed, gpus=1 if comm is None else comm.world_size,
+                    approximate_em_enabled=top_k is not None, approx_top_k=top_k,
+                    cuda_approx_topk_enabled=top_k is not None)
     return labels, means, cov, weights, info
 
 

@@ -197,15 +197,15 @@ class GMMXX:
         self.triton_approx_topk_enabled_ = False
         self.triton_streaming_update_enabled_ = False
         self.triton_labels_enabled_ = False
-        self.approximate_em_enabled_ = False
-        self.approx_top_k_ = None
+        self.approximate_em_enabled_ = bool(info.get("approximate_em_enabled", False))
+        self.approx_top_k_ = info.get("approx_top_k")
         self.large_n_streaming_enabled_ = bool(info.get("large_n_streaming_enabled", False))
         self.copy_stream_prefetch_enabled_ = bool(info.get("copy_stream_prefetch_enabled", False))
         self.last_fallback_reason_ = None
         self.last_backend_used_ = "cuda"
         self.cuda_estep_enabled_ = True
         self.cuda_fused_update_enabled_ = True
-        self.cuda_approx_topk_enabled_ = False
+        self.cuda_approx_topk_enabled_ = bool(info.get("cuda_approx_topk_enabled", False))
 
     # --- input handling --------------------------------------------------------
 
@@ -239,8 +239,6 @@ class GMMXX:
             raise ValueError(
                 f"backend={self.backend!r} is not provided by gmmxx_b200; this engine implements the CUDA backend "
                 "(use backend='cuda' or 'auto')")
-        if self.approx_top_k is not None and self.approx_top_k < self.k:
-            raise NotImplementedError("approximate top-k EM is not implemented by the gmmxx_b200 engine")
         if self.device.type != "cuda":
             raise nat.CudaBackendUnavailable("the gmmxx_b200 engine needs a CUDA device")
         nat.load()
@@ -272,7 +270,7 @@ class GMMXX:
         torch.cuda.manual_seed_all(self.seed)
         kw = dict(max_iters=self.niter, tol=self.tol, init_means=init_means, init_variances=init_covariances,
                   init_weights=init_weights, init_params=self.init_params, reg_covar=self.reg_covar,
-                  compute_labels=self.compute_labels_on_fit, verbose=self.verbose)
+                  compute_labels=self.compute_labels_on_fit, verbose=self.verbose, approx_top_k=self.approx_top_k)
         if self._is_large_cpu_stream_input(x_b):
             if batch_size is not None and x_b.shape[0] != 1:
                 raise ValueError("large-N CPU streaming supports batch size 1")

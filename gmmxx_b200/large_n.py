@@ -78,8 +78,11 @@ def em_fit_streamed(
     compute_labels: bool = True,
     verbose: bool = False,
     streamer: Optional[ChunkStreamer] = None,
+    approx_top_k: Optional[int] = None,
 ):
-    """Soft EM over host-resident X (B == 1), streamed chunk by chunk."""
+    """Soft EM over host-resident X (B == 1), streamed chunk by chunk;
+    ``approx_top_k`` as in engine.em_fit (the reference's large-N driver takes
+    the same option, large_n.py:887-1005)."""
     covc = engine.cov_code(cov_type)
     device = torch.device(device)
     if x_host.dtype not in engine._X_DTYPES:
@@ -103,6 +106,10 @@ def em_fit_streamed(
         means, cov, weights, source = engine.initial_parameters(
             cov_type, probe, n_components, init_means, init_variances, init_weights, reg_covar, init_params)
         k = means.shape[1]
+        top_k = engine.resolve_approx_top_k(approx_top_k, k)
+        scratch = None
+        if top_k is not None:
+            scratch = torch.empty(nat.topk_scratch_bytes(1, st.chunk, top_k), dtype=torch.uint8, device=device)
         stream = engine._stream_ptr(device)
         f = nat.stat_width(covc, d)
         ws = engine._WS.get(device, nat.workspace_bytes(covc, 1, st.chunk, d, k))
@@ -125,6 +132,11 @@ def em_fit_streamed(
             stats.zero_()
             ll.zero_()
             for xc, _ in st.chunks():
+                if top_k is not None:
+                    nat.call("gmmxx_em_accumulate_topk", covc, xdt, xc.data_ptr(), 1, xc.shape[1], d, k, top_k,
+                             ws.data_ptr(), ws.numel(), scratch.data_ptr(), scratch.numel(), stats.data_ptr(),
+                             ll.data_ptr(), stream)
+                    continue
                 nat.call("gmmxx_em_accumulate", covc, xdt, xc.data_ptr(), 1, xc.shape[1], d, k, ws.data_ptr(),
                          ws.numel(), stats.data_ptr(), ll.data_ptr(), stream)
             nat.call("gmmxx_em_finalize", covc, 1, d, k, n, stats.data_ptr(), ll.data_ptr(), engine._p(xx),
@@ -155,8 +167,9 @@ def em_fit_streamed(
         "triton_estep_enabled": False,
         "triton_fused_update_enabled": False,
         "triton_streaming_update_enabled": False,
-        "approximate_em_enabled": False,
-        "approx_top_k": None,
+        "approximate_em_enabled": top_k is not None,
+        "approx_top_k": top_k,
+        "cuda_approx_topk_enabled": top_k is not None,
         "large_n_streaming_enabled": True,
         "copy_stream_prefetch_enabled": True,
         "cuda_engine": "gmmxx_b200",

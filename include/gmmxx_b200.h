@@ -134,6 +134,26 @@ GMMXX_API int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x,
                         void* workspace, size_t workspace_bytes,
                         float* stats, double* log_likelihood, void* stream);
 
+/* Approximate top-k EM (the reference's approx_top_k option): as
+ * gmmxx_em_accumulate, but each row's responsibilities are the softmax of its
+ * top_k largest logits (equal logits: the lower component index ranks first)
+ * and zero for the other components, and *log_likelihood receives the sum of
+ * those top_k log-sum-exps.  1 <= top_k < K and top_k <= 64.  Runs on the
+ * CUDA-core kernels (topk_rows_kernel, topk_mstep_kernel,
+ * stats_reduce_kernel) for every covariance type and x dtype.  `scratch`
+ * (16-byte aligned, gmmxx_topk_scratch_bytes(B, N, top_k) bytes, contents
+ * ignored) holds the per-row lists between the two passes.
+ * Replaces: gmmxx/_cuda.py:783-889 (approx_topk_update_spherical) and the
+ * torch path torch_fallback.py:667-767 (_topk_logits_for_chunk,
+ * _accumulate_topk_stats) used by the four loops (2101-2141, 2504-2530,
+ * 2915-2942). */
+GMMXX_API size_t gmmxx_topk_scratch_bytes(int64_t B, int64_t N, int64_t top_k);
+GMMXX_API int gmmxx_em_accumulate_topk(int cov_type, int x_dtype, const void* x,
+                        int64_t B, int64_t N, int64_t D, int64_t K, int64_t top_k,
+                        void* workspace, size_t workspace_bytes,
+                        void* scratch, size_t scratch_bytes,
+                        float* stats, double* log_likelihood, void* stream);
+
 /* M-step finalize from reduced statistics (torch_fallback.py:2293-2305,
  * 2654-2666, 3141-3167): new means / covariances / weights written in place,
  * empty components (n_k <= min_weight) keep their old means (and, except

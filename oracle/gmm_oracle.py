@@ -318,6 +318,7 @@ def fit(
     min_weight: float = 1e-8,
     compute_labels: bool = True,
     dtype=np.float32,
+    approx_top_k=None,
 ):
     """Soft EM, following the four reference loops:
 
@@ -326,6 +327,13 @@ def fit(
     * diag: torch_fallback.py:2486-2696, finalize 2654-2666;
     * tied / full: torch_fallback.py:2864-3200 (_batch_gmm_matrix_torch_native),
       finalize 3141-3167.
+
+    ``approx_top_k`` (1 <= top_k < K) runs the reference's approximate EM
+    (_resolve_approx_top_k, torch_fallback.py:599-607; _topk_logits_for_chunk
+    and _accumulate_topk_stats, 667-767): each row's responsibilities are the
+    softmax of its top_k logits and zero elsewhere, and the log-likelihood sums
+    the log-sum-exp of those top_k logits.  Equal logits rank the lower
+    component index first.  top_k >= K is exact EM.
 
     Returns ``(labels, means, covariances, weights, info)`` like the reference.
     """
@@ -342,6 +350,13 @@ def fit(
         raise ValueError("x must contain at least one sample")
     if max_iters <= 0:
         raise ValueError("max_iters must be positive")
+    top_k = None
+    if approx_top_k is not None:
+        top_k = int(approx_top_k)
+        if top_k <= 0:
+            raise ValueError("approx_top_k must be positive or None")
+        if top_k >= k:
+            top_k = None
     means, cov, weights = _init_params(cov_type, x, k, init_means, init_variances, init_weights, reg_covar, dtype)
     dt = dtype
     x_sq_all = np.square(x).sum(axis=-1).astype(dt)
@@ -377,6 +392,16 @@ def fit(
             n1 = min(n0 + chunk_size_N, n)
             xc = x[:, n0:n1]
             xsq = x_sq_all[:, n0:n1]
+            if top_k is not None:
+                lg = model.logits(xc, xsq, 0, k)
+                order = np.argsort(-lg, axis=-1, kind="stable")[..., :top_k]
+                vals = np.take_along_axis(lg, order, axis=-1)
+                lse = _logsumexp(vals)
+                total_ll = dt(total_ll + lse.sum(dtype=dt))
+                r = np.zeros_like(lg)
+                np.put_along_axis(r, order, np.exp(vals - lse[..., None]).astype(dt), axis=-1)
+                _accumulate(cov_type, r, xc, xsq, 0, k, nk, sum_x, sum_sq, dt)
+                continue
             if cov_type == "spherical" or k > chunk_size_K:
                 lse = stream_logsumexp(model, xc, xsq, chunk_size_K)
             else:
@@ -385,14 +410,7 @@ def fit(
             for k0 in range(0, k, chunk_size_K):
                 k1 = min(k0 + chunk_size_K, k)
                 r = np.exp(model.logits(xc, xsq, k0, k1) - lse[:, :, None]).astype(dt)
-                nk[:, k0:k1] += r.sum(axis=1)
-                sum_x[:, k0:k1] += np.swapaxes(r, 1, 2) @ xc
-                if cov_type == "spherical":
-                    sum_sq[:, k0:k1] += (r * xsq[:, :, None]).sum(axis=1)
-                elif cov_type == "diag":
-                    sum_sq[:, k0:k1] += np.swapaxes(r, 1, 2) @ np.square(xc)
-                elif cov_type == "full":
-                    sum_sq[:, k0:k1] += np.einsum("bnk,bnd,bne->bkde", r, xc, xc, optimize=True).astype(dt)
+                _accumulate(cov_type, r, xc, xsq, k0, k1, nk, sum_x, sum_sq, dt)
         active = nk > dt(min_weight)
         nk_safe = np.maximum(nk, dt(min_weight))
         means_new = (sum_x / nk_safe[..., None]).astype(dt)
@@ -442,8 +460,23 @@ def fit(
         "lower_bound": history[-1],
         "lower_bound_history": history,
         "init_source": "user",
+        "approximate_em_enabled": top_k is not None,
+        "approx_top_k": top_k,
     }
     return labels, means, cov, weights, info
+
+
+def _accumulate(cov_type, r, xc, xsq, k0, k1, nk, sum_x, sum_sq, dt):
+    """Sufficient statistics of responsibilities ``r`` (B, n, k1 - k0) for
+    components k0..k1 (torch_fallback.py:2255-2291 and the per-type loops)."""
+    nk[:, k0:k1] += r.sum(axis=1)
+    sum_x[:, k0:k1] += np.swapaxes(r, 1, 2) @ xc
+    if cov_type == "spherical":
+        sum_sq[:, k0:k1] += (r * xsq[:, :, None]).sum(axis=1)
+    elif cov_type == "diag":
+        sum_sq[:, k0:k1] += np.swapaxes(r, 1, 2) @ np.square(xc)
+    elif cov_type == "full":
+        sum_sq[:, k0:k1] += np.einsum("bnk,bnd,bne->bkde", r, xc, xc, optimize=True).astype(dt)
 
 
 def fit_spherical(x, n_components, max_iters=100, tol=1e-4, init_means=None, init_variances=None, init_weights=None, **kw):

@@ -7,8 +7,8 @@ Run in a container that has the reference checkout (read-only) available:
 It imports ``gmmxx.torch_fallback`` from that checkout, runs the four soft-EM
 loops (``batch_gmm_{Spherical,Diagonal,Tied,Full}_torch_native``) on small
 seeded problems with injected initial parameters, ``tol=0`` and Triton off,
-then records the fitted parameters, the lower-bound history and the three
-inference outputs (assign / score_samples / predict_proba) on the fitted
+(and, for the APPROX_CASES, ``approx_top_k``), then records the fitted
+parameters, the lower-bound history and the three inference outputs (assign / score_samples / predict_proba) on the fitted
 parameters into ``tests/golden/<case>.npz``.  The fixtures are what the tests
 use; nothing at test time reads the reference.
 """
@@ -40,6 +40,19 @@ CASES = [
     ("full_basic", "full", 2, 800, 3, 3, 6, 1e-6, 32768, 1024, "blobs"),
     ("full_empty_cluster", "full", 1, 600, 3, 3, 4, 1e-6, 32768, 1024, "far_init"),
     ("full_jitter_ladder", "full", 1, 400, 3, 2, 3, 0.0, 32768, 1024, "zero_dim"),
+]
+
+# Approximate top-k EM (the reference's approx_top_k: each row's
+# responsibilities restricted to its top_k logits): the case fields above plus
+# top_k.  Seeded after CASES, so adding them leaves the earlier fixtures as
+# they were.
+APPROX_CASES = [
+    ("sph_approx_topk", "spherical", 1, 1000, 5, 8, 5, 1e-6, 32768, 3, "overlap", 3),
+    ("sph_approx_topk_k100", "spherical", 1, 2000, 4, 100, 3, 1e-6, 32768, 1024, "blobs", 8),
+    ("diag_approx_topk", "diag", 2, 600, 4, 7, 4, 1e-6, 250, 3, "overlap", 2),
+    ("diag_approx_topk_k80", "diag", 1, 1500, 6, 80, 3, 1e-6, 32768, 1024, "blobs", 5),
+    ("tied_approx_topk", "tied", 1, 700, 3, 5, 4, 1e-6, 32768, 2, "overlap", 2),
+    ("full_approx_topk", "full", 1, 600, 3, 4, 4, 1e-6, 32768, 1024, "blobs", 2),
 ]
 
 
@@ -94,7 +107,8 @@ def main(ref_root):
                  tf.full_predict_proba_torch_native_chunked),
     }
     torch.set_num_threads(max(1, min(8, os.cpu_count() or 1)))
-    for seed, (name, cov, b, n, d, k, iters, reg, csn, csk, variant) in enumerate(CASES):
+    cases = [c + (None,) for c in CASES] + APPROX_CASES
+    for seed, (name, cov, b, n, d, k, iters, reg, csn, csk, variant, top_k) in enumerate(cases):
         x, init_means, init_w = make_data(1000 + seed, b, n, d, k, variant)
         if cov == "spherical":
             init_var = tf._global_spherical_variance(x, k, reg)
@@ -104,7 +118,7 @@ def main(ref_root):
             init_var = tf._global_tied_covariance(x, reg)
         else:
             init_var = tf._global_full_covariance(x, k, reg)
-        kw = dict(reg_covar=reg, chunk_size_N=csn, chunk_size_K=csk, compute_labels=True)
+        kw = dict(reg_covar=reg, chunk_size_N=csn, chunk_size_K=csk, compute_labels=True, approx_top_k=top_k)
         if cov == "spherical":
             kw.update(gmm_use_triton_estep=False, gmm_use_triton_streaming_update=False)
         else:
@@ -125,6 +139,7 @@ def main(ref_root):
             labels=labels.numpy(), means=means.numpy(), cov=var.numpy(), weights=w.numpy(),
             lower_bound_history=np.array(info["lower_bound_history"], dtype=np.float64),
             assign=a.numpy(), score_samples=s.numpy(), predict_proba=p.numpy(),
+            **({} if top_k is None else {"approx_top_k": np.array(top_k)}),
         )
         print(f"{name}: lb={info['lower_bound']:.6f} n_iter={info['n_iter']}")
 

@@ -115,3 +115,58 @@ def test_large_k_spherical_workspace_has_per_group_row_partials(lib):
     slope1 = (_native.workspace_bytes(_native.SPHERICAL, 1, n2, d, 1024) -
               _native.workspace_bytes(_native.SPHERICAL, 1, n1, d, 1024)) / (n2 - n1)
     assert abs(slope1 - (4 + 8 / 64)) < 0.01
+
+
+def test_topk_scratch_bytes(lib):
+    """Two [B][N][top_k] lists (component indices, responsibilities), each
+    rounded up to 256 bytes; 0 for invalid sizes."""
+    assert _native.topk_scratch_bytes(2, 1000, 8) == 2 * ((2 * 1000 * 8 * 4 + 255) // 256 * 256)
+    assert _native.topk_scratch_bytes(1, 0, 4) == 0
+    assert lib.gmmxx_topk_scratch_bytes(0, 10, 4) == 0
+    assert lib.gmmxx_topk_scratch_bytes(1, 10, 0) == 0
+
+
+def _aligned(nbytes, align=256):
+    buf = ctypes.create_string_buffer(nbytes + align)
+    return buf, (ctypes.addressof(buf) + align - 1) // align * align
+
+
+def test_topk_arguments_rejected_without_gpu(lib):
+    """top_k outside [1, K - 1], above the engine window, or a scratch buffer
+    that is too small or misaligned: refused before any CUDA call."""
+    b, n, d, k = 1, 10, 4, 100
+    wsb = _native.workspace_bytes(_native.SPHERICAL, b, n, d, k)
+    ws_buf, ws = _aligned(wsb)
+    x = ctypes.c_float(0.0)
+    stats = ctypes.c_float(0.0)
+    ll = ctypes.c_double(0.0)
+    sb = _native.topk_scratch_bytes(b, n, 4)
+    sc_buf, sc = _aligned(sb)
+
+    def call(top_k, scratch=sc, scratch_bytes=sb):
+        return lib.gmmxx_em_accumulate_topk(_native.SPHERICAL, _native.FLOAT32, ctypes.addressof(x), b, n, d, k,
+                                            top_k, ws, wsb, scratch, scratch_bytes, ctypes.addressof(stats),
+                                            ctypes.addressof(ll), None)
+
+    assert call(0) == _native.ERR_INVALID and b"top_k" in lib.gmmxx_last_error()
+    assert call(k) == _native.ERR_INVALID
+    assert call(65) == _native.ERR_UNSUPPORTED
+    assert call(4, scratch_bytes=sb - 1) == _native.ERR_WORKSPACE
+    assert call(4, scratch=None) == _native.ERR_INVALID
+    assert call(4, scratch=sc + 4) == _native.ERR_INVALID
+    assert b"aligned" in lib.gmmxx_last_error()
+
+
+def test_resolve_approx_top_k():
+    """The reference's _resolve_approx_top_k (torch_fallback.py:599-607) plus
+    the engine window."""
+    from gmmxx_b200 import engine
+
+    assert engine.resolve_approx_top_k(None, 8) is None
+    assert engine.resolve_approx_top_k(8, 8) is None
+    assert engine.resolve_approx_top_k(9, 8) is None
+    assert engine.resolve_approx_top_k(3, 8) == 3
+    with pytest.raises(ValueError):
+        engine.resolve_approx_top_k(0, 8)
+    with pytest.raises(_native.UnsupportedShape):
+        engine.resolve_approx_top_k(engine.MAX_APPROX_TOP_K + 1, 1000)

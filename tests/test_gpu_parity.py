@@ -16,11 +16,11 @@ pytestmark = pytest.mark.gpu
 PARAM_TOL = dict(rtol=1e-4, atol=1e-4)
 
 
-def _fit(cov, x, k, iters, init_means, init_var, init_w, reg=1e-6):
+def _fit(cov, x, k, iters, init_means, init_var, init_w, reg=1e-6, approx_top_k=None):
     from gmmxx_b200 import engine
 
     return engine.em_fit(cov, x, k, max_iters=iters, tol=0.0, init_means=init_means, init_variances=init_var,
-                         init_weights=init_w, reg_covar=reg)
+                         init_weights=init_w, reg_covar=reg, approx_top_k=approx_top_k)
 
 
 def test_canary(cuda_device):
@@ -35,8 +35,10 @@ def test_fit_matches_reference_golden(cuda_device, case):
     g = load_golden(case)
     cov = str(g["cov_type"])
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    top_k = int(g["approx_top_k"]) if "approx_top_k" in g else None  # approximate top-k EM cases
     labels, means, c, w, info = _fit(cov, t(g["x"]), int(g["n_components"]), int(g["iters"]), t(g["init_means"]),
-                                     t(g["init_var"]), t(g["init_weights"]), float(g["reg_covar"]))
+                                     t(g["init_var"]), t(g["init_weights"]), float(g["reg_covar"]), top_k)
+    assert info["approximate_em_enabled"] == (top_k is not None) and info["approx_top_k"] == top_k
     np.testing.assert_allclose(means.cpu().numpy(), g["means"], **PARAM_TOL)
     np.testing.assert_allclose(c.cpu().numpy(), g["cov"], **PARAM_TOL)
     np.testing.assert_allclose(w.cpu().numpy(), g["weights"], **PARAM_TOL)
