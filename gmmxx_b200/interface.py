@@ -15,6 +15,7 @@ through the GPU each iteration (gmmxx_b200.large_n), as in the reference
 from __future__ import annotations
 
 import math
+import os
 import warnings
 from typing import Any, Optional
 
@@ -234,10 +235,21 @@ class GMMXX:
             return data, bsz
         raise ValueError("data must have shape (N, D) or (B, N, D)")
 
+    def _effective_backend(self) -> str:
+        """``backend``, with the GMMXX_BACKEND environment variable consulted
+        when it is "auto" and ignored when not a valid name (the reference's
+        resolve_backend_with_env, _dispatch.py:128-144)."""
+        if self.backend == "auto":
+            env = os.environ.get("GMMXX_BACKEND")
+            if env in _VALID_BACKENDS:
+                return env
+        return self.backend
+
     def _require_engine(self) -> None:
-        if self.backend in {"triton", "torch"}:
+        backend = self._effective_backend()
+        if backend in {"triton", "torch"}:
             raise ValueError(
-                f"backend={self.backend!r} is not provided by gmmxx_b200; this engine implements the CUDA backend "
+                f"backend={backend!r} is not provided by gmmxx_b200; this engine implements the CUDA backend "
                 "(use backend='cuda' or 'auto')")
         if self.device.type != "cuda":
             raise nat.CudaBackendUnavailable("the gmmxx_b200 engine needs a CUDA device")

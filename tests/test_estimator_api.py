@@ -123,3 +123,19 @@ def test_inference_needs_a_fit():
     for call in (m.predict, m.predict_proba, m.score_samples, m.score, m.bic, m.aic):
         with pytest.raises(RuntimeError, match="not trained"):
             call(torch.randn(4, 2))
+
+
+def test_gmmxx_backend_environment_variable(monkeypatch):
+    """GMMXX_BACKEND picks the backend when the keyword is "auto" (the
+    reference's _dispatch.py:128-144); an explicit keyword wins and invalid
+    values are ignored.  A backend this engine does not provide raises."""
+    x = torch.randn(16, 2)
+    monkeypatch.setenv("GMMXX_BACKEND", "torch")
+    with pytest.raises(ValueError, match="not provided"):
+        GMMXX(n_components=2, device="cpu").fit(x)
+    with pytest.raises(nat.CudaBackendUnavailable):  # explicit keyword wins
+        GMMXX(n_components=2, device="cpu", backend="cuda").fit(x)
+    monkeypatch.setenv("GMMXX_BACKEND", "bogus")
+    assert GMMXX(n_components=2)._effective_backend() == "auto"
+    with pytest.raises(nat.CudaBackendUnavailable):
+        GMMXX(n_components=2, device="cpu").fit(x)
