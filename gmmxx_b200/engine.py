@@ -298,11 +298,13 @@ def em_loop(ops, cov_type, means, cov, weights, *, n_total, max_iters, tol, reg_
         if comm is not None:
             comm.allreduce_(stats)
             comm.allreduce_(ll)
+        if verbose:
+            prev_means, prev_cov = means.clone(), cov.clone()
         ops.finalize(n_total, stats, ll, xx, reg_covar, min_weight, means, cov, weights, lb_hist[it:])
         if verbose or tol > 0.0:
             lb = float(lb_hist[it].item())
             if verbose:
-                print(f"Iter {it}, lower_bound: {lb:.6f}")
+                print(verbose_line(cov_type, it, lb, means, prev_means, cov, prev_cov))
             if tol > 0.0 and prev is not None and it + 1 < max_iters and abs(lb - prev) < tol:
                 break
             prev = lb
@@ -315,6 +317,20 @@ def em_loop(ops, cov_type, means, cov, weights, *, n_total, max_iters, tol, reg_
         # for iterations whose bound was not collected.
         hist = [0.0] * (n_iter - 1) + [hist[-1]]
     return n_iter, hist, elapsed
+
+
+def verbose_line(cov_type, it, lb, means, prev_means, cov=None, prev_cov=None) -> str:
+    """The per-iteration line the reference's loops print with verbose=True:
+    bound and largest mean shift (torch_fallback.py:2310-2316, large_n.py:
+    1542-1547), plus the largest variance change for diag
+    (torch_fallback.py:2680-2694) or covariance change for tied / full
+    (3180-3194)."""
+    shift = (means - prev_means).norm(dim=-1).max().item()
+    line = f"Iter {it}, lower_bound: {lb:.6f}, mean_shift: {shift:.6f}"
+    if prev_cov is not None and cov_type in ("diag", "tied", "full"):
+        name = "variance_shift" if cov_type == "diag" else "covariance_shift"
+        line += f", {name}: {(cov.float() - prev_cov.float()).abs().max().item():.6f}"
+    return line
 
 
 def fit_info(n_iter, hist, source, elapsed, gpus=1, **extra):

@@ -139,13 +139,15 @@ def em_fit_streamed(
                     continue
                 nat.call("gmmxx_em_accumulate", covc, xdt, xc.data_ptr(), 1, xc.shape[1], d, k, ws.data_ptr(),
                          ws.numel(), stats.data_ptr(), ll.data_ptr(), stream)
+            if verbose:
+                prev_means = means.clone()
             nat.call("gmmxx_em_finalize", covc, 1, d, k, n, stats.data_ptr(), ll.data_ptr(), engine._p(xx),
                      float(reg_covar), float(min_weight), means.data_ptr(), cov.data_ptr(), weights.data_ptr(),
                      lb_hist[it:].data_ptr(), stream)
             if verbose or tol > 0.0:
                 lb = float(lb_hist[it].item())
                 if verbose:
-                    print(f"Iter {it}, lower_bound: {lb:.6f}")
+                    print(engine.verbose_line(cov_type, it, lb, means, prev_means))
                 if tol > 0.0 and prev is not None and it + 1 < max_iters and abs(lb - prev) < tol:
                     break
                 prev = lb

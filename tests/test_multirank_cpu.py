@@ -216,3 +216,33 @@ def test_dead_rank_surfaces_as_error(tmp_path):
     err = (tmp_path / "r0.err")
     assert err.exists(), "the surviving rank must see an error from its collective"
     assert not (tmp_path / "r0.npz").exists()
+
+
+@pytest.mark.parametrize("cov_type,extra", [("spherical", None), ("diag", "variance_shift"),
+                                            ("tied", "covariance_shift"), ("full", "covariance_shift")])
+def test_verbose_lines_match_the_reference_format(cov_type, extra, capsys):
+    """verbose=True prints one line per iteration in the reference's format
+    (torch_fallback.py:2310-2316, 2680-2694, 3180-3194): the bound, the
+    largest mean shift and, for diag / tied / full, the largest change of the
+    variances or covariances."""
+    import re
+
+    from gmmxx_b200 import engine
+
+    x, m0, c0, w0 = _problem(cov_type, b=1)
+    ops = OracleOps(cov_type, x, m0.shape[1])
+    means, cov, weights = (torch.from_numpy(a.copy()) for a in (m0, c0, w0))
+    n_iter, hist, _ = engine.em_loop(ops, cov_type, means, cov, weights, n_total=x.shape[1], max_iters=3, tol=0.0,
+                                     reg_covar=1e-6, min_weight=1e-8, verbose=True)
+    lines = capsys.readouterr().out.strip().splitlines()
+    assert len(lines) == n_iter == 3
+    pat = r"Iter (\d+), lower_bound: (-?\d+\.\d{6}), mean_shift: (\d+\.\d{6})"
+    if extra:
+        pat += rf", {extra}: (\d+\.\d{{6}})"
+    for it, line in enumerate(lines):
+        mt = re.fullmatch(pat, line)
+        assert mt, line
+        assert int(mt.group(1)) == it
+        assert float(mt.group(2)) == pytest.approx(hist[it], abs=1e-6)
+    # the first iteration moves the means away from their initial rows
+    assert float(re.fullmatch(pat, lines[0]).group(3)) > 0.0
