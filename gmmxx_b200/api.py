@@ -10,6 +10,14 @@ do not change the result: the engine streams rows and components itself.
 responsibilities restricted to its top_k components, as the reference's
 torch_fallback.py:667-767); None or >= K is exact EM.
 
+Half-precision ``x`` (bf16 / fp16) is read as stored and every parameter and
+logit is computed and returned in fp32: the estimator's upcast semantics
+(interface.py:426-433), exact because the conversion to fp32 is exact.  The
+reference's torch functions instead keep the parameters in ``x.dtype``
+between iterations (torch_fallback.py:2295, 2656-2666, 3145-3167) and, for
+spherical, form the cross term ``x @ means^T`` in ``x.dtype``
+(torch_fallback.py:348); those roundings are not reproduced.
+
 Inference functions mirror the reference's ``*_torch_native_chunked``
 functions (torch_fallback.py:780-1345) without the torch-specific suffix.
 """
