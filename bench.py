@@ -37,8 +37,6 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-import numpy as np  # noqa: E402
-
 
 def algorithmic_flops(cov: str, n: int, d: int, k: int) -> float:
     """Per-iteration algorithmic FLOPs of the E-step logit contraction plus the
