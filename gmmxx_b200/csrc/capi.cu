@@ -150,9 +150,10 @@ int tc_infer(int cov, int dt, const void* x, int64_t N, int64_t D, int64_t K, co
   return rc;
 }
 
-int infer_common(int cov, int dt, const void* x, int64_t B, int64_t N, int64_t D, int64_t K, const float* means,
+// parameters, x and workspace of an inference call whose sizes and output
+// pointers the caller has checked; then the component table
+int infer_common(int cov, const void* x, int64_t B, int64_t N, int64_t D, int64_t K, const float* means,
                  const float* covp, const float* weights, void* ws, size_t wsb, cudaStream_t st, Layout* L) {
-  if (int rc = check_shape(cov, dt, B, N, D, K)) return rc;
   GMMXX_REQUIRE(means, "means");
   GMMXX_REQUIRE(covp, "cov");
   GMMXX_REQUIRE(weights, "weights");
@@ -352,10 +353,11 @@ int gmmxx_assign(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N,
                  const float* means, const float* cov, const float* weights, int64_t* labels_out, void* workspace,
                  size_t workspace_bytes, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Layout L;
-  if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
-    return rc;
+  if (int rc = check_shape(cov_type, x_dtype, B, N, D, K)) return rc;
   if (N > 0) GMMXX_REQUIRE(labels_out, "labels_out");
+  Layout L;
+  if (int rc = infer_common(cov_type, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
+    return rc;
   bool done = false;
   const int rc = tc_infer(cov_type, x_dtype, x, N, D, K, L, static_cast<char*>(workspace), 2, nullptr, labels_out, st,
                           &done);
@@ -369,10 +371,11 @@ int gmmxx_logsumexp(int cov_type, int x_dtype, const void* x, int64_t B, int64_t
                     const float* means, const float* cov, const float* weights, float* lse_out, void* workspace,
                     size_t workspace_bytes, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Layout L;
-  if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
-    return rc;
+  if (int rc = check_shape(cov_type, x_dtype, B, N, D, K)) return rc;
   if (N > 0) GMMXX_REQUIRE(lse_out, "lse_out");
+  Layout L;
+  if (int rc = infer_common(cov_type, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
+    return rc;
   bool done = false;
   const int rc = tc_infer(cov_type, x_dtype, x, N, D, K, L, static_cast<char*>(workspace), 1, lse_out, nullptr, st,
                           &done);
@@ -386,13 +389,14 @@ int gmmxx_resp(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, i
                const float* means, const float* cov, const float* weights, const float* log_norm, float* resp_out,
                void* workspace, size_t workspace_bytes, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Layout L;
-  if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
-    return rc;
+  if (int rc = check_shape(cov_type, x_dtype, B, N, D, K)) return rc;
   if (N > 0) {
     GMMXX_REQUIRE(log_norm, "log_norm");
     GMMXX_REQUIRE(resp_out, "resp_out");
   }
+  Layout L;
+  if (int rc = infer_common(cov_type, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
+    return rc;
   RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, static_cast<char*>(workspace));
   a.lse_in = log_norm;
   a.out = resp_out;
@@ -403,10 +407,11 @@ int gmmxx_predict_proba(int cov_type, int x_dtype, const void* x, int64_t B, int
                         const float* means, const float* cov, const float* weights, float* proba_out,
                         void* workspace, size_t workspace_bytes, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Layout L;
-  if (int rc = infer_common(cov_type, x_dtype, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
-    return rc;
+  if (int rc = check_shape(cov_type, x_dtype, B, N, D, K)) return rc;
   if (N > 0) GMMXX_REQUIRE(proba_out, "proba_out");
+  Layout L;
+  if (int rc = infer_common(cov_type, x, B, N, D, K, means, cov, weights, workspace, workspace_bytes, st, &L))
+    return rc;
   char* ws = static_cast<char*>(workspace);
   bool done = false;
   const int rc = tc_infer(cov_type, x_dtype, x, N, D, K, L, ws, 3, proba_out, nullptr, st, &done);

@@ -170,3 +170,46 @@ def test_resolve_approx_top_k():
         engine.resolve_approx_top_k(0, 8)
     with pytest.raises(_native.UnsupportedShape):
         engine.resolve_approx_top_k(engine.MAX_APPROX_TOP_K + 1, 1000)
+
+
+def test_entry_points_validate_every_pointer_before_launching(lib):
+    """Each entry point refuses a NULL output, parameter or workspace, or a bad
+    scalar, with GMMXX_ERR_INVALID and a message naming it -- before any CUDA
+    call, so a CPU-only host answers too."""
+    b, n, d, k = 1, 10, 4, 3
+    wsb = _native.workspace_bytes(_native.TIED, b, n, d, k)
+    ws_buf, ws = _aligned(wsb)
+    f = ctypes.c_float(1.0)
+    p = ctypes.addressof(f)
+    dbl = ctypes.c_double(0.0)
+    pd = ctypes.addressof(dbl)
+    cov, dt = _native.DIAG, _native.FLOAT32
+    infer_args = lambda out: (cov, dt, p, b, n, d, k, p, p, p, out, ws, wsb, None)
+    cases = [
+        ("labels_out", lib.gmmxx_assign, infer_args(None)),
+        ("lse_out", lib.gmmxx_logsumexp, infer_args(None)),
+        ("proba_out", lib.gmmxx_predict_proba, infer_args(None)),
+        ("log_norm", lib.gmmxx_resp, (cov, dt, p, b, n, d, k, p, p, p, None, p, ws, wsb, None)),
+        ("resp_out", lib.gmmxx_resp, (cov, dt, p, b, n, d, k, p, p, p, p, None, ws, wsb, None)),
+        ("means", lib.gmmxx_assign, (cov, dt, p, b, n, d, k, None, p, p, p, ws, wsb, None)),
+        ("x", lib.gmmxx_logsumexp, (cov, dt, None, b, n, d, k, p, p, p, p, ws, wsb, None)),
+        ("workspace", lib.gmmxx_predict_proba, (cov, dt, p, b, n, d, k, p, p, p, p, None, wsb, None)),
+        ("stats", lib.gmmxx_em_accumulate, (cov, dt, p, b, n, d, k, ws, wsb, None, pd, None)),
+        ("log_likelihood", lib.gmmxx_em_accumulate, (cov, dt, p, b, n, d, k, ws, wsb, p, None, None)),
+        ("x", lib.gmmxx_em_accumulate, (cov, dt, None, b, n, d, k, ws, wsb, p, pd, None)),
+        ("xx_total", lib.gmmxx_em_finalize, (_native.TIED, b, d, k, n, p, pd, None, 1e-6, 1e-8, p, p, p, None,
+                                             None)),
+        ("n_total", lib.gmmxx_em_finalize, (cov, b, d, k, 0, p, pd, None, 1e-6, 1e-8, p, p, p, None, None)),
+        ("min_weight", lib.gmmxx_em_finalize, (cov, b, d, k, n, p, pd, None, 1e-6, 0.0, p, p, p, None, None)),
+        ("weights", lib.gmmxx_em_prepare, (cov, b, d, k, p, p, None, 1e-6, 1e-8, ws, wsb, None)),
+        ("reg_covar", lib.gmmxx_em_prepare, (cov, b, d, k, p, p, p, -1.0, 1e-8, ws, wsb, None)),
+        ("xx_out", lib.gmmxx_xx_total, (dt, p, b, n, d, None, ws, wsb, None)),
+        ("status_out", lib.gmmxx_workspace_status, (ws, None, None)),
+        ("in", lib.gmmxx_canary_add_offset, (None, p, 4, 1, None)),
+    ]
+    for name, fn, args in cases:
+        assert fn(*args) == _native.ERR_INVALID, name
+        assert name.encode() in lib.gmmxx_last_error(), (name, lib.gmmxx_last_error())
+    # a misaligned workspace is refused the same way
+    assert lib.gmmxx_assign(*infer_args(p)[:11], ws + 8, wsb, None) == _native.ERR_INVALID
+    assert b"aligned" in lib.gmmxx_last_error()
