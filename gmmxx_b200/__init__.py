@@ -29,6 +29,7 @@ from .api import (
     tied_predict_proba,
     tied_score_samples,
 )
+from . import cuda_ops  # noqa: F401  (the reference's operator-level surface, gmmxx.cuda_ops)
 from .interface import GMMXX
 from .large_n import em_fit_streamed
 
@@ -59,6 +60,7 @@ __all__ = [
     "full_score_samples",
     "full_predict_proba",
     "em_fit_streamed",
+    "cuda_ops",
 ]
 
 __version__ = "0.1.0"

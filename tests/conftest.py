@@ -23,7 +23,10 @@ def pytest_configure(config):
 
 
 def golden_cases():
-    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+    """The EM fit / inference cases (make_golden.py); the operator cases
+    (ops_*.npz, make_operator_golden.py) are loaded by name."""
+    names = (os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+    return sorted(n for n in names if not n.startswith("ops_"))
 
 
 def load_golden(name):
