@@ -31,7 +31,13 @@ from .api import (
 )
 from . import cuda_ops  # noqa: F401  (the reference's operator-level surface, gmmxx.cuda_ops)
 from .interface import GMMXX
-from .large_n import em_fit_streamed
+from .large_n import (
+    batch_gmm_largeN_cpu,
+    em_fit_streamed,
+    large_n_predict_cpu,
+    large_n_predict_proba_cpu,
+    large_n_score_samples_cpu,
+)
 
 __all__ = [
     "GMMXX",
@@ -60,6 +66,10 @@ __all__ = [
     "full_score_samples",
     "full_predict_proba",
     "em_fit_streamed",
+    "batch_gmm_largeN_cpu",
+    "large_n_predict_cpu",
+    "large_n_predict_proba_cpu",
+    "large_n_score_samples_cpu",
     "cuda_ops",
 ]
 

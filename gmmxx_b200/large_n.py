@@ -195,3 +195,174 @@ def predict_streamed(kind: str, cov_type: str, x_host: torch.Tensor, means, cov,
         for xc, _ in st.chunks():
             outs.append(fn(cov_type, xc, means, cov, weights))
         return torch.cat(outs, dim=1)
+
+
+# ---------------------------------------------------------------------------
+# the reference's large-N entry points (gmmxx/large_n.py:866-1594, 1907-2502)
+# ---------------------------------------------------------------------------
+
+_COV_TYPES = ("spherical", "diag", "tied", "full")
+
+
+def _validate_large_n_input(x_cpu: torch.Tensor, device) -> torch.device:
+    """The reference's input contract (large_n.py:468-478): (1, N, D) floating
+    point in host memory, a CUDA target device."""
+    device = torch.device(device)
+    if x_cpu.ndim != 3:
+        raise ValueError("x must have shape (B, N, D)")
+    if x_cpu.shape[0] != 1:
+        raise NotImplementedError("Large-N CPU streaming currently supports only B=1")
+    if x_cpu.device.type != "cpu":
+        raise ValueError("Large-N streaming expects a CPU input tensor")
+    if device.type != "cuda":
+        raise ValueError("Large-N streaming expects a CUDA target device")
+    if not x_cpu.dtype.is_floating_point:
+        raise TypeError("GMM input must be a floating point tensor")
+    return device
+
+
+def _check_backend(backend: str) -> None:
+    """backend (with GMMXX_BACKEND consulted for "auto") must resolve to this
+    engine; the reference's torch and Triton backends are not provided."""
+    import os
+
+    valid = ("auto", "cuda", "triton", "torch")
+    if backend not in valid:
+        raise ValueError(f"backend must be one of {valid}, got {backend!r}")
+    effective = backend
+    if backend == "auto" and os.environ.get("GMMXX_BACKEND") in valid:
+        effective = os.environ["GMMXX_BACKEND"]
+    if effective in ("torch", "triton"):
+        raise ValueError(f"backend={effective!r} is not provided by gmmxx_b200; this engine implements the CUDA "
+                         "backend (use backend='cuda' or 'auto')")
+
+
+def _compute_input(x_cpu: torch.Tensor, dtype: Optional[torch.dtype]) -> torch.Tensor:
+    """X in the dtype the reference computes in (its chunks are converted to
+    ``dtype`` on the device).  bf16 / fp16 X with an fp32 compute dtype is read
+    as stored (the conversion is exact); a conversion that rounds (fp32 to a
+    16-bit type, between the 16-bit types, float64 to fp32) is applied once on
+    the host."""
+    target = x_cpu.dtype if dtype is None else dtype
+    if target not in engine._X_DTYPES:
+        raise TypeError(f"compute dtype {target} not supported (float32, bfloat16, float16)")
+    if target == x_cpu.dtype or (target == torch.float32 and x_cpu.dtype in (torch.bfloat16, torch.float16)):
+        return x_cpu
+    return x_cpu.to(target)
+
+
+def batch_gmm_largeN_cpu(
+    x_cpu: torch.Tensor,
+    n_components: int,
+    *,
+    covariance_type: str,
+    device: torch.device,
+    dtype: torch.dtype,
+    max_iters: int = 100,
+    tol: float = 1e-4,
+    verbose: bool = False,
+    init_params: str = "kmeans",
+    reg_covar: float = 1e-6,
+    chunk_size_N: int = 32768,
+    chunk_size_K: int = 1024,
+    kmeans_init_iters: int = 10,
+    kmeans_init_tol: float = 1e-4,
+    kmeans_use_triton: bool = True,
+    gmm_use_triton="auto",
+    min_weight: float = 1e-8,
+    compute_labels: bool = True,
+    max_init_samples: int = 65536,
+    approx_top_k: Optional[int] = None,
+    backend: str = "auto",
+    legacy_no_triton: bool = False,
+    seed: int = 0,
+):
+    """Soft EM over host-resident X with the reference's signature and return
+    value (large_n.py:866-1594): ``(labels (1, N) int64 on the host or None,
+    means, covariances, weights, info)``.  Rows stream through the GPU in
+    ``chunk_size_N``-row chunks (em_fit_streamed).  ``chunk_size_K``, the
+    k-means and Triton arguments and ``max_init_samples`` steer only the
+    reference's own kernels and initialisation and are validated, not needed;
+    initial means are ``n_components`` rows drawn with ``seed`` (the
+    reference's fallback when flash_kmeans is absent)."""
+    del kmeans_init_iters, kmeans_init_tol, kmeans_use_triton, gmm_use_triton, max_init_samples, legacy_no_triton
+    device = _validate_large_n_input(x_cpu, device)
+    if covariance_type not in _COV_TYPES:
+        raise ValueError("covariance_type must be 'spherical', 'diag', 'tied', or 'full'")
+    if n_components <= 0:
+        raise ValueError("n_components must be positive")
+    if max_iters <= 0:
+        raise ValueError("max_iters must be positive")
+    if chunk_size_N <= 0 or chunk_size_K <= 0:
+        raise ValueError("chunk_size_N and chunk_size_K must be positive")
+    if min_weight <= 0.0:
+        raise ValueError("min_weight must be positive")
+    _check_backend(backend)
+    x = _compute_input(x_cpu, dtype)
+    torch.manual_seed(seed)
+    labels, means, cov, weights, info = em_fit_streamed(
+        covariance_type, x, int(n_components), device=device, chunk_rows=int(chunk_size_N), max_iters=max_iters,
+        tol=tol, init_params=init_params, reg_covar=reg_covar, min_weight=min_weight,
+        compute_labels=compute_labels, verbose=verbose, approx_top_k=approx_top_k)
+    info = dict(info, fallback_reason=None)
+    return (None if labels is None else labels.cpu()), means, cov, weights, info
+
+
+def _predict_to_host(kind: str, x_cpu, means, variances, weights, covariance_type, device, dtype, chunk_size_N,
+                     chunk_size_K, backend):
+    device = _validate_large_n_input(x_cpu, device)
+    if covariance_type not in _COV_TYPES:
+        raise ValueError("covariance_type must be 'spherical', 'diag', 'tied', or 'full'")
+    if chunk_size_N <= 0 or chunk_size_K <= 0:
+        raise ValueError("chunk_size_N and chunk_size_K must be positive")
+    _check_backend(backend)
+    x = _compute_input(x_cpu, dtype)
+    n, k = x.shape[1], means.shape[1]
+    fn = {"assign": engine.assign, "score_samples": engine.score_samples,
+          "predict_proba": engine.predict_proba}[kind]
+    shape, out_dtype = {"assign": ((1, n), torch.int64), "score_samples": ((1, n), torch.float32),
+                        "predict_proba": ((1, n, k), torch.float32)}[kind]
+    out = torch.empty(shape, dtype=out_dtype)
+    with torch.cuda.device(device):
+        st = ChunkStreamer(x, int(chunk_size_N), device)
+        for xc, n0 in st.chunks():
+            out[:, n0:n0 + xc.shape[1]] = fn(covariance_type, xc, means, variances, weights).cpu()
+    return out
+
+
+def large_n_predict_cpu(x_cpu, means, variances, weights, *, covariance_type: str, device, dtype, chunk_size_N: int,
+                        chunk_size_K: int, use_triton: bool = True, return_triton_used: bool = False,
+                        return_backend_used: bool = False, backend: str = "auto", legacy_no_triton: bool = False):
+    """Labels (1, N) int64 on the host for host-resident X (the reference's
+    large_n.py:1907-2075); with ``return_backend_used`` also "cuda", with
+    ``return_triton_used`` also False."""
+    del use_triton, legacy_no_triton
+    labels = _predict_to_host("assign", x_cpu, means, variances, weights, covariance_type, device, dtype,
+                              chunk_size_N, chunk_size_K, backend)
+    if return_backend_used:
+        return labels, "cuda"
+    if return_triton_used:
+        return labels, False
+    return labels
+
+
+def large_n_score_samples_cpu(x_cpu, means, variances, weights, *, covariance_type: str, device, dtype,
+                              chunk_size_N: int, chunk_size_K: int, use_triton: bool = True, backend: str = "auto",
+                              legacy_no_triton: bool = False, return_backend_used: bool = False):
+    """Per-row log-likelihood (1, N) fp32 on the host (the reference's
+    large_n.py:2078-2256)."""
+    del use_triton, legacy_no_triton
+    scores = _predict_to_host("score_samples", x_cpu, means, variances, weights, covariance_type, device, dtype,
+                              chunk_size_N, chunk_size_K, backend)
+    return (scores, "cuda") if return_backend_used else scores
+
+
+def large_n_predict_proba_cpu(x_cpu, means, variances, weights, *, covariance_type: str, device, dtype,
+                              chunk_size_N: int, chunk_size_K: int, use_triton: bool = True, backend: str = "auto",
+                              legacy_no_triton: bool = False, return_backend_used: bool = False):
+    """Responsibilities (1, N, K) fp32 on the host (the reference's
+    large_n.py:2259-2502)."""
+    del use_triton, legacy_no_triton
+    probs = _predict_to_host("predict_proba", x_cpu, means, variances, weights, covariance_type, device, dtype,
+                             chunk_size_N, chunk_size_K, backend)
+    return (probs, "cuda") if return_backend_used else probs
