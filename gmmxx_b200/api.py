@@ -169,14 +169,110 @@ batch_gmm_full = batch_gmm_Full
 batch_gmm_tied = batch_gmm_Tied
 
 
+# --- the reference's *_torch_native names (torch_fallback.py:1897-3336) -------
+# Same parameters as the reference's loops; the Triton and k-means switches
+# steer only the reference's own kernels and are validated, not needed.  They
+# run on this engine (CUDA tensors), not on torch.
+
+
+def _check_switch(name, value):
+    if not isinstance(value, bool) and value != "auto":
+        raise ValueError(f"{name} must be a bool or 'auto'")
+
+
+def batch_gmm_Spherical_torch_native(
+    x: torch.Tensor,
+    n_components: int,
+    max_iters: int = 100,
+    tol: float = 1e-4,
+    init_means: Optional[torch.Tensor] = None,
+    init_variances: Optional[torch.Tensor] = None,
+    init_weights: Optional[torch.Tensor] = None,
+    verbose: bool = False,
+    *,
+    init_params: str = "kmeans",
+    reg_covar: float = 1e-6,
+    chunk_size_N: int = 32768,
+    chunk_size_K: int = 1024,
+    kmeans_init_iters: int = 10,
+    kmeans_init_tol: float = 1e-4,
+    kmeans_use_triton: bool = True,
+    gmm_use_triton_estep="auto",
+    gmm_use_triton_streaming_update="auto",
+    min_weight: float = 1e-8,
+    compute_labels: bool = True,
+    approx_top_k: Optional[int] = None,
+):
+    """Spherical soft EM with the reference loop's parameters
+    (torch_fallback.py:1897-2397)."""
+    _check_switch("gmm_use_triton_estep", gmm_use_triton_estep)
+    _check_switch("gmm_use_triton_streaming_update", gmm_use_triton_streaming_update)
+    return _fit("spherical", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+
+
+def _matrix_native(cov_type, doc):
+    def fit(
+        x: torch.Tensor,
+        n_components: int,
+        max_iters: int = 100,
+        tol: float = 1e-4,
+        init_means: Optional[torch.Tensor] = None,
+        init_variances: Optional[torch.Tensor] = None,
+        init_weights: Optional[torch.Tensor] = None,
+        verbose: bool = False,
+        *,
+        init_params: str = "kmeans",
+        reg_covar: float = 1e-6,
+        chunk_size_N: int = 32768,
+        chunk_size_K: int = 1024,
+        kmeans_init_iters: int = 10,
+        kmeans_init_tol: float = 1e-4,
+        kmeans_use_triton: bool = True,
+        gmm_use_triton="auto",
+        min_weight: float = 1e-8,
+        compute_labels: bool = True,
+        approx_top_k: Optional[int] = None,
+    ):
+        _check_switch("gmm_use_triton", gmm_use_triton)
+        return _fit(cov_type, x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
+                    init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+
+    fit.__doc__ = doc
+    return fit
+
+
+batch_gmm_Diagonal_torch_native = _matrix_native(
+    "diag", "Diagonal soft EM with the reference loop's parameters (torch_fallback.py:2401-2728).")
+batch_gmm_Diagonal_torch_native.__name__ = "batch_gmm_Diagonal_torch_native"
+batch_gmm_Full_torch_native = _matrix_native(
+    "full", "Full-covariance soft EM with the reference loop's parameters (torch_fallback.py:3247-3290).")
+batch_gmm_Full_torch_native.__name__ = "batch_gmm_Full_torch_native"
+batch_gmm_Tied_torch_native = _matrix_native(
+    "tied", "Tied-covariance soft EM with the reference loop's parameters (torch_fallback.py:3293-3336).")
+batch_gmm_Tied_torch_native.__name__ = "batch_gmm_Tied_torch_native"
+
+
 # --- inference (torch_fallback.py:780-1345) ----------------------------------
 
 
 def _inf(fn, cov_type):
-    def run(x, means, covariances, weights, *, chunk_size_N: int = 32768, chunk_size_K: int = 1024):
+    """The inference call with the reference's parameter names: ``variances``
+    (spherical, diag), ``covariance`` (tied), ``covariances`` (full)."""
+    def call(x, means, params, weights, chunk_size_N, chunk_size_K):
         if chunk_size_N <= 0 or chunk_size_K <= 0:
             raise ValueError("chunk_size_N and chunk_size_K must be positive")
-        return fn(cov_type, x, means, covariances, weights)
+        return fn(cov_type, x, means, params, weights)
+
+    if cov_type in ("spherical", "diag"):
+        def run(x, means, variances, weights, *, chunk_size_N: int = 32768, chunk_size_K: int = 1024):
+            return call(x, means, variances, weights, chunk_size_N, chunk_size_K)
+    elif cov_type == "tied":
+        def run(x, means, covariance, weights, *, chunk_size_N: int = 32768, chunk_size_K: int = 1024):
+            return call(x, means, covariance, weights, chunk_size_N, chunk_size_K)
+    else:
+        def run(x, means, covariances, weights, *, chunk_size_N: int = 32768, chunk_size_K: int = 1024):
+            return call(x, means, covariances, weights, chunk_size_N, chunk_size_K)
 
     run.__name__ = f"{cov_type}_{fn.__name__}"
     run.__doc__ = f"{fn.__doc__} ({cov_type} covariance)"
@@ -195,3 +291,18 @@ tied_predict_proba = _inf(engine.predict_proba, "tied")
 full_assign = _inf(engine.assign, "full")
 full_score_samples = _inf(engine.score_samples, "full")
 full_predict_proba = _inf(engine.predict_proba, "full")
+
+
+# the reference's inference names (torch_fallback.py:780-1345)
+spherical_assign_torch_native_chunked = spherical_assign
+spherical_score_samples_torch_native_chunked = spherical_score_samples
+spherical_predict_proba_torch_native_chunked = spherical_predict_proba
+diagonal_assign_torch_native_chunked = diagonal_assign
+diagonal_score_samples_torch_native_chunked = diagonal_score_samples
+diagonal_predict_proba_torch_native_chunked = diagonal_predict_proba
+tied_assign_torch_native_chunked = tied_assign
+tied_score_samples_torch_native_chunked = tied_score_samples
+tied_predict_proba_torch_native_chunked = tied_predict_proba
+full_assign_torch_native_chunked = full_assign
+full_score_samples_torch_native_chunked = full_score_samples
+full_predict_proba_torch_native_chunked = full_predict_proba

@@ -1,0 +1,62 @@
+"""The functional API's names and parameters are the reference's
+(gmmxx/__init__.py:11-34, torch_fallback.py:780-1345, 1897-3513), and its
+argument checks run on the host before any kernel."""
+
+import inspect
+
+import pytest
+import torch
+
+import gmmxx_b200 as G
+
+FIT_COMMON = ["x", "n_components", "max_iters", "tol", "init_means", "init_variances", "init_weights", "verbose",
+              "init_params", "reg_covar", "chunk_size_N", "chunk_size_K", "kmeans_init_iters", "kmeans_init_tol"]
+TAIL = ["min_weight", "compute_labels", "approx_top_k"]
+
+
+@pytest.mark.parametrize("name,switches", [
+    ("batch_gmm_Spherical", ["use_triton"]),
+    ("batch_gmm_Diagonal", ["use_triton"]),
+    ("batch_gmm_Full", ["use_triton"]),
+    ("batch_gmm_Tied", ["use_triton"]),
+    ("batch_gmm_Spherical_torch_native",
+     ["kmeans_use_triton", "gmm_use_triton_estep", "gmm_use_triton_streaming_update"]),
+    ("batch_gmm_Diagonal_torch_native", ["kmeans_use_triton", "gmm_use_triton"]),
+    ("batch_gmm_Full_torch_native", ["kmeans_use_triton", "gmm_use_triton"]),
+    ("batch_gmm_Tied_torch_native", ["kmeans_use_triton", "gmm_use_triton"]),
+])
+def test_fit_signatures(name, switches):
+    params = list(inspect.signature(getattr(G, name)).parameters)
+    assert params == FIT_COMMON + switches + TAIL
+
+
+@pytest.mark.parametrize("cov,third", [("spherical", "variances"), ("diagonal", "variances"),
+                                       ("tied", "covariance"), ("full", "covariances")])
+@pytest.mark.parametrize("kind", ["assign", "score_samples", "predict_proba"])
+def test_inference_signatures(cov, third, kind):
+    for name in (f"{cov}_{kind}", f"{cov}_{kind}_torch_native_chunked"):
+        fn = getattr(G, name)
+        assert list(inspect.signature(fn).parameters) == ["x", "means", third, "weights", "chunk_size_N",
+                                                          "chunk_size_K"], name
+
+
+def test_lowercase_aliases():
+    assert G.batch_gmm_spherical is G.batch_gmm_Spherical
+    assert G.batch_gmm_diag is G.batch_gmm_Diagonal and G.batch_gmm_diagonal is G.batch_gmm_Diagonal
+    assert G.batch_gmm_full is G.batch_gmm_Full and G.batch_gmm_tied is G.batch_gmm_Tied
+
+
+@pytest.mark.parametrize("call,exc", [
+    (lambda x: G.batch_gmm_Diagonal_torch_native(x, 3, gmm_use_triton="sometimes"), ValueError),
+    (lambda x: G.batch_gmm_Spherical_torch_native(x, 3, gmm_use_triton_estep="x"), ValueError),
+    (lambda x: G.batch_gmm_Spherical(x, 3, approx_top_k=0), ValueError),
+    (lambda x: G.batch_gmm_Spherical(x, 0), ValueError),
+    (lambda x: G.batch_gmm_Tied(x, 3, chunk_size_N=0), ValueError),
+    (lambda x: G.batch_gmm_Full(x, 3, min_weight=0.0), ValueError),
+    (lambda x: G.batch_gmm_Spherical(x[0], 3), ValueError),          # not (B, N, D)
+    (lambda x: G.batch_gmm_Spherical(x, 3), ValueError),             # host tensor: the engine needs CUDA
+    (lambda x: G.spherical_assign(x, x[:, :2], torch.ones(1, 2), torch.ones(1, 2), chunk_size_N=0), ValueError),
+])
+def test_argument_checks(call, exc):
+    with pytest.raises(exc):
+        call(torch.zeros(1, 8, 2))
