@@ -8,8 +8,9 @@ test_cuda_diag_safe.py, test_cuda_tied.py, test_cuda_full.py,
 test_cuda_approx_topk_spherical.py).
 
 Tolerances: fp32 log-sum-exp and statistics within 1e-4 relative / 1e-4
-absolute, responsibilities within 1e-5 absolute, labels equal on >= 99.9 % of
-rows (rows whose two best logits tie to fp32 rounding may differ)."""
+absolute, responsibilities within 5e-5 absolute (fp32 logits of magnitude
+~100 carry ~1e-5 of rounding), labels equal on >= 99.9 % of rows (rows whose
+two best logits tie to fp32 rounding may differ)."""
 
 import math
 
@@ -59,7 +60,7 @@ def _check_estep(lg, ids, lse, r):
     assert ids.dtype == torch.int32 and ids.shape == lg.shape[:2]
     assert (ids.cpu().long() == lg.argmax(-1)).double().mean() >= 0.999
     np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.numpy(), **TOL)
-    np.testing.assert_allclose(r.cpu().numpy(), torch.exp(lg - ref_lse[..., None]).numpy(), atol=1e-5)
+    np.testing.assert_allclose(r.cpu().numpy(), torch.exp(lg - ref_lse[..., None]).numpy(), atol=5e-5)
 
 
 @pytest.mark.parametrize("cov", ["spherical", "diag"])
@@ -115,7 +116,7 @@ def test_full_estep_matches_reference_golden(cuda_device):
     assert ids.dtype == torch.int32
     assert (ids.cpu().numpy() == g["assign"]).mean() >= 0.999
     np.testing.assert_allclose(lse.cpu().numpy(), g["lse"], **TOL)
-    np.testing.assert_allclose(r.cpu().numpy(), g["resp"], atol=1e-5)
+    np.testing.assert_allclose(r.cpu().numpy(), g["resp"], atol=5e-5)
 
 
 def _soft_stats_ref(x, means, var, log_w):
