@@ -515,8 +515,8 @@ def predict_proba(cov_type, x, means, cov, weights, out: Optional[torch.Tensor] 
     covc, x, means, cov, weights, ws, (b, n, d, k) = _infer_args(cov_type, x, means, cov, weights)
     if out is None:
         out = torch.empty((b, n, k), dtype=torch.float32, device=x.device)
-    elif out.shape != (b, n, k) or out.dtype != torch.float32 or not out.is_contiguous():
-        raise ValueError("out must be a contiguous float32 (B, N, K) tensor")
+    elif out.shape != (b, n, k) or out.dtype != torch.float32 or not out.is_contiguous() or out.device != x.device:
+        raise ValueError("out must be a contiguous float32 (B, N, K) tensor on x's device")
     with torch.cuda.device(x.device):
         nat.call("gmmxx_predict_proba", covc, _X_DTYPES[x.dtype], x.data_ptr(), b, n, d, k, means.data_ptr(),
                  cov.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
