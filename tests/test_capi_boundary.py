@@ -213,3 +213,23 @@ def test_entry_points_validate_every_pointer_before_launching(lib):
     # a misaligned workspace is refused the same way
     assert lib.gmmxx_assign(*infer_args(p)[:11], ws + 8, wsb, None) == _native.ERR_INVALID
     assert b"aligned" in lib.gmmxx_last_error()
+
+
+def test_missing_library_raises_cuda_backend_unavailable():
+    """No fallback when the native library is absent (the reference's
+    CudaBackendUnavailable, gmmxx/_cuda.py:57-64): a fresh interpreter whose
+    library path does not exist gets the exception from load(), with the
+    build command in its message."""
+    import subprocess
+    import sys
+
+    code = (
+        "from gmmxx_b200 import _native as nat\n"
+        "try:\n"
+        "    nat.load('/nonexistent/libgmmxx_b200.so')\n"
+        "except nat.CudaBackendUnavailable as e:\n"
+        "    print('unavailable:', 'not built' in str(e))\n"
+    )
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert "unavailable: True" in out.stdout
