@@ -47,8 +47,9 @@ class OracleOps:
     the second moment being sum r x^2 (diag, D), sum r |x|^2 (spherical, 1),
     nothing (tied) or sum r x x^T (full, D*D)."""
 
-    def __init__(self, cov_type: str, x_shard: np.ndarray, k: int):
+    def __init__(self, cov_type: str, x_shard: np.ndarray, k: int, top_k=None):
         self.cov_type = cov_type
+        self.top_k = top_k  # approximate EM: responsibilities over each row's top_k logits
         self.x = x_shard.astype(np.float64)
         self.b, self.n, self.d = self.x.shape
         self.k = k
@@ -71,8 +72,15 @@ class OracleOps:
         x = self.x
         xsq = np.square(x).sum(axis=-1)
         lg = self._model.logits(x, xsq, 0, self.k)
-        lse = orc._logsumexp(lg)
-        r = np.exp(lg - lse[:, :, None])
+        if self.top_k is not None:
+            order = np.argsort(-lg, axis=-1, kind="stable")[..., :self.top_k]
+            vals = np.take_along_axis(lg, order, axis=-1)
+            lse = orc._logsumexp(vals)
+            r = np.zeros_like(lg)
+            np.put_along_axis(r, order, np.exp(vals - lse[:, :, None]), axis=-1)
+        else:
+            lse = orc._logsumexp(lg)
+            r = np.exp(lg - lse[:, :, None])
         d = self.d
         st = np.zeros((self.b, self.k, self.stat_width))
         st[..., 0] = r.sum(axis=1)
@@ -142,7 +150,7 @@ def _problem(cov_type, seed=7, b=2, n=600, d=3, k=4):
     return x, init_m, init_c, init_w
 
 
-def _rank_main(rank, world, port, cov_type, iters, out_dir, fail_rank):
+def _rank_main(rank, world, port, cov_type, iters, out_dir, fail_rank, top_k=None):
     from gmmxx_b200 import engine
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -152,7 +160,7 @@ def _rank_main(rank, world, port, cov_type, iters, out_dir, fail_rank):
         x, m0, c0, w0 = _problem(cov_type)
         n = x.shape[1]
         lo, hi = rank * n // world, (rank + 1) * n // world
-        ops = OracleOps(cov_type, x[:, lo:hi], m0.shape[1])
+        ops = OracleOps(cov_type, x[:, lo:hi], m0.shape[1], top_k)
         means = torch.from_numpy(m0.copy())
         cov = torch.from_numpy(c0.copy())
         weights = torch.from_numpy(w0.copy())
@@ -171,10 +179,10 @@ def _rank_main(rank, world, port, cov_type, iters, out_dir, fail_rank):
             dist.destroy_process_group()
 
 
-def _launch(cov_type, iters, tmp_path, fail_rank=-1, world=2):
+def _launch(cov_type, iters, tmp_path, fail_rank=-1, world=2, top_k=None):
     port = _free_port()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, cov_type, iters, str(tmp_path), fail_rank))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, cov_type, iters, str(tmp_path), fail_rank, top_k))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -206,6 +214,27 @@ def test_sharded_fit_matches_single_process(cov_type, tmp_path):
     np.testing.assert_allclose(r0["cov"], c, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(r0["weights"], w, rtol=1e-5, atol=1e-7)
     # the last bound is the mean log-likelihood over all rows of both shards
+    np.testing.assert_allclose(r0["hist"][-1], info["lower_bound_history"][-1], rtol=1e-6)
+
+
+def test_sharded_approx_fit_matches_single_process(tmp_path):
+    """Approximate top-k EM (each row's responsibilities over its 2 best of 4
+    components) sharded over two ranks equals the single-process oracle's
+    approximate EM: the top-k lists are per row, so sharding changes only the
+    summation order of the statistics."""
+    codes = _launch("diag", 4, tmp_path, top_k=2)
+    assert codes == [0, 0]
+    r0 = np.load(tmp_path / "r0.npz")
+    r1 = np.load(tmp_path / "r1.npz")
+    for key in ("means", "cov", "weights", "hist"):
+        assert np.array_equal(r0[key], r1[key]), f"ranks disagree on {key}"
+    x, m0, c0, w0 = _problem("diag")
+    _, m, c, w, info = orc.fit("diag", x, m0.shape[1], 4, 0.0, m0, c0, w0, compute_labels=False, dtype=np.float64,
+                               approx_top_k=2)
+    assert info["approximate_em_enabled"]
+    np.testing.assert_allclose(r0["means"], m, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(r0["cov"], c, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(r0["weights"], w, rtol=1e-5, atol=1e-7)
     np.testing.assert_allclose(r0["hist"][-1], info["lower_bound_history"][-1], rtol=1e-6)
 
 
