@@ -4,8 +4,10 @@ public names (gmmxx/cuda_ops.py:55-87), its argument checks
 and the finalize / projection algebra against golden vectors recorded from
 the reference's own operators (tests/golden/make_operator_golden.py).  The
 algebra runs here on CPU tensors with the operators' CUDA-device check
-replaced for the test; everything that launches a kernel is in
-tests/test_gpu_cuda_ops.py."""
+replaced for the test.  The GPU operator tests (tests/test_gpu_cuda_ops.py)
+also run here once with the kernel calls replaced by host fakes, which
+checks each operator's own argument handling and finalize rules; the GPU run
+checks the kernels."""
 
 import numpy as np
 import pytest
@@ -98,3 +100,84 @@ def test_tied_project_and_log_det_match_reference(host_checks):
     y = cuda_ops.tied_project(_t(g, "x"), _t(g, "L"))
     np.testing.assert_allclose(y.numpy(), g["y"], rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(cuda_ops.tied_log_det(_t(g, "L")).numpy(), g["log_det"], rtol=1e-6)
+
+
+class _FakeOps:
+    """Stand-in for engine.CudaOps on the host: the per-iteration prologue
+    (variance floor, weight floor and renormalisation) and the spherical
+    statistics of exact or top-k EM, from the oracle's float32 logits."""
+
+    def __init__(self, cov, x, k, top_k=None):
+        self.cov, self.x, self.k, self.top_k = cov, x, k, top_k
+        self.stat_width = x.shape[-1] + 2
+
+    def prepare(self, m, v, w, reg, mw):
+        v.clamp_(min=reg)
+        w.clamp_(min=mw)
+        w /= w.sum(-1, keepdim=True)
+        self.params = (m, v, w)
+
+    def accumulate(self, stats, ll):
+        lg = _oracle_logits(self.cov, self.x, *self.params).double()
+        if self.top_k:
+            vals, idx = lg.topk(self.top_k, -1)
+            lse = torch.logsumexp(vals, -1)
+            r = torch.zeros_like(lg).scatter_(-1, idx, torch.exp(vals - lse[..., None]))
+        else:
+            lse = torch.logsumexp(lg, -1)
+            r = torch.exp(lg - lse[..., None])
+        x = self.x.double()
+        d = x.shape[-1]
+        stats[..., 0] += r.sum(1).float()
+        stats[..., 1:1 + d] += (r.transpose(1, 2) @ x).float()
+        stats[..., 1 + d] += (r * x.square().sum(-1)[..., None]).sum(1).float()
+        ll += lse.sum()
+
+
+def _oracle_logits(cov, x, means, c, w):
+    import oracle
+
+    return torch.from_numpy(oracle.component_logits(cov, x.float().numpy(), means.float().numpy(),
+                                                    c.float().numpy(), w.float().numpy()))
+
+
+@pytest.fixture
+def fake_engine(monkeypatch, host_checks):
+    """The kernel calls of cuda_ops replaced by host fakes built on the oracle
+    (test infrastructure), so that each operator's own argument handling and
+    finalize algebra run on the CPU."""
+    import contextlib
+
+    from gmmxx_b200 import engine
+
+    monkeypatch.setattr(engine, "assign", lambda cov, x, m, c, w: _oracle_logits(cov, x, m, c, w).argmax(-1))
+    monkeypatch.setattr(engine, "score_samples",
+                        lambda cov, x, m, c, w: torch.logsumexp(_oracle_logits(cov, x, m, c, w), -1))
+    monkeypatch.setattr(engine, "resp",
+                        lambda cov, x, m, c, w, ln: torch.exp(_oracle_logits(cov, x, m, c, w) - ln[..., None]))
+    monkeypatch.setattr(engine, "canary_add_offset", lambda t, o: t + o)
+    monkeypatch.setattr(engine, "CudaOps", _FakeOps)
+    monkeypatch.setattr(cuda_ops, "has_cuda", lambda: True)
+    monkeypatch.setattr(torch.cuda, "device", lambda d: contextlib.nullcontext())
+
+
+@pytest.mark.parametrize("name,kwargs", [
+    ("test_spherical_and_diag_estep", dict(cov="spherical", dtype=torch.float32)),
+    ("test_spherical_and_diag_estep", dict(cov="diag", dtype=torch.bfloat16)),
+    ("test_tied_estep", {}),
+    ("test_full_estep_matches_reference_golden", {}),
+    ("test_soft_update_spherical", {}),
+    ("test_fused_spherical", {}),
+    ("test_approx_topk_matches_reference_golden", dict(case="approx_small")),
+    ("test_approx_topk_matches_reference_golden", dict(case="approx_k150")),
+    ("test_approx_topk_arguments", {}),
+    ("test_finalize_operators_on_device", dict(case="full_finalize")),
+    ("test_canary_and_availability", {}),
+])
+def test_operator_host_logic_with_a_fake_engine(fake_engine, name, kwargs):
+    """The GPU operator tests (tests/test_gpu_cuda_ops.py) run on the CPU with
+    the engine faked: this checks the operators' own host logic and the
+    tests' expectations; the GPU run checks the kernels behind them."""
+    import test_gpu_cuda_ops as gpu_tests
+
+    getattr(gpu_tests, name)(torch.device("cpu"), **kwargs)
