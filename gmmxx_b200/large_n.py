@@ -11,6 +11,7 @@ handles B == 1.
 
 from __future__ import annotations
 
+import os
 import time
 from typing import Optional
 
@@ -224,8 +225,6 @@ def _validate_large_n_input(x_cpu: torch.Tensor, device) -> torch.device:
 def _check_backend(backend: str) -> None:
     """backend (with GMMXX_BACKEND consulted for "auto") must resolve to this
     engine; the reference's torch and Triton backends are not provided."""
-    import os
-
     valid = ("auto", "cuda", "triton", "torch")
     if backend not in valid:
         raise ValueError(f"backend must be one of {valid}, got {backend!r}")
