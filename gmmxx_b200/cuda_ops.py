@@ -136,7 +136,7 @@ def _spherical_stats(x, means, var, log_w, top_k: Optional[int] = None):
     """(n_k, sum r x, sum r |x|^2, sum of the rows' log-sum-exp) for the
     parameters as given: the engine's per-iteration prologue runs on copies
     with a variance floor of 1e-30 (the reference's clamp in
-    approx_topk_update_spherical, _cuda.py:830) and a negligible weight floor,
+    approx_topk_update_spherical, _cuda.py:829) and a negligible weight floor,
     and the weights it renormalises are corrected for in the log-likelihood."""
     b, n, d = x.shape
     k = means.shape[1]
