@@ -124,8 +124,9 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_baseline(cfg, mix, init, rows: int, iters: int = 1):
-    """The oracle (numpy port of the reference torch path) on a bounded sample."""
+def cpu_baseline(cfg, mix, init, rows: int, iters: int = 1, approx_top_k=None):
+    """The oracle (numpy port of the reference torch path) on a bounded sample
+    (approximate top-k EM when ``approx_top_k`` is given)."""
     import torch
 
     import oracle
@@ -134,7 +135,7 @@ def cpu_baseline(cfg, mix, init, rows: int, iters: int = 1):
     x = synthetic.sample_rows(cfg, mix, rows, torch.device("cpu"), seed=12345).float().numpy()
     means, cov, w = init
     t0 = time.perf_counter()
-    oracle.fit(cfg.cov_type, x, cfg.K, iters, 0.0, means, cov, w, compute_labels=False)
+    oracle.fit(cfg.cov_type, x, cfg.K, iters, 0.0, means, cov, w, compute_labels=False, approx_top_k=approx_top_k)
     dt = time.perf_counter() - t0
     return {"value": rows * cfg.B * iters / dt, "unit": "samples/s", "cores": os.cpu_count(),
             "kind": "port", "sample": f"{cfg.B}x{rows} rows of config {cfg.index}, {iters} EM iteration(s), "
@@ -153,9 +154,9 @@ def run_reference(args, cfg):
     rows = args.ref_rows
     vals = []
     for _ in range(args.warmup):
-        cpu_baseline(cfg, mix, init, rows)
+        cpu_baseline(cfg, mix, init, rows, approx_top_k=args.approx_top_k)
     for _ in range(args.steps):
-        vals.append(cpu_baseline(cfg, mix, init, rows)["value"])
+        vals.append(cpu_baseline(cfg, mix, init, rows, approx_top_k=args.approx_top_k)["value"])
     v = statistics.median(vals)
     line = {
         "impl": "reference", "metric": "EM samples/s per iteration", "value": v, "unit": "samples/s",
@@ -230,10 +231,14 @@ def run_infer(args, cfg, x, means, cov, weights):
 def workload_config(cfg, args):
     names = {0: "configs[0] spherical", 1: "configs[1] diag", 2: "configs[2] tied", 3: "configs[3] full",
              4: "configs[4] spherical large-K"}
-    return {"workload": f"{names[cfg.index]} GMM EM iteration", "covariance_type": cfg.cov_type,
+    conf = {"workload": f"{names[cfg.index]} GMM EM iteration", "covariance_type": cfg.cov_type,
             "x_dtype": str(cfg.dtype).replace("torch.", ""), "B": cfg.B, "N": cfg.N, "D": cfg.D, "K": cfg.K,
             "parallelism": f"dp{args.gpus} (rows sharded, stats allreduce)",
             "l2": "inputs larger than L2 (126 MB); no flush needed"}
+    if args.approx_top_k:
+        conf["workload"] = f"{names[cfg.index]} GMM approximate top-{args.approx_top_k} EM iteration"
+        conf["approx_top_k"] = args.approx_top_k
+    return conf
 
 
 def main():
@@ -251,8 +256,12 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--infer", choices=["predict", "score", "proba"], default=None,
                     help="time an inference call (labels / score_samples / predict_proba) instead of EM")
+    ap.add_argument("--approx-top-k", type=int, default=None,
+                    help="time approximate top-k EM (CUDA-core kernels) instead of exact EM; no e2e leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.approx_top_k:
+        args.no_e2e = True
 
     from gmmxx_b200 import synthetic
 
@@ -296,7 +305,8 @@ def main():
             raise SystemExit("--infer runs on one GPU")
         run_infer(args, cfg, x, means, cov, weights)
         return
-    ops = engine.CudaOps(cfg.cov_type, x, cfg.K)
+    top_k = engine.resolve_approx_top_k(args.approx_top_k, cfg.K)
+    ops = engine.CudaOps(cfg.cov_type, x, cfg.K, top_k)
     B, D, K = cfg.B, cfg.D, cfg.K
     stats = torch.zeros((B, K, ops.stat_width), dtype=torch.float32, device=dev)
     ll = torch.zeros((1,), dtype=torch.float64, device=dev)
@@ -438,7 +448,8 @@ def main():
         }
         if world == 1 and not args.no_cpu:
             try:
-                line["cpu_baseline"] = cpu_baseline(cfg, mix, (init_means, init_cov, init_w), args.cpu_rows)
+                line["cpu_baseline"] = cpu_baseline(cfg, mix, (init_means, init_cov, init_w), args.cpu_rows,
+                                                    approx_top_k=args.approx_top_k)
             except Exception as exc:  # report, never fake
                 line["cpu_baseline"] = {"error": repr(exc)}
         print(json.dumps(line), flush=True)
