@@ -51,14 +51,16 @@ def algorithmic_flops(cov: str, n: int, d: int, k: int) -> float:
     return 2.0 * n * k * (d + q) + 2.0 * n * k * (1 + d + q)
 
 
-def launches_per_iteration(cfg, tc_path: bool) -> int:
+def launches_per_iteration(cfg, tc_path: bool, approx: bool = False) -> int:
     """Kernels of this library launched per EM iteration: prep_weights +
     prep_table (+ 2 Cholesky kernels for tied / full), the statistics kernels,
-    finalize (per component, then per problem).  Statistics: 3 (pack, tensor-core kernel, reduce; or rows, mstep,
-    reduce), and for spherical K > 1024 the grouped passes: pack, G row-partial
+    finalize (per component, then per problem).  Statistics: 3 (pack,
+    tensor-core kernel, reduce; or rows, mstep, reduce; or the two approximate
+    top-k passes and reduce); 2 for the one-pass K <= 64 kernel and its
+    reduce; for spherical K > 1024 the grouped passes: pack, G row-partial
     launches, combine, log-likelihood sum, G x (M-step launch + reduce)."""
     prep = 2 + (2 if cfg.cov_type in ("tied", "full") else 0)
-    stats = 2 if (not tc_path and cfg.K <= 64) else 3  # one-pass CUDA-core kernel + reduce for K <= 64
+    stats = 2 if (not tc_path and not approx and cfg.K <= 64) else 3  # K <= 64: one-pass kernel + reduce
     if tc_path and cfg.cov_type == "spherical" and cfg.K > 1024:
         groups = (((cfg.K + 127) // 128) + 7) // 8
         stats = 3 + 3 * groups
@@ -414,8 +416,8 @@ def main():
 
     if rank == 0:
         peaks = load_peaks()
-        tc_path = nat.accumulate_path(engine.cov_code(cfg.cov_type), engine._X_DTYPES[cfg.dtype], cfg.B, n_local, D,
-                                      K) == 1
+        tc_path = top_k is None and nat.accumulate_path(engine.cov_code(cfg.cov_type), engine._X_DTYPES[cfg.dtype],
+                                                        cfg.B, n_local, D, K) == 1
         flops = algorithmic_flops(cfg.cov_type, n_local * cfg.B, D, K)
         achieved = flops / (acc_ms / 1e3) / 1e12
         long_run = ms * args.steps > 1000.0
@@ -436,6 +438,7 @@ def main():
                          "frac": achieved / peak, "traffic": traffic,
                          "kernel": ((("em_tc_diag_kernel" if cfg.cov_type == "diag" else "em_tc_kernel")
                                      + " (+ tc_pack_kernel, tc_reduce_kernel)") if tc_path
+                                    else "topk_rows_kernel + topk_mstep_kernel + stats_reduce_kernel" if top_k
                                     else ("em_small_kernel + stats_reduce_kernel" if cfg.K <= 64
                                           else "rows_kernel + mstep_kernel + stats_reduce_kernel")),
                          "peak_source": f"{peaks['source']} bf16 {'sustained' if long_run else 'burst'}",
@@ -443,7 +446,7 @@ def main():
                          "hbm_frac": (n_local * cfg.B * D * torch.empty((), dtype=cfg.dtype).element_size()) /
                                      (acc_ms / 1e3) / 1e9 / peaks["hbm_gbs"]},
             "clocks": clocks,
-            "gpu_launches": args.steps * launches_per_iteration(cfg, tc_path),
+            "gpu_launches": args.steps * launches_per_iteration(cfg, tc_path, top_k is not None),
             "e2e": e2e,
         }
         if world == 1 and not args.no_cpu:
