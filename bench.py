@@ -424,7 +424,7 @@ def main():
         peak = peaks["bf16_sus"] if long_run else peaks["bf16"]
         traffic = None
         tpath = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tpath):
+        if os.path.exists(tpath) and top_k is None:  # the captured traffic is the exact-EM kernel's
             with open(tpath) as f:
                 tr = json.load(f).get(f"config{cfg.index}")
             if tr:
