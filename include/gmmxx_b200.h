@@ -92,9 +92,11 @@ GMMXX_API int64_t gmmxx_stat_width(int cov_type, int64_t D);
 GMMXX_API size_t gmmxx_workspace_bytes(int cov_type, int64_t B, int64_t N, int64_t D, int64_t K);
 
 /* Which statistics kernels gmmxx_em_accumulate launches for this shape:
- * *path_out = 1 for the tensor-core kernel (tc_pack_kernel, em_tc_kernel,
- * tc_reduce_kernel), 0 for the CUDA-core kernels (rows_kernel, mstep_kernel,
- * stats_reduce_kernel).  Honours GMMXX_B200_KERNEL.  A device that cannot
+ * *path_out = 1 for the tensor-core kernels (tc_pack_kernel, then
+ * em_tc_diag_kernel for diag or em_tc_kernel for spherical, then
+ * tc_reduce_kernel), 0 for the CUDA-core kernels (rows_kernel, mstep_kernel
+ * and stats_reduce_kernel; em_small_kernel and stats_reduce_kernel when
+ * K <= 64).  Honours GMMXX_B200_KERNEL.  A device that cannot
  * co-schedule the kernel's thread-block cluster falls back to the CUDA-core
  * kernels at launch time, which this query does not predict.  No counterpart
  * in the reference (its dispatch is the Python table in _runtime.py:31-216). */
