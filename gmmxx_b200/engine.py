@@ -9,9 +9,11 @@ One soft-EM iteration is three C ABI calls on the current CUDA stream:
                          only when the rows are sharded over several ranks
     gmmxx_em_finalize    M-step finalize, identical on every rank
 
-so parameters stay bit-identical across ranks without a broadcast.  The loop
-never synchronises the host unless ``tol > 0`` or ``verbose`` (as in the
-reference, gmmxx/torch_fallback.py:2060-2330).
+so parameters stay bit-identical across ranks without a broadcast.  With
+``approx_top_k`` the statistics call is ``gmmxx_em_accumulate_topk`` (each
+row's responsibilities over its top_k components).  The loop never
+synchronises the host unless ``tol > 0`` or ``verbose`` (as in the reference,
+gmmxx/torch_fallback.py:2060-2330).
 
 Semantics follow the reference's torch loops; see ``batch_gmm_*`` in
 ``gmmxx_b200.api`` for the public signatures.
