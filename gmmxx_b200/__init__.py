@@ -105,4 +105,30 @@ __all__ = [
     "cuda_ops",
 ]
 
+# The reference exports its Triton kernels under these names and sets each to
+# None when Triton is unavailable (gmmxx/__init__.py:35-101).  This engine has
+# no Triton kernels, so they are None here too: code that imports them, or
+# tests them against None before use, runs unchanged.
+approx_topk_update_spherical_config = None
+triton_approx_topk_update_spherical = None
+spherical_assign_triton = None
+spherical_logsumexp_triton = None
+spherical_resp_triton = None
+diag_assign_triton = None
+diag_logsumexp_triton = None
+diag_resp_triton = None
+full_assign_triton = None
+full_logsumexp_triton = None
+full_resp_triton = None
+triton_blocked_update_diag = None
+triton_blocked_update_full = None
+triton_blocked_update_spherical = None
+triton_blocked_update_tied_projected = None
+triton_streaming_update_spherical = None
+triton_weighted_update_spherical = None
+fused_single_tile_update_config = None
+triton_fused_single_tile_update_diag = None
+triton_fused_single_tile_update_spherical = None
+triton_fused_single_tile_update_tied_native = None
+
 __version__ = "0.1.0"

@@ -60,3 +60,32 @@ def test_lowercase_aliases():
 def test_argument_checks(call, exc):
     with pytest.raises(exc):
         call(torch.zeros(1, 8, 2))
+
+
+REFERENCE_EXPORTS = [
+    "batch_gmm_Spherical", "batch_gmm_Spherical_torch_native", "batch_gmm_Diagonal",
+    "batch_gmm_Diagonal_torch_native", "batch_gmm_Full", "batch_gmm_Full_torch_native", "batch_gmm_Tied",
+    "batch_gmm_Tied_torch_native", "batch_gmm_spherical", "batch_gmm_diagonal", "batch_gmm_diag", "batch_gmm_full",
+    "batch_gmm_tied", "diagonal_assign_torch_native_chunked", "diagonal_predict_proba_torch_native_chunked",
+    "diagonal_score_samples_torch_native_chunked", "full_assign_torch_native_chunked",
+    "full_predict_proba_torch_native_chunked", "full_score_samples_torch_native_chunked",
+    "tied_assign_torch_native_chunked", "tied_predict_proba_torch_native_chunked",
+    "tied_score_samples_torch_native_chunked", "GMMXX", "batch_gmm_largeN_cpu", "large_n_predict_cpu",
+    "large_n_predict_proba_cpu", "large_n_score_samples_cpu", "spherical_assign_triton", "spherical_logsumexp_triton",
+    "spherical_resp_triton", "diag_assign_triton", "diag_logsumexp_triton", "diag_resp_triton", "full_assign_triton",
+    "full_logsumexp_triton", "full_resp_triton", "triton_blocked_update_diag", "triton_blocked_update_full",
+    "triton_blocked_update_spherical", "triton_blocked_update_tied_projected", "triton_streaming_update_spherical",
+    "triton_weighted_update_spherical", "fused_single_tile_update_config", "triton_fused_single_tile_update_diag",
+    "triton_fused_single_tile_update_spherical", "triton_fused_single_tile_update_tied_native",
+    "approx_topk_update_spherical_config", "triton_approx_topk_update_spherical", "cuda_ops",
+]
+
+
+def test_every_reference_export_is_importable():
+    """Every name the reference package exports (gmmxx/__init__.py:104-154)
+    imports from gmmxx_b200; the Triton kernels are None, as they are in the
+    reference when Triton is unavailable."""
+    for name in REFERENCE_EXPORTS:
+        assert hasattr(G, name), name
+        if "triton" in name or name.endswith("_config"):
+            assert getattr(G, name) is None, name
