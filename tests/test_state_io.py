@@ -106,3 +106,16 @@ def test_loaded_nonfinite_bound_survives(tmp_path):
     state["fit_info"]["lower_bound"] = float("-inf")
     GMMXX(k=1, device="cpu").load_state_dict(state).save(tmp_path / "m.pt")
     assert math.isinf(GMMXX.load(tmp_path / "m.pt", device="cpu").lower_bound_)
+
+
+@pytest.mark.parametrize("cov_type,per_component", [("spherical", 1), ("diag", 3), ("full", 6)])
+def test_parameter_count_for_bic_and_aic(cov_type, per_component):
+    """The free-parameter count of the reference's bic / aic
+    (interface.py:2537-2547): means K D + covariances + K - 1 weights, per
+    problem; tied shares one D(D+1)/2 block."""
+    r = GMMXX(k=1, device="cpu").load_state_dict(_state(cov_type, 3))
+    k, d = 4, 3
+    assert r._n_parameters(1) == k * d + k * per_component + k - 1
+    assert r._n_parameters(3) == 3 * (k * d + k * per_component + k - 1)
+    t = GMMXX(k=1, device="cpu").load_state_dict(_state("tied", None))
+    assert t._n_parameters(1) == k * d + d * (d + 1) // 2 + k - 1
