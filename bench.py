@@ -2,26 +2,31 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
-A step is one full soft-EM iteration (prepare, fused E+M statistics,
+A step is one full soft-EM iteration (prepare, fused E+M statistics, one
 allreduce when N > 1, finalize) over the configuration's whole synthetic
 dataset, which is resident in HBM and sharded by rows across the ranks
 (strong scaling: the total N is the configuration's N at every GPU count).
-Default workload: configs[1] of BASELINE.json -- diagonal GMM, bf16 X with fp32
-accumulation, N = 50,000,000, D = 64, K = 512.
+Default workload: configs[1] of BASELINE.json -- diagonal GMM, bf16 X with
+fp32 accumulation, N = 50,000,000, D = 64, K = 512.
 
 ``value``  samples/s per EM iteration, device-timed (CUDA events on the compute
            stream, barrier + synchronize on both sides, max over ranks).
-``e2e``    the same metric through the public streamed API: X in pinned host
-           memory, every step copies its rows host->device (double-buffered
-           copy stream overlapping the kernels) and reads the fitted
-           parameters and lower bound back to the host.
+``e2e``    the same metric through the public streamed API
+           (``large_n.em_fit_streamed``, one call of K iterations): X in
+           pinned host memory, every iteration copies its rows host->device
+           (double-buffered copy stream overlapping the kernels) and reads the
+           iteration's lower bound back to the host.
 ``roofline`` the dominant kernel launch (gmmxx_em_accumulate) against the
-           measured bf16 tensor peak, algorithmic FLOPs only.
-``cpu_baseline`` the numpy oracle port of the reference's torch path on the
-           host cores, on a bounded row sample, rank 0 at N = 1.
+           measured bf16 tensor peak, algorithmic FLOPs only; ``kernel`` names
+           the statistics kernels the library reports it launched.
+``cpu_baseline`` the reference's own torch CPU implementation
+           (``gmmxx.torch_fallback.batch_gmm_*_torch_native``, the unmodified
+           package installed under baseline/_ref) on the host cores, on a
+           bounded row sample, rank 0 at N = 1.
 
-``--impl reference`` times that CPU port alone (the reference's own
-implementation is PyTorch code that cannot travel to the GPU host).
+``--impl reference`` times that reference CPU path alone, per step on a
+bounded row sample.  Only when baseline/_ref cannot be imported does either
+leg fall back to the numpy restatement under oracle/ (``kind: "port"``).
 """
 
 from __future__ import annotations
@@ -62,7 +67,7 @@ def launches_per_iteration(cfg, tc_path: bool, approx: bool = False) -> int:
     prep = 2 + (2 if cfg.cov_type in ("tied", "full") else 0)
     stats = 2 if (not tc_path and not approx and cfg.K <= 64) else 3  # K <= 64: one-pass kernel + reduce
     if tc_path and cfg.cov_type == "spherical" and cfg.K > 1024:
-        groups = (((cfg.K + 127) // 128) + 7) // 8
+        groups = (((cfg.K + 127) // 128) + 3) // 4  # groups of 4 chunks (512 components)
         stats = 3 + 3 * groups
     return prep + stats + 2
 
@@ -126,26 +131,71 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_baseline(cfg, mix, init, rows: int, iters: int = 1, approx_top_k=None):
-    """The oracle (numpy port of the reference torch path) on a bounded sample
-    (approximate top-k EM when ``approx_top_k`` is given)."""
+REF_PATH = os.path.join(ROOT, "baseline", "_ref")
+# rows per problem of one timed reference sample (about 1-3 s of host work on 16 threads)
+REF_ROWS = {0: 100_000, 1: 200_000, 2: 500_000, 3: 16_384, 4: 20_000}
+# rows per problem of the cpu_baseline leg (about 10-30 s)
+CPU_ROWS = {0: 100_000, 1: 1_000_000, 2: 2_000_000, 3: 65_536, 4: 100_000}
+
+
+def reference_module():
+    """The reference's own torch implementation (gmmxx.torch_fallback of the
+    unmodified package installed under baseline/_ref), or (None, reason)."""
+    if not os.path.isdir(os.path.join(REF_PATH, "gmmxx")):
+        return None, "baseline/_ref not installed"
+    if REF_PATH not in sys.path:
+        sys.path.insert(0, REF_PATH)
+    try:
+        from gmmxx import torch_fallback
+    except Exception as exc:  # report, never fake
+        return None, repr(exc)
+    return torch_fallback, None
+
+
+def cpu_sample(cfg, mix, init, rows: int, iters: int = 1, approx_top_k=None):
+    """One timed fit of ``iters`` EM iterations on ``rows`` rows per problem,
+    on the host cores, by the reference's own torch CPU path
+    (batch_gmm_*_torch_native from baseline/_ref, tol=0, no Triton, same
+    initial parameters as the GPU arm, labels off); the numpy port of it under
+    oracle/ only when the reference cannot be imported."""
     import torch
 
-    import oracle
     from gmmxx_b200 import synthetic
 
-    x = synthetic.sample_rows(cfg, mix, rows, torch.device("cpu"), seed=12345).float().numpy()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x = synthetic.sample_rows(cfg, mix, rows, torch.device("cpu"), seed=12345).float()
     means, cov, w = init
+    tf, why = reference_module()
+    sample = f"{cfg.B}x{rows} rows of config {cfg.index}, {iters} EM iteration(s), float32"
+    if tf is not None:
+        fn = {"spherical": tf.batch_gmm_Spherical_torch_native, "diag": tf.batch_gmm_Diagonal_torch_native,
+              "tied": tf.batch_gmm_Tied_torch_native, "full": tf.batch_gmm_Full_torch_native}[cfg.cov_type]
+        kw = dict(max_iters=iters, tol=0.0, init_means=torch.from_numpy(means), init_variances=torch.from_numpy(cov),
+                  init_weights=torch.from_numpy(w), reg_covar=1e-6, compute_labels=False, approx_top_k=approx_top_k)
+        if cfg.cov_type == "spherical":
+            kw.update(gmm_use_triton_estep=False, gmm_use_triton_streaming_update=False)
+        else:
+            kw.update(gmm_use_triton=False)
+        t0 = time.perf_counter()
+        fn(x, cfg.K, **kw)
+        dt = time.perf_counter() - t0
+        return {"value": rows * cfg.B * iters / dt, "unit": "samples/s", "cores": threads, "kind": "reference",
+                "sample": f"{sample}, the reference's {fn.__name__} (torch {torch.__version__} CPU, "
+                          f"{threads} threads), {dt:.2f} s"}
+    import oracle
+
     t0 = time.perf_counter()
-    oracle.fit(cfg.cov_type, x, cfg.K, iters, 0.0, means, cov, w, compute_labels=False, approx_top_k=approx_top_k)
+    oracle.fit(cfg.cov_type, x.numpy(), cfg.K, iters, 0.0, means, cov, w, compute_labels=False,
+               approx_top_k=approx_top_k)
     dt = time.perf_counter() - t0
-    return {"value": rows * cfg.B * iters / dt, "unit": "samples/s", "cores": os.cpu_count(),
-            "kind": "port", "sample": f"{cfg.B}x{rows} rows of config {cfg.index}, {iters} EM iteration(s), "
-                                      f"numpy float32 on {os.cpu_count()} host threads, {dt:.2f} s"}
+    return {"value": rows * cfg.B * iters / dt, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{sample}, numpy port under oracle/ ({dt:.2f} s); reference not importable: {why}"}
 
 
 def run_reference(args, cfg):
-    """--impl reference: the CPU port timed per step on bounded samples."""
+    """--impl reference: the reference's torch CPU path timed per step on a
+    bounded row sample (rank 0 only; other ranks exit without work)."""
     from gmmxx_b200 import synthetic
 
     rank = int(os.environ.get("RANK", "0"))
@@ -153,20 +203,18 @@ def run_reference(args, cfg):
         return
     mix = synthetic.mixture_params(cfg)
     init = synthetic.initial_params(cfg, mix)
-    rows = args.ref_rows
-    vals = []
+    rows = args.ref_rows or REF_ROWS[cfg.index]
     for _ in range(args.warmup):
-        cpu_baseline(cfg, mix, init, rows, approx_top_k=args.approx_top_k)
-    for _ in range(args.steps):
-        vals.append(cpu_baseline(cfg, mix, init, rows, approx_top_k=args.approx_top_k)["value"])
-    v = statistics.median(vals)
+        cpu_sample(cfg, mix, init, rows, approx_top_k=args.approx_top_k)
+    runs = [cpu_sample(cfg, mix, init, rows, approx_top_k=args.approx_top_k) for _ in range(args.steps)]
+    v = statistics.median(r["value"] for r in runs)
     line = {
         "impl": "reference", "metric": "EM samples/s per iteration", "value": v, "unit": "samples/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * rows * cfg.B / v,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": workload_config(cfg, args),
-        "cpu_baseline": {"value": v, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{cfg.B}x{rows} rows per step, 1 EM iteration, numpy float32"},
+        "cpu_baseline": {"value": v, "unit": "samples/s", "cores": runs[0]["cores"], "kind": runs[0]["kind"],
+                         "sample": f"per step: {runs[0]['sample']}"},
         "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -251,10 +299,12 @@ def main():
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=0, help="override total N (smaller runs)")
-    ap.add_argument("--ref-rows", type=int, default=200_000, help="rows per step of --impl reference")
-    ap.add_argument("--cpu-rows", type=int, default=1_000_000,
-                    help="rows of the cpu_baseline sample (about 10 s of host work for config 1)")
+    ap.add_argument("--ref-rows", type=int, default=0,
+                    help="rows per problem of each --impl reference step (default: per configuration)")
+    ap.add_argument("--cpu-rows", type=int, default=0,
+                    help="rows per problem of the cpu_baseline sample (default: per configuration, 10-30 s)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--chunk-rows", type=int, default=1 << 22, help="rows per host->device chunk of the e2e leg")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--infer", choices=["predict", "score", "proba"], default=None,
                     help="time an inference call (labels / score_samples / predict_proba) instead of EM")
@@ -310,7 +360,10 @@ def main():
     top_k = engine.resolve_approx_top_k(args.approx_top_k, cfg.K)
     ops = engine.CudaOps(cfg.cov_type, x, cfg.K, top_k)
     B, D, K = cfg.B, cfg.D, cfg.K
-    stats = torch.zeros((B, K, ops.stat_width), dtype=torch.float32, device=dev)
+    nstat = B * K * ops.stat_width
+    # the statistics and (last slot, multi-rank only) the log-likelihood: one collective per step
+    pack = torch.zeros((nstat + (1 if comm else 0),), dtype=torch.float32, device=dev)
+    stats = pack[:nstat].view(B, K, ops.stat_width)
     ll = torch.zeros((1,), dtype=torch.float64, device=dev)
     lb = torch.zeros((1,), dtype=torch.float32, device=dev)
     xx = None
@@ -333,8 +386,9 @@ def main():
         if i is not None:
             ev_acc[i][1].record(stream)
         if comm:
-            comm.allreduce_(stats)
-            comm.allreduce_(ll)
+            pack[nstat:].copy_(ll)
+            comm.allreduce_(pack)
+            ll.copy_(pack[nstat:])
         ops.finalize(cfg.N, stats, ll, xx, 1e-6, 1e-8, means, cov, weights, lb)
 
     for _ in range(args.warmup):
@@ -361,63 +415,54 @@ def main():
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms, acc_ms = float(ms_t[0]), float(ms_t[1])
     ops.check_status()
+    kernel_path = ops.kernel_path()
+    tc_path = top_k is None and ops.paths == {1}
     value = cfg.N * cfg.B / (ms / 1e3)
 
-    # --- end to end through the streamed public API (host-resident X) -------
+    # --- end to end through the public streamed API (host-resident X) -------
     e2e = None
     if not args.no_e2e and cfg.B == 1:
         x_host = torch.empty((1, n_local, D), dtype=cfg.dtype, pin_memory=True)
         x_host.copy_(x)
         del x, ops
         torch.cuda.empty_cache()
-        chunk = 1 << 22
-        streamer = large_n.ChunkStreamer(x_host, chunk, dev)
-        m2, c2, w2, _ = engine.initial_parameters(cfg.cov_type, streamer.bufs[0][:, :1], cfg.K,
-                                                  torch.from_numpy(init_means), torch.from_numpy(init_cov),
-                                                  torch.from_numpy(init_w), 1e-6)
-        ops2 = engine.CudaOps(cfg.cov_type, streamer.bufs[0], cfg.K)
-        host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (m2, c2, w2, lb)]
+        streamer = large_n.ChunkStreamer(x_host, args.chunk_rows, dev)
+        init_t = [torch.from_numpy(a) for a in (init_means, init_cov, init_w)]
 
-        def e2e_step():
-            ops2.prepare(m2, c2, w2, 1e-6, 1e-8)
-            stats.zero_()
-            ll.zero_()
-            for xc, _ in streamer.chunks():
-                nat.call("gmmxx_em_accumulate", ops2.covc, ops2.xdt, xc.data_ptr(), 1, xc.shape[1], D, K,
-                         ops2.ws.data_ptr(), ops2.ws.numel(), stats.data_ptr(), ll.data_ptr(), ops2.stream)
-            if comm:
-                comm.allreduce_(stats)
-                comm.allreduce_(ll)
-            ops2.finalize(cfg.N, stats, ll, xx, 1e-6, 1e-8, m2, c2, w2, lb)
-            for h, t in zip(host_out, (m2, c2, w2, lb)):
-                h.copy_(t, non_blocking=True)
+        def e2e_fit(iters):
+            # tol > 0 makes the loop read each iteration's lower bound back to the
+            # host (the step's result); 1e-30 never stops these fits early
+            return large_n.em_fit_streamed(cfg.cov_type, x_host, K, device=dev, chunk_rows=args.chunk_rows,
+                                           max_iters=iters, tol=1e-30, init_means=init_t[0],
+                                           init_variances=init_t[1], init_weights=init_t[2], reg_covar=1e-6,
+                                           compute_labels=False, streamer=streamer, comm=comm)
 
-        for _ in range(args.warmup):
-            e2e_step()
+        e2e_fit(args.warmup)
         if comm:
             dist.barrier()
         torch.cuda.synchronize()
         streamer.h2d_bytes = 0
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
+        _, m2, c2, w2, info2 = e2e_fit(args.steps)
+        host_out = [t.cpu() for t in (m2, c2, w2)]
         e1.record(stream)
         torch.cuda.synchronize()
         if comm:
             dist.barrier()
-        ems = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+        it2 = info2["n_iter"]
+        ems = torch.tensor([e0.elapsed_time(e1) / it2], dtype=torch.float64, device=dev)
         if comm:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
         e2e = {"value": cfg.N * cfg.B / (float(ems[0]) / 1e3), "unit": "samples/s",
-               "h2d_bytes_per_step": streamer.h2d_bytes // args.steps,
-               "d2h_bytes_per_step": sum(h.numel() * h.element_size() for h in host_out),
-               "path": "gmmxx_b200.large_n streamed host-resident X (pinned, 4M-row double buffer)"}
+               "h2d_bytes_per_step": streamer.h2d_bytes // it2,
+               "d2h_bytes_per_step": 4 + sum(h.numel() * h.element_size() for h in host_out) // it2,
+               "iterations": it2, "kernel_path": info2["kernel_path"],
+               "path": f"gmmxx_b200.large_n.em_fit_streamed, one call of {it2} iterations over pinned host X "
+                       f"({args.chunk_rows}-row double-buffered chunks), lower bound read back every iteration"}
 
     if rank == 0:
         peaks = load_peaks()
-        tc_path = top_k is None and nat.accumulate_path(engine.cov_code(cfg.cov_type), engine._X_DTYPES[cfg.dtype],
-                                                        cfg.B, n_local, D, K) == 1
         flops = algorithmic_flops(cfg.cov_type, n_local * cfg.B, D, K)
         achieved = flops / (acc_ms / 1e3) / 1e12
         long_run = ms * args.steps > 1000.0
@@ -427,8 +472,9 @@ def main():
         if os.path.exists(tpath) and top_k is None:  # the captured traffic is the exact-EM kernel's
             with open(tpath) as f:
                 tr = json.load(f).get(f"config{cfg.index}")
-            if tr:
+            if tr and tr.get("path", "tensor-core") == kernel_path:
                 traffic = tr["read_bytes_per_row"] * n_local * cfg.B + tr["write_bytes_per_launch"]
+        kernel_names = {"diag": "em_tc_diag_kernel", "spherical": "em_tc_kernel", "tied": "em_tc_diag_kernel<tied>"}
         line = {
             "metric": "EM samples/s per iteration", "value": value, "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -436,8 +482,9 @@ def main():
             "config": workload_config(cfg, args),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": ((("em_tc_diag_kernel" if cfg.cov_type == "diag" else "em_tc_kernel")
-                                     + " (+ tc_pack_kernel, tc_reduce_kernel)") if tc_path
+                         "kernel_path": kernel_path,
+                         "kernel": ((kernel_names.get(cfg.cov_type, "?") + " (+ tc_pack_kernel, tc_reduce_kernel)")
+                                    if tc_path
                                     else "topk_rows_kernel + topk_mstep_kernel + stats_reduce_kernel" if top_k
                                     else ("em_small_kernel + stats_reduce_kernel" if cfg.K <= 64
                                           else "rows_kernel + mstep_kernel + stats_reduce_kernel")),
@@ -451,8 +498,8 @@ def main():
         }
         if world == 1 and not args.no_cpu:
             try:
-                line["cpu_baseline"] = cpu_baseline(cfg, mix, (init_means, init_cov, init_w), args.cpu_rows,
-                                                    approx_top_k=args.approx_top_k)
+                line["cpu_baseline"] = cpu_sample(cfg, mix, (init_means, init_cov, init_w),
+                                                  args.cpu_rows or CPU_ROWS[cfg.index], approx_top_k=args.approx_top_k)
             except Exception as exc:  # report, never fake
                 line["cpu_baseline"] = {"error": repr(exc)}
         print(json.dumps(line), flush=True)

@@ -71,6 +71,7 @@ _SIGNATURES = {
     "gmmxx_workspace_bytes": (_SZ, [_I32, _I64, _I64, _I64, _I64]),
     "gmmxx_workspace_status": (_I32, [_P, _P, _P]),
     "gmmxx_accumulate_path": (_I32, [_I32, _I32, _I64, _I64, _I64, _I64, _P]),
+    "gmmxx_last_accumulate_path": (_I32, []),
     "gmmxx_em_prepare": (_I32, [_I32, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _SZ, _P]),
     "gmmxx_em_accumulate": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P, _P, _P]),
     "gmmxx_topk_scratch_bytes": (_SZ, [_I64, _I64, _I64]),
@@ -145,6 +146,17 @@ def accumulate_path(cov: int, xdt: int, b: int, n: int, d: int, k: int) -> int:
     out = ctypes.c_int(0)
     call("gmmxx_accumulate_path", cov, xdt, b, n, d, k, ctypes.addressof(out))
     return out.value
+
+
+# gmmxx_last_accumulate_path values
+PATH_NAMES = {-1: None, 0: "cuda-core", 1: "tensor-core", 2: "cuda-core (tensor-core launch had no co-resident cluster)"}
+
+
+def last_accumulate_path() -> int:
+    """Statistics path of the last successful gmmxx_em_accumulate on this host
+    thread: 1 tensor cores, 0 CUDA cores, 2 CUDA cores after the tensor-core
+    launch found no co-resident cluster, -1 none yet."""
+    return int(load().gmmxx_last_accumulate_path())
 
 
 def workspace_bytes(cov: int, b: int, n: int, d: int, k: int) -> int:

@@ -13,6 +13,10 @@
 namespace gmmxx {
 
 static thread_local char g_err[1024] = {0};
+// statistics path of the last successful gmmxx_em_accumulate on this thread
+// (gmmxx_last_accumulate_path): -1 none, 0 CUDA cores, 1 tensor cores,
+// 2 CUDA cores after the tensor-core launch found no co-resident cluster
+static thread_local int g_last_path = -1;
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -165,6 +169,29 @@ int infer_common(int cov, const void* x, int64_t B, int64_t N, int64_t D, int64_
                         const_cast<float*>(weights), 0.f, 0.f, 0, *L, static_cast<char*>(ws), st);
 }
 
+// the CUDA-core statistics kernels of gmmxx_em_accumulate
+int accumulate_simt(int cov_type, int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,
+                    const Layout& L, char* ws, float* stats, double* log_likelihood, cudaStream_t st) {
+  RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
+  a.ll_part = reinterpret_cast<double*>(ws + L.llpart);
+  a.ll = log_likelihood;
+  if (L.Kp == kBK) {  // one component tile: logsumexp and statistics in one pass
+    a.stats = stats;
+    a.part = reinterpret_cast<float*>(ws + L.mpart);
+    return launch_em_small(cov_type, a, (int)B, st);
+  }
+  a.lse_out = reinterpret_cast<float*>(ws + L.lse);
+  if (cov_type == GMMXX_TIED) a.q_out = reinterpret_cast<float*>(ws + L.qrow);
+  if (int rc = launch_rows(cov_type, MODE_LSE, a, (int)B, st)) return rc;
+  a.lse_in = a.lse_out;
+  a.q_in = a.q_out;  // the M-step reads x^T P x instead of recomputing it per component tile
+  a.q_out = nullptr;
+  a.stats = stats;
+  a.part = reinterpret_cast<float*>(ws + L.mpart);
+  if (int rc = launch_mstep(cov_type, a, (int)B, st)) return rc;
+  return launch_stats_reduce(a, (int)B, st);
+}
+
 }  // namespace
 
 extern "C" {
@@ -244,6 +271,7 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int mode = kernel_mode();
   const bool tc_ok = L.tc_cluster > 0 && x_dtype == GMMXX_BFLOAT16;
+  bool fallback = false;
   if (mode == 2 && !tc_ok)
     return set_error(GMMXX_ERR_UNSUPPORTED, "tensor-core kernel required but the shape / dtype is outside its window");
   if (tc_ok && mode != 1) {
@@ -256,27 +284,18 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
       t.wait_ns = t.test_stall ? 100000000ull : 2000000000ull;
     }
     const int rc = tc::launch_em_tc(cov_type, t, st);
-    if (rc != GMMXX_ERR_UNSUPPORTED || mode == 2) return rc;  // else: no co-resident cluster -> CUDA-core kernels
+    if (rc != GMMXX_ERR_UNSUPPORTED || mode == 2) {
+      if (rc == GMMXX_OK) g_last_path = 1;
+      return rc;
+    }
+    fallback = true;  // no co-resident cluster: the CUDA-core kernels below
   }
-  RowArgs a = make_rows(cov_type, x_dtype, x, B, N, D, K, L, ws);
-  a.ll_part = reinterpret_cast<double*>(ws + L.llpart);
-  a.ll = log_likelihood;
-  if (L.Kp == kBK) {  // one component tile: logsumexp and statistics in one pass
-    a.stats = stats;
-    a.part = reinterpret_cast<float*>(ws + L.mpart);
-    return launch_em_small(cov_type, a, (int)B, st);
-  }
-  a.lse_out = reinterpret_cast<float*>(ws + L.lse);
-  if (cov_type == GMMXX_TIED) a.q_out = reinterpret_cast<float*>(ws + L.qrow);
-  if (int rc = launch_rows(cov_type, MODE_LSE, a, (int)B, st)) return rc;
-  a.lse_in = a.lse_out;
-  a.q_in = a.q_out;  // the M-step reads x^T P x instead of recomputing it per component tile
-  a.q_out = nullptr;
-  a.stats = stats;
-  a.part = reinterpret_cast<float*>(ws + L.mpart);
-  if (int rc = launch_mstep(cov_type, a, (int)B, st)) return rc;
-  return launch_stats_reduce(a, (int)B, st);
+  const int rc = accumulate_simt(cov_type, x_dtype, x, B, N, D, K, L, ws, stats, log_likelihood, st);
+  if (rc == GMMXX_OK) g_last_path = fallback ? 2 : 0;
+  return rc;
 }
+
+int gmmxx_last_accumulate_path(void) { return g_last_path; }
 
 size_t gmmxx_topk_scratch_bytes(int64_t B, int64_t N, int64_t top_k) {
   if (B <= 0 || N < 0 || top_k <= 0) return 0;

@@ -35,6 +35,8 @@
 #include "tc_api.cuh"
 
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 #include <type_traits>
@@ -770,6 +772,11 @@ int launch_tc_reduce(const TcLaunch& L, int ncl, cudaStream_t st) {
 
 int clustered_launch(const void* kern, int threads, int smem, const TcLaunch& L, int* ncl_out) {
   const int nclus = L.cluster_size;
+  {  // test hook: GMMXX_B200_TEST_NO_CLUSTER=1 answers as a device with no co-resident cluster would
+    const char* e = getenv("GMMXX_B200_TEST_NO_CLUSTER");
+    if (e != nullptr && strcmp(e, "1") == 0)
+      return set_error(GMMXX_ERR_UNSUPPORTED, "no co-resident cluster of %d CTAs (GMMXX_B200_TEST_NO_CLUSTER)", nclus);
+  }
   if (smem > 232448) return set_error(GMMXX_ERR_UNSUPPORTED, "tensor-core kernel shared memory over budget");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "tensor-core kernel attributes: %s", cudaGetErrorString(e));

@@ -18,6 +18,8 @@
 #include "gmm_common.cuh"
 #include "rows_api.cuh"
 
+#include <cuda.h>
+
 #include <mutex>
 
 namespace gmmxx {
@@ -33,25 +35,66 @@ static __device__ __align__(256) char g_static_scratch[kStaticScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
-char* g_scratch_ptr[kMaxDevices] = {nullptr};
+struct ScratchEntry {
+  char* ptr;
+  unsigned long long ctx_id;  // the context the address belongs to (0: not known)
+};
+ScratchEntry g_scratch[kMaxDevices] = {};
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the current context, or 0 when the driver cannot say.  A
+// device's primary context that was torn down and created again (for
+// instance after cudaDeviceReset) gets a new id, and with it the array a new
+// address.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 // Device address of the scratch array on the current device.  The symbol's
 // name in host code is only a host-side handle, so the address is looked up
-// once per device (with that device current) and cached.
+// with the device current and cached per device together with the id of the
+// context it was found in; a call in another context (the device was reset)
+// looks it up again.  While no context id can be had the address is looked
+// up on every call.
 int scratch_address(char** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return set_error(GMMXX_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
+  ScratchEntry& ent = g_scratch[dev];
+  if (ent.ptr == nullptr || ctx == 0 || ent.ctx_id != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess || p == nullptr)
       return set_error(GMMXX_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
-    g_scratch_ptr[dev] = static_cast<char*>(p);
+    ent.ptr = static_cast<char*>(p);
+    // the lookup made the device's primary context current if none was
+    ent.ctx_id = current_context_id();
   }
-  *out = g_scratch_ptr[dev];
+  *out = ent.ptr;
   return GMMXX_OK;
 }
 

@@ -135,9 +135,12 @@ def spherical_resp(x, means, var, log_w, log_norm, out: Optional[torch.Tensor] =
 def _spherical_stats(x, means, var, log_w, top_k: Optional[int] = None):
     """(n_k, sum r x, sum r |x|^2, sum of the rows' log-sum-exp) for the
     parameters as given: the engine's per-iteration prologue runs on copies
-    with a variance floor of 1e-30 (the reference's clamp in
-    approx_topk_update_spherical, _cuda.py:829) and a negligible weight floor,
-    and the weights it renormalises are corrected for in the log-likelihood."""
+    with a negligible weight floor (the weights it renormalises are corrected
+    for in the log-likelihood).  The variances are floored at 1e-30 only for
+    approximate top-k EM (the reference's clamp in
+    approx_topk_update_spherical, _cuda.py:829-830); the exact operators take
+    log(var) unclamped as the reference's do (_cuda.py:581), apart from a
+    floor at 0 for negative variances."""
     b, n, d = x.shape
     k = means.shape[1]
     ops = engine.CudaOps("spherical", x, k, top_k)
@@ -145,7 +148,7 @@ def _spherical_stats(x, means, var, log_w, top_k: Optional[int] = None):
     v = var.clone()
     w = _weights(log_w).clone()
     with torch.cuda.device(x.device):
-        ops.prepare(m, v, w, 1e-30, 1e-30)
+        ops.prepare(m, v, w, 1e-30 if top_k is not None else 0.0, 1e-30)
         stats = torch.zeros((b, k, ops.stat_width), dtype=torch.float32, device=x.device)
         ll = torch.zeros((1,), dtype=torch.float64, device=x.device)
         ops.accumulate(stats, ll)

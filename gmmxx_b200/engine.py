@@ -5,8 +5,9 @@ One soft-EM iteration is three C ABI calls on the current CUDA stream:
 
     gmmxx_em_prepare     prologue (clamp / renormalise) + component table
     gmmxx_em_accumulate  fused E-step + M-step statistics over the local rows
-    [allreduce]          stats (B, K, F) fp32 and the log-likelihood (fp64),
-                         only when the rows are sharded over several ranks
+    [allreduce]          one collective of stats (B, K, F) and the
+                         log-likelihood packed into one fp32 buffer, only
+                         when the rows are sharded over several ranks
     gmmxx_em_finalize    M-step finalize, identical on every rank
 
 so parameters stay bit-identical across ranks without a broadcast.  With
@@ -213,6 +214,19 @@ class Comm:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group)
         return t
 
+    def broadcast_(self, t: torch.Tensor, src: int = 0) -> torch.Tensor:
+        """Rank ``src``'s tensor on every rank (``src`` is a rank of the group)."""
+        self.dist.broadcast(t, src=self.dist.get_global_rank(self.group, src) if self.group is not None else src,
+                            group=self.group)
+        return t
+
+
+def kernel_path_name(paths) -> str:
+    """The statistics kernels a fit ran, from the gmmxx_last_accumulate_path
+    values its accumulate calls reported (several when chunks differed)."""
+    names = [nat.PATH_NAMES.get(p) for p in sorted(paths) if nat.PATH_NAMES.get(p)]
+    return " + ".join(names) if names else "none"
+
 
 class CudaOps:
     """The four per-iteration kernels of one fit, bound to one device buffer
@@ -231,6 +245,7 @@ class CudaOps:
         self.ws = _WS.get(x.device, nat.workspace_bytes(self.covc, self.b, self.n, self.d, k))
         # approximate top-k EM: the per-row lists between its two passes
         self.top_k = top_k
+        self.paths = set()  # gmmxx_last_accumulate_path after each exact-EM accumulate call
         self.scratch = None
         if top_k is not None:
             self.scratch = torch.empty(nat.topk_scratch_bytes(self.b, self.n, top_k), dtype=torch.uint8,
@@ -253,6 +268,13 @@ class CudaOps:
             return
         nat.call("gmmxx_em_accumulate", self.covc, self.xdt, self.x.data_ptr(), self.b, self.n, self.d, self.k,
                  self.ws.data_ptr(), self.ws.numel(), stats.data_ptr(), ll.data_ptr(), self.stream)
+        self.paths.add(nat.last_accumulate_path())
+
+    def kernel_path(self) -> str:
+        """Which statistics kernels this fit launched (fit_info's kernel_path)."""
+        if self.top_k is not None:
+            return "cuda-core (approximate top-k)"
+        return kernel_path_name(self.paths)
 
     def finalize(self, n_total, stats, ll, xx, reg_covar, min_weight, means, cov, weights, lb_slot) -> None:
         nat.call("gmmxx_em_finalize", self.covc, self.b, self.d, self.k, n_total, stats.data_ptr(), ll.data_ptr(),
@@ -280,7 +302,11 @@ def em_loop(ops, cov_type, means, cov, weights, *, n_total, max_iters, tol, reg_
     dev = means.device
     b, k = weights.shape
     d = means.shape[2]
-    stats = torch.zeros((b, k, ops.stat_width), dtype=torch.float32, device=dev)
+    nstat = b * k * ops.stat_width
+    # one buffer for the collective: the statistics and, in its last slot, the
+    # log-likelihood (fp32 there; per-rank sums are exact to ~1e-7 relative)
+    pack = torch.zeros((nstat + (1 if comm is not None else 0),), dtype=torch.float32, device=dev)
+    stats = pack[:nstat].view(b, k, ops.stat_width)
     ll = torch.zeros((1,), dtype=torch.float64, device=dev)
     lb_hist = torch.zeros((max_iters,), dtype=torch.float32, device=dev)
     xx = None
@@ -297,9 +323,10 @@ def em_loop(ops, cov_type, means, cov, weights, *, n_total, max_iters, tol, reg_
         stats.zero_()
         ll.zero_()
         ops.accumulate(stats, ll)
-        if comm is not None:
-            comm.allreduce_(stats)
-            comm.allreduce_(ll)
+        if comm is not None:  # the iteration's one collective
+            pack[nstat:].copy_(ll)
+            comm.allreduce_(pack)
+            ll.copy_(pack[nstat:])
         if verbose:
             prev_means, prev_cov = means.clone(), cov.clone()
         ops.finalize(n_total, stats, ll, xx, reg_covar, min_weight, means, cov, weights, lb_hist[it:])
@@ -409,7 +436,7 @@ def em_fit(
         labels = assign(cov_type, x, means, cov, weights) if compute_labels else None
     info = fit_info(n_iter, hist, source, elapsed, gpus=1 if comm is None else comm.world_size,
                     approximate_em_enabled=top_k is not None, approx_top_k=top_k,
-                    cuda_approx_topk_enabled=top_k is not None)
+                    cuda_approx_topk_enabled=top_k is not None, kernel_path=ops.kernel_path())
     return labels, means, cov, weights, info
 
 

@@ -277,6 +277,9 @@ class GMMXX:
         optional extras over the reference estimator."""
         self._reset_fit_state()
         x_b, batch_size = self._normalize_input(data)
+        if batch_size is None:  # unbatched (N, D) data: init tensors may come without the batch axis
+            init_means, init_covariances, init_weights = self._batched_init(init_means, init_covariances,
+                                                                            init_weights)
         self._require_engine()
         torch.manual_seed(self.seed)
         torch.cuda.manual_seed_all(self.seed)
@@ -295,6 +298,17 @@ class GMMXX:
         self._set_fit_result(labels_b=labels_b, means_b=means_b, variances_b=cov_b, weights_b=w_b, info=info,
                              batch_size=batch_size)
         return self
+
+    def _batched_init(self, init_means, init_covariances, init_weights):
+        """Initial parameters of an unbatched fit in the engine's (1, ...) shapes:
+        means (K, D), covariances (K,) / (K, D) / (D, D) / (K, D, D) by type and
+        weights (K,) gain the batch axis; tensors that already have it pass."""
+        cov_ndim = {"spherical": 1, "diag": 2, "tied": 2, "full": 3}[self.covariance_type]
+
+        def add(t, ndim):
+            return t.unsqueeze(0) if torch.is_tensor(t) and t.ndim == ndim else t
+
+        return add(init_means, 2), add(init_covariances, cov_ndim), add(init_weights, 1)
 
     def fit(self, data, y: Any = None, **init):
         del y

@@ -1,18 +1,25 @@
 """Host-resident X streamed through the GPU every EM iteration.
 
 Rebuild of the reference's large-N driver (gmmxx/large_n.py:866-1594,
-prefetcher 502-627): X stays in (pinned) host memory; each iteration streams
-it through two device chunk buffers on a copy stream while the compute stream
+prefetcher 502-627): X stays in host memory; each iteration streams it
+through two device chunk buffers on a copy stream while the compute stream
 runs ``gmmxx_em_accumulate`` on the previous chunk.  Statistics accumulate on
 the device across chunks, so the host never synchronises inside an iteration
-(the reference syncs once per chunk, large_n.py:313).  Like the reference it
+(the reference syncs once per chunk, large_n.py:313).  Pinned X is copied to
+the device straight from its rows; pageable X goes through two pinned staging
+chunks, so the extra host memory is two chunks, not a second copy of X (the
+reference's prefetcher stages the same way, large_n.py:502-573).
+
+With ``comm`` every rank streams its own row shard and the iteration's
+statistics are sum-allreduced, exactly as ``engine.em_fit`` does for
+device-resident shards (one collective per iteration).  Like the reference it
 handles B == 1.
 """
 
 from __future__ import annotations
 
+import contextlib
 import os
-import time
 from typing import Optional
 
 import torch
@@ -22,7 +29,15 @@ from . import engine
 
 
 class ChunkStreamer:
-    """Double-buffered host -> device row chunks (copy stream + events)."""
+    """Double-buffered host -> device row chunks (copy stream + events).
+
+    Every device buffer is refilled only after the compute stream has
+    finished with the chunk it last held, including a chunk yielded by an
+    earlier ``chunks()`` pass (the 'free' events carry over between passes).
+    For pageable X the rows are first copied on the host into one of two
+    pinned staging chunks; a staging chunk is refilled only after its previous
+    host -> device copy has completed (the host waits on that copy's event),
+    so the host copy of one chunk overlaps the device work of the other."""
 
     def __init__(self, x_host: torch.Tensor, chunk_rows: int, device: torch.device):
         if x_host.ndim != 3 or x_host.shape[0] != 1:
@@ -30,35 +45,107 @@ class ChunkStreamer:
         if x_host.is_cuda:
             raise ValueError("x_host must be in host memory")
         self.x = x_host.contiguous()
-        if not self.x.is_pinned():
-            self.x = self.x.pin_memory()
+        self.pinned = self.x.is_pinned()
         self.n, self.d = self.x.shape[1], self.x.shape[2]
         self.chunk = max(1, min(int(chunk_rows), self.n))
         self.device = device
         self.bufs = [torch.empty((1, self.chunk, self.d), dtype=self.x.dtype, device=device) for _ in range(2)]
+        self.stage = None
+        if not self.pinned:
+            self.stage = [torch.empty((1, self.chunk, self.d), dtype=self.x.dtype, pin_memory=True) for _ in range(2)]
         self.copy_stream = torch.cuda.Stream(device=device)
         self.copied = [torch.cuda.Event() for _ in range(2)]
         self.free = [torch.cuda.Event() for _ in range(2)]
+        self.free_recorded = [False, False]  # free[slot] was recorded at least once (any pass)
+        self.h2d_pending = [False, False]    # staging chunk slot has a copy that may be in flight
         self.h2d_bytes = 0
 
     def chunks(self):
-        """Yield (device view (1, rows, D), row offset); the caller's compute
-        stream must not outrun the yielded chunk's copy (handled here)."""
+        """Yield (device view (1, rows, D), row offset).  The compute stream
+        waits for each chunk's copy before the caller's work on it; the chunk's
+        buffer is released when the caller asks for the next one (or leaves
+        the loop)."""
         compute = torch.cuda.current_stream(self.device)
-        starts = list(range(0, self.n, self.chunk))
-        for ci, n0 in enumerate(starts):
+        for ci, n0 in enumerate(range(0, self.n, self.chunk)):
             slot = ci & 1
             n1 = min(n0 + self.chunk, self.n)
+            src = self.x[:, n0:n1]
+            if self.stage is not None:
+                if self.h2d_pending[slot]:
+                    self.copied[slot].synchronize()  # the staging chunk's previous copy has landed
+                staged = self.stage[slot][:, : n1 - n0]
+                staged.copy_(src)
+                src = staged
             with torch.cuda.stream(self.copy_stream):
-                if ci >= 2:
+                if self.free_recorded[slot]:
                     self.copy_stream.wait_event(self.free[slot])
                 dst = self.bufs[slot][:, : n1 - n0]
-                dst.copy_(self.x[:, n0:n1], non_blocking=True)
+                dst.copy_(src, non_blocking=True)
                 self.h2d_bytes += dst.numel() * dst.element_size()
                 self.copied[slot].record(self.copy_stream)
+            self.h2d_pending[slot] = True
             compute.wait_event(self.copied[slot])
-            yield dst, n0
-            self.free[slot].record(compute)
+            try:
+                yield dst, n0
+            finally:
+                self.free[slot].record(compute)
+                self.free_recorded[slot] = True
+
+
+class StreamedOps(engine.CudaOps):
+    """The four per-iteration kernels of ``engine.em_loop`` over host-resident
+    rows: ``xx_total`` and ``accumulate`` stream this rank's rows chunk by
+    chunk; ``prepare``, ``finalize`` and the status check are those of
+    device-resident X (``engine.CudaOps``)."""
+
+    def __init__(self, cov_type: str, streamer: ChunkStreamer, k: int, top_k: Optional[int] = None):
+        self.cov_type = cov_type
+        self.covc = engine.cov_code(cov_type)
+        self.st = streamer
+        self.b, self.n, self.d = 1, streamer.n, streamer.d
+        self.k = k
+        self.xdt = engine._X_DTYPES[streamer.x.dtype]
+        self.device = streamer.device
+        self.stream = engine._stream_ptr(streamer.device)
+        self.stat_width = nat.stat_width(self.covc, self.d)
+        self.ws = engine._WS.get(streamer.device, nat.workspace_bytes(self.covc, 1, streamer.chunk, self.d, k))
+        self.top_k = top_k
+        self.paths = set()
+        self.scratch = None
+        if top_k is not None:
+            self.scratch = torch.empty(nat.topk_scratch_bytes(1, streamer.chunk, top_k), dtype=torch.uint8,
+                                       device=streamer.device)
+
+    def xx_total(self, xx: torch.Tensor) -> None:
+        for xc, _ in self.st.chunks():
+            nat.call("gmmxx_xx_total", self.xdt, xc.data_ptr(), 1, xc.shape[1], self.d, xx.data_ptr(),
+                     self.ws.data_ptr(), self.ws.numel(), self.stream)
+
+    def accumulate(self, stats, ll) -> None:
+        for xc, _ in self.st.chunks():
+            n = xc.shape[1]
+            if self.top_k is not None:
+                nat.call("gmmxx_em_accumulate_topk", self.covc, self.xdt, xc.data_ptr(), 1, n, self.d, self.k,
+                         self.top_k, self.ws.data_ptr(), self.ws.numel(), self.scratch.data_ptr(),
+                         self.scratch.numel(), stats.data_ptr(), ll.data_ptr(), self.stream)
+                continue
+            nat.call("gmmxx_em_accumulate", self.covc, self.xdt, xc.data_ptr(), 1, n, self.d, self.k,
+                     self.ws.data_ptr(), self.ws.numel(), stats.data_ptr(), ll.data_ptr(), self.stream)
+            self.paths.add(nat.last_accumulate_path())
+
+
+def _device_ctx(device: torch.device):
+    return torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext()
+
+
+def _from_rank0(comm, make, shape, dtype, device) -> torch.Tensor:
+    """``make()`` evaluated on rank 0 and broadcast (every rank the same
+    initial parameter); without ``comm`` just ``make()``."""
+    if comm is None:
+        return make()
+    t = make().to(device=device, dtype=dtype).contiguous() if comm.rank == 0 else \
+        torch.zeros(shape, dtype=dtype, device=device)
+    return comm.broadcast_(t, 0)
 
 
 def em_fit_streamed(
@@ -80,105 +167,68 @@ def em_fit_streamed(
     verbose: bool = False,
     streamer: Optional[ChunkStreamer] = None,
     approx_top_k: Optional[int] = None,
+    comm: Optional[engine.Comm] = None,
 ):
     """Soft EM over host-resident X (B == 1), streamed chunk by chunk;
     ``approx_top_k`` as in engine.em_fit (the reference's large-N driver takes
-    the same option, large_n.py:887-1005)."""
-    covc = engine.cov_code(cov_type)
+    the same option, large_n.py:887-1005).
+
+    With ``comm``, ``x_host`` is this rank's row shard: the fit is over the
+    union of the shards (statistics allreduced once per iteration, the
+    finalize replicated), the initial means / covariances that are not given
+    are drawn on rank 0 and broadcast, and the returned labels are the
+    shard's."""
+    engine.cov_code(cov_type)
     device = torch.device(device)
     if x_host.dtype not in engine._X_DTYPES:
         raise TypeError(f"x dtype {x_host.dtype} not supported")
     b, n, d = x_host.shape
     engine.check_window(cov_type, d)
-    if n == 0:
-        raise ValueError("x must contain at least one sample")
-    with torch.cuda.device(device):
+    if max_iters <= 0:
+        raise ValueError("max_iters must be positive")
+    with _device_ctx(device):
+        n_total = n
+        if comm is not None:
+            nt = torch.tensor([n], dtype=torch.int64, device=device)
+            comm.allreduce_(nt)
+            n_total = int(nt.item())
+        if n_total == 0:
+            raise ValueError("x must contain at least one sample")
         st = streamer or ChunkStreamer(x_host, chunk_rows, device)
         if init_means is None:
             if init_params not in {"kmeans", "random"}:
                 raise ValueError("init_params must be 'kmeans' or 'random'")
-            idx = torch.randint(0, n, (1, n_components))
-            init_means = torch.gather(st.x, 1, idx[..., None].expand(-1, -1, d)).float()
-        # initial covariance from the full data when not given
-        if init_variances is None:
-            sample = st.x[:, :: max(1, n // (1 << 20))].to(device)
-            init_variances = engine.global_covariance(cov_type, sample, init_means.shape[1], reg_covar)
+
+            def draw():  # _random_init_means (torch_fallback.py:1384-1387) over this shard's rows
+                idx = torch.randint(0, n, (1, n_components))
+                return torch.gather(st.x, 1, idx[..., None].expand(-1, -1, d)).float()
+
+            init_means = _from_rank0(comm, draw, (1, n_components, d), torch.float32, device)
+        k = init_means.shape[1]
+        if init_variances is None:  # from a row sample of the (rank-0) data
+            def gcov():
+                sample = st.x[:, :: max(1, n // (1 << 20))].to(device)
+                return engine.global_covariance(cov_type, sample, k, reg_covar)
+
+            shape = {"spherical": (1, k), "diag": (1, k, d), "tied": (1, d, d), "full": (1, k, d, d)}[cov_type]
+            init_variances = _from_rank0(comm, gcov, shape, torch.float32, device)
         probe = st.bufs[0][:, :1]
         means, cov, weights, source = engine.initial_parameters(
             cov_type, probe, n_components, init_means, init_variances, init_weights, reg_covar, init_params)
-        k = means.shape[1]
         top_k = engine.resolve_approx_top_k(approx_top_k, k)
-        scratch = None
-        if top_k is not None:
-            scratch = torch.empty(nat.topk_scratch_bytes(1, st.chunk, top_k), dtype=torch.uint8, device=device)
-        stream = engine._stream_ptr(device)
-        f = nat.stat_width(covc, d)
-        ws = engine._WS.get(device, nat.workspace_bytes(covc, 1, st.chunk, d, k))
-        stats = torch.zeros((1, k, f), dtype=torch.float32, device=device)
-        ll = torch.zeros((1,), dtype=torch.float64, device=device)
-        lb_hist = torch.zeros((max_iters,), dtype=torch.float32, device=device)
-        xdt = engine._X_DTYPES[x_host.dtype]
-        xx = None
-        if covc == nat.TIED:
-            xx = torch.zeros((1, d, d), dtype=torch.float32, device=device)
-            for xc, _ in st.chunks():
-                nat.call("gmmxx_xx_total", xdt, xc.data_ptr(), 1, xc.shape[1], d, xx.data_ptr(), ws.data_ptr(),
-                         ws.numel(), stream)
-        prev = None
-        it = 0
-        t0 = time.perf_counter()
-        for it in range(max_iters):
-            nat.call("gmmxx_em_prepare", covc, 1, d, k, means.data_ptr(), cov.data_ptr(), weights.data_ptr(),
-                     float(reg_covar), float(min_weight), ws.data_ptr(), ws.numel(), stream)
-            stats.zero_()
-            ll.zero_()
-            for xc, _ in st.chunks():
-                if top_k is not None:
-                    nat.call("gmmxx_em_accumulate_topk", covc, xdt, xc.data_ptr(), 1, xc.shape[1], d, k, top_k,
-                             ws.data_ptr(), ws.numel(), scratch.data_ptr(), scratch.numel(), stats.data_ptr(),
-                             ll.data_ptr(), stream)
-                    continue
-                nat.call("gmmxx_em_accumulate", covc, xdt, xc.data_ptr(), 1, xc.shape[1], d, k, ws.data_ptr(),
-                         ws.numel(), stats.data_ptr(), ll.data_ptr(), stream)
-            if verbose:
-                prev_means = means.clone()
-            nat.call("gmmxx_em_finalize", covc, 1, d, k, n, stats.data_ptr(), ll.data_ptr(), engine._p(xx),
-                     float(reg_covar), float(min_weight), means.data_ptr(), cov.data_ptr(), weights.data_ptr(),
-                     lb_hist[it:].data_ptr(), stream)
-            if verbose or tol > 0.0:
-                lb = float(lb_hist[it].item())
-                if verbose:
-                    print(engine.verbose_line(cov_type, it, lb, means, prev_means))
-                if tol > 0.0 and prev is not None and it + 1 < max_iters and abs(lb - prev) < tol:
-                    break
-                prev = lb
-        elapsed = time.perf_counter() - t0
-        n_iter = it + 1
-        hist = lb_hist[:n_iter].tolist()
-        if cov_type != "spherical" and not (tol > 0.0 or verbose):
-            hist = [0.0] * (n_iter - 1) + [hist[-1]]
+        ops = StreamedOps(cov_type, st, k, top_k)
+        n_iter, hist, elapsed = engine.em_loop(ops, cov_type, means, cov, weights, n_total=n_total,
+                                               max_iters=max_iters, tol=tol, reg_covar=reg_covar,
+                                               min_weight=min_weight, verbose=verbose, comm=comm)
         labels = None
         if compute_labels:
             labels = torch.empty((1, n), dtype=torch.int64, device=device)
             for xc, n0 in st.chunks():
                 labels[:, n0:n0 + xc.shape[1]] = engine.assign(cov_type, xc, means, cov, weights)
-    info = {
-        "n_iter": n_iter,
-        "lower_bound": hist[-1],
-        "lower_bound_history": hist,
-        "init_source": source,
-        "triton_estep_enabled": False,
-        "triton_fused_update_enabled": False,
-        "triton_streaming_update_enabled": False,
-        "approximate_em_enabled": top_k is not None,
-        "approx_top_k": top_k,
-        "cuda_approx_topk_enabled": top_k is not None,
-        "large_n_streaming_enabled": True,
-        "copy_stream_prefetch_enabled": True,
-        "cuda_engine": "gmmxx_b200",
-        "backend_breakdown": {"cuda": n_iter},
-        "ms_per_iter": 1e3 * elapsed / n_iter,
-    }
+    info = engine.fit_info(n_iter, hist, source, elapsed, gpus=1 if comm is None else comm.world_size,
+                           approximate_em_enabled=top_k is not None, approx_top_k=top_k,
+                           cuda_approx_topk_enabled=top_k is not None, large_n_streaming_enabled=True,
+                           copy_stream_prefetch_enabled=True, kernel_path=ops.kernel_path())
     return labels, means, cov, weights, info
 
 

@@ -98,10 +98,20 @@ GMMXX_API size_t gmmxx_workspace_bytes(int cov_type, int64_t B, int64_t N, int64
  * and stats_reduce_kernel; em_small_kernel and stats_reduce_kernel when
  * K <= 64).  Honours GMMXX_B200_KERNEL.  A device that cannot
  * co-schedule the kernel's thread-block cluster falls back to the CUDA-core
- * kernels at launch time, which this query does not predict.  No counterpart
- * in the reference (its dispatch is the Python table in _runtime.py:31-216). */
+ * kernels at launch time, which this query does not predict; read
+ * gmmxx_last_accumulate_path after the call for the path that ran.  No
+ * counterpart in the reference (its dispatch is the Python table in
+ * _runtime.py:31-216). */
 GMMXX_API int gmmxx_accumulate_path(int cov_type, int x_dtype, int64_t B, int64_t N, int64_t D, int64_t K,
                                     int* path_out);
+
+/* The statistics kernels the last successful gmmxx_em_accumulate call on this
+ * host thread launched: 1 tensor-core kernels, 0 CUDA-core kernels as
+ * planned, 2 CUDA-core kernels because the tensor-core launch found no
+ * co-resident thread-block cluster (the fallback), -1 no call yet.  The
+ * choice is made on the host when the call launches, so the value is exact
+ * without a synchronisation.  No counterpart in the reference. */
+GMMXX_API int gmmxx_last_accumulate_path(void);
 
 /* Reads (and clears) the sticky device status word kept in `workspace`
  * (GMMXX_OK, GMMXX_ERR_NOT_PD, GMMXX_ERR_TIMEOUT, or GMMXX_ERR_UNSUPPORTED when
@@ -218,7 +228,8 @@ GMMXX_API int gmmxx_predict_proba(int cov_type, int x_dtype, const void* x,
  * device array of 8 MiB that every GPU loading this library keeps until the
  * process exits; shapes whose table does not fit return GMMXX_ERR_WORKSPACE.
  * The first call on a device looks up that array's device address (make it
- * before any stream capture).  All calls on a device share the array, so
+ * before any stream capture); so does the first call after the device's
+ * context was torn down and created again.  All calls on a device share the array, so
  * calls that overlap on the GPU race; the covariance status word (jitter
  * ladder) is cleared per call and not reported. */
 GMMXX_API int gmmxx_logsumexp_noalloc(int cov_type, int x_dtype, const void* x,

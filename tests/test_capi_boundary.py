@@ -233,3 +233,9 @@ def test_missing_library_raises_cuda_backend_unavailable():
     out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
     assert out.returncode == 0, out.stderr
     assert "unavailable: True" in out.stdout
+
+
+def test_last_accumulate_path_before_any_call(lib):
+    # no accumulate call has succeeded on this thread (none can without a GPU)
+    assert lib.gmmxx_last_accumulate_path() in (-1, 0, 1, 2)
+    assert _native.PATH_NAMES[-1] is None

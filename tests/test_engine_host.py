@@ -88,3 +88,37 @@ def test_engine_windows():
         engine.check_x(torch.zeros(4, 2))
     with pytest.raises(TypeError):
         engine.check_x([[0.0]])
+
+
+def test_kernel_path_names():
+    from gmmxx_b200 import engine
+
+    assert engine.kernel_path_name({1}) == "tensor-core"
+    assert engine.kernel_path_name({0}) == "cuda-core"
+    assert "no co-resident cluster" in engine.kernel_path_name({2})
+    assert engine.kernel_path_name({1, 2}).startswith("tensor-core + cuda-core")
+    assert engine.kernel_path_name(set()) == "none"
+
+
+def test_accumulate_records_the_no_cluster_fallback(monkeypatch):
+    """CudaOps.accumulate keeps what the library reports after each call
+    (gmmxx_last_accumulate_path); a tensor-core launch that found no
+    co-resident cluster and ran the CUDA-core kernels is named in fit_info's
+    kernel_path."""
+    import types
+
+    from gmmxx_b200 import _native as nat
+    from gmmxx_b200 import engine
+
+    ops = object.__new__(engine.CudaOps)
+    ops.top_k, ops.paths = None, set()
+    ops.covc, ops.xdt, ops.b, ops.n, ops.d, ops.k = nat.DIAG, nat.BFLOAT16, 1, 70_000, 64, 128
+    ops.x = types.SimpleNamespace(data_ptr=lambda: 0)
+    ops.ws = torch.zeros(16, dtype=torch.uint8)
+    ops.stream = 0
+    calls = []
+    monkeypatch.setattr(nat, "call", lambda name, *a: calls.append(name))
+    monkeypatch.setattr(nat, "last_accumulate_path", lambda: 2)
+    ops.accumulate(torch.zeros(4), torch.zeros(1, dtype=torch.float64))
+    assert calls == ["gmmxx_em_accumulate"]
+    assert ops.kernel_path() == nat.PATH_NAMES[2]

@@ -275,3 +275,107 @@ def test_verbose_lines_match_the_reference_format(cov_type, extra, capsys):
         assert float(mt.group(2)) == pytest.approx(hist[it], abs=1e-6)
     # the first iteration moves the means away from their initial rows
     assert float(re.fullmatch(pat, lines[0]).group(3)) > 0.0
+
+
+# ---------------------------------------------------------------------------
+# the host-streamed driver sharded over ranks (large_n.em_fit_streamed)
+# ---------------------------------------------------------------------------
+
+
+class CpuChunker:
+    """CPU stand-in for ``large_n.ChunkStreamer``: the shard's row chunks in
+    order (no device buffers or streams)."""
+
+    def __init__(self, x_host, chunk_rows, device):
+        self.x = x_host
+        self.n, self.d = x_host.shape[1], x_host.shape[2]
+        self.chunk = max(1, min(int(chunk_rows), self.n))
+        self.device = torch.device(device)
+        self.bufs = [x_host[:, :self.chunk]]
+        self.passes = 0
+
+    def chunks(self):
+        self.passes += 1
+        for n0 in range(0, self.n, self.chunk):
+            yield self.x[:, n0:n0 + self.chunk], n0
+
+
+class OracleStreamOps(OracleOps):
+    """``large_n.StreamedOps`` on the CPU: OracleOps over each streamed chunk."""
+
+    def __init__(self, cov_type, streamer, k, top_k=None):
+        super().__init__(cov_type, streamer.x.numpy(), k, top_k)
+        self.st = streamer
+
+    def accumulate(self, stats, ll):
+        whole = self.x
+        try:
+            for xc, _ in self.st.chunks():
+                self.x = xc.numpy().astype(np.float64)
+                self.n = self.x.shape[1]
+                super().accumulate(stats, ll)
+        finally:
+            self.x, self.n = whole, whole.shape[1]
+
+    def kernel_path(self):
+        return "oracle"
+
+
+def _stream_rank_main(rank, world, port, cov_type, iters, out_dir, given_init):
+    from gmmxx_b200 import engine, large_n
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        large_n.ChunkStreamer = CpuChunker
+        large_n.StreamedOps = OracleStreamOps
+        x, m0, c0, w0 = _problem(cov_type, b=1)
+        n = x.shape[1]
+        lo, hi = rank * n // world, (rank + 1) * n // world
+        shard = torch.from_numpy(np.ascontiguousarray(x[:, lo:hi], dtype=np.float32))
+        torch.manual_seed(100 + rank)  # a rank-local draw would differ between ranks
+        init = dict(init_means=torch.from_numpy(m0), init_variances=torch.from_numpy(c0),
+                    init_weights=torch.from_numpy(w0)) if given_init else dict(init_params="random")
+        _, means, cov, weights, info = large_n.em_fit_streamed(
+            cov_type, shard, m0.shape[1], device="cpu", chunk_rows=70, max_iters=iters, tol=0.0,
+            compute_labels=False, comm=engine.Comm(), **init)
+        np.savez(os.path.join(out_dir, f"s{rank}.npz"), means=means.numpy(), cov=cov.numpy(),
+                 weights=weights.numpy(), hist=np.array(info["lower_bound_history"]), gpus=info["gpus"])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("cov_type,given_init", [("diag", True), ("tied", True), ("spherical", False),
+                                                 ("full", False)])
+def test_sharded_streamed_fit(cov_type, given_init, tmp_path):
+    """Each rank streams its own shard in chunks; one allreduce per iteration
+    joins them.  With given initial parameters the fit equals the
+    single-process oracle on all rows; with drawn ones, rank 0's draw is
+    broadcast, so the ranks still end identical."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_stream_rank_main, args=(r, 2, port, cov_type, 4, str(tmp_path), given_init))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+            pytest.fail("a rank did not finish within 120 s")
+    assert [p.exitcode for p in procs] == [0, 0]
+    r0, r1 = np.load(tmp_path / "s0.npz"), np.load(tmp_path / "s1.npz")
+    for key in ("means", "cov", "weights", "hist"):
+        assert np.array_equal(r0[key], r1[key]), f"ranks disagree on {key}"
+    assert int(r0["gpus"]) == 2
+    if given_init:
+        x, m0, c0, w0 = _problem(cov_type, b=1)
+        _, m, c, w, info = orc.fit(cov_type, x, m0.shape[1], 4, 0.0, m0, c0, w0, compute_labels=False,
+                                   dtype=np.float64)
+        np.testing.assert_allclose(r0["means"], m, rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(r0["cov"], c, rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(r0["weights"], w, rtol=1e-5, atol=1e-7)
+        np.testing.assert_allclose(r0["hist"][-1], info["lower_bound_history"][-1], rtol=1e-6)
