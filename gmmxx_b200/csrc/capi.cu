@@ -125,6 +125,7 @@ tc::TcLaunch make_tc(int cov, const void* x, int64_t N, int64_t D, int64_t K, co
   t.lse = reinterpret_cast<float*>(ws + (L.tc_lse ? L.tc_lse : L.lse));
   t.wt = reinterpret_cast<const float*>(ws + L.wt);
   t.cc = reinterpret_cast<const CompConst*>(ws + L.cc);
+  t.linv = cov == GMMXX_TIED ? reinterpret_cast<const float*>(ws + L.linv) : nullptr;
   t.params = ws + L.tc_params;
   t.consts = reinterpret_cast<float*>(ws + L.tc_consts);
   t.part = reinterpret_cast<float*>(ws + L.tc_part);
@@ -253,7 +254,7 @@ int gmmxx_accumulate_path(int cov_type, int x_dtype, int64_t B, int64_t N, int64
   if (int rc = check_shape(cov_type, x_dtype, B, N, D, K)) return rc;
   GMMXX_REQUIRE(path_out, "path_out");
   const Layout L = make_layout(cov_type, B, N, D, K);
-  const bool tc_ok = L.tc_cluster > 0 && x_dtype == GMMXX_BFLOAT16;
+  const bool tc_ok = L.tc_cluster > 0 && tc_dtype_ok(cov_type, x_dtype);
   *path_out = (tc_ok && kernel_mode() != 1) ? 1 : 0;
   return GMMXX_OK;
 }
@@ -270,7 +271,7 @@ int gmmxx_em_accumulate(int cov_type, int x_dtype, const void* x, int64_t B, int
   char* ws = static_cast<char*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int mode = kernel_mode();
-  const bool tc_ok = L.tc_cluster > 0 && x_dtype == GMMXX_BFLOAT16;
+  const bool tc_ok = L.tc_cluster > 0 && tc_dtype_ok(cov_type, x_dtype);
   bool fallback = false;
   if (mode == 2 && !tc_ok)
     return set_error(GMMXX_ERR_UNSUPPORTED, "tensor-core kernel required but the shape / dtype is outside its window");

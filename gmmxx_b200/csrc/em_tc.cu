@@ -645,9 +645,50 @@ __global__ void tc_pack_kernel(int K, int64_t Kp_table, const float* wt, const C
   }
 }
 
+// Tied covariance (em_tc_diag.cu, tied mode): per chunk three term blocks of
+// [192 rows][64 features] bf16 with 128-byte swizzle -- rows 0-127 the
+// chunk's components' x coefficient -2 (P mu)_d, rows 128 + i row
+// 16 p0 + i of L^-1 for the pieces [p0, p1) of y = L^-1 x that this chunk's
+// cluster rank computes (the 4 pieces of 16 rows spread over the C ranks),
+// each value split into three bf16 terms; then the epilogue constants.
+__global__ void tc_pack_tied_kernel(int K, int64_t Kp_table, int csize, const float* wt, const float* linv,
+                                    const CompConst* cc, char* params, float* consts) {
+  const int row = blockIdx.x % 192, chunk = blockIdx.x / 192;
+  char* img = params + (int64_t)chunk * 3 * kTiedTermBytes;
+  const int p0 = 4 * chunk / csize, p1 = 4 * (chunk + 1) / csize;
+  const int k = chunk * kKC + row;
+  for (int d = threadIdx.x; d < 64; d += blockDim.x) {
+    float v = 0.f;
+    if (row < kKC) {
+      if (k < K) v = wt[(int64_t)d * Kp_table + k];
+    } else if (row - kKC < 16 * (p1 - p0)) {
+      v = linv[(16 * p0 + (row - kKC)) * 64 + d];
+    }
+#pragma unroll
+    for (int j = 0; j < kNS; ++j) {
+      const __nv_bfloat16 h = __float2bfloat16(v);
+      *reinterpret_cast<__nv_bfloat16*>(img + j * kTiedTermBytes + sw128(row, d)) = h;
+      v -= __bfloat162float(h);
+    }
+  }
+  if (threadIdx.x == 0 && row < kKC) {
+    float* cs = consts + (int64_t)chunk * 3 * 128;
+    if (k < K) {
+      const CompConst q = cc[k];
+      cs[row] = q.mpm;
+      cs[128 + row] = 0.5f * kLog2e * q.s;
+      cs[256 + row] = kLog2e * (q.lw - 0.5f * q.ln);
+    } else {
+      cs[row] = 0.f;
+      cs[128 + row] = 0.f;
+      cs[256 + row] = -INFINITY;
+    }
+  }
+}
+
 // stats[k][f] += sum over clusters of part[cl][k][f] (fixed order), ll += sum part_ll
 __global__ void tc_reduce_kernel(const float* part, const double* part_ll, int ncl, int K, int64_t Kp, int F,
-                                 float* stats, double* ll) {
+                                 float* stats, double* ll, int n_ll) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < (int64_t)K * F) {
     const int64_t k = i / F, f = i - k * F;
@@ -657,7 +698,7 @@ __global__ void tc_reduce_kernel(const float* part, const double* part_ll, int n
   }
   if (i == 0 && ll != nullptr) {
     double s = 0.0;
-    for (int c = 0; c < ncl; ++c) s += part_ll[c];
+    for (int c = 0; c < n_ll; ++c) s += part_ll[c];
     *ll += s;
   }
 }
@@ -737,7 +778,11 @@ EncodeTiledFn encode_fn() {
 
 int launch_tc_pack(int cov, int db, const TcLaunch& L, cudaStream_t st) {
   const unsigned grid = (unsigned)(L.nchunks * kKC);
-  if (cov == GMMXX_DIAG && db == 1)
+  if (cov == GMMXX_TIED && db == 1) {
+    if (L.linv == nullptr) return set_error(GMMXX_ERR_WORKSPACE, "tied tensor-core pack: no L^-1 in the workspace");
+    tc_pack_tied_kernel<<<(unsigned)(L.nchunks * 192), 64, 0, st>>>(L.K, L.Kp_table, L.cluster_size, L.wt, L.linv,
+                                                                    L.cc, L.params, L.consts);
+  } else if (cov == GMMXX_DIAG && db == 1)
     tc_pack_kernel<GMMXX_DIAG, 1><<<grid, 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
   else if (cov == GMMXX_SPHERICAL && db == 1)
     tc_pack_kernel<GMMXX_SPHERICAL, 1><<<grid, 64, 0, st>>>(L.K, L.Kp_table, L.wt, L.cc, L.params, L.consts);
@@ -748,25 +793,28 @@ int launch_tc_pack(int cov, int db, const TcLaunch& L, cudaStream_t st) {
   return check_launch("tc_pack_kernel");
 }
 
-int make_x_tensor_map(const TcLaunch& L, CUtensorMap* tmap) {
-  // X (N rows x D bf16), 128-row x 64-column boxes, 128-byte swizzle
+int make_x_tensor_map(const TcLaunch& L, CUtensorMap* tmap, bool fp32) {
+  // X (N rows x D), 128-row boxes of 128 bytes per row (64 bf16 or 32 fp32
+  // columns), 128-byte swizzle
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return set_error(GMMXX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t esz = fp32 ? 4 : 2;
   cuuint64_t dims[2] = {(cuuint64_t)L.D, (cuuint64_t)L.N};
-  cuuint64_t strides[1] = {(cuuint64_t)L.D * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)kBM};
+  cuuint64_t strides[1] = {(cuuint64_t)L.D * esz};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esz), (cuuint32_t)kBM};
   cuuint32_t es[2] = {1, 1};
-  CUresult cr = enc(tmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(L.x), dims, strides, box, es,
+  CUresult cr = enc(tmap, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                    const_cast<void*>(L.x), dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return set_error(GMMXX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
   return GMMXX_OK;
 }
 
-int launch_tc_reduce(const TcLaunch& L, int ncl, cudaStream_t st) {
+int launch_tc_reduce(const TcLaunch& L, int ncl, cudaStream_t st, int n_ll) {
   const int64_t n = (int64_t)L.K * L.F;
-  tc_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(L.part, L.part_ll, ncl, L.K,
-                                                                                      L.Kp_part, L.F, L.stats, L.ll);
+  tc_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(
+      L.part, L.part_ll, ncl, L.K, L.Kp_part, L.F, L.stats, L.ll, n_ll < 0 ? ncl : n_ll);
   return check_launch("tc_reduce_kernel");
 }
 
@@ -953,6 +1001,7 @@ static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
 
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st) {
   if (cov == GMMXX_DIAG && L.D == 64 && L.cluster_size <= kMaxClusterDiag) return launch_em_tc_diag(L, st);
+  if (cov == GMMXX_TIED) return launch_em_tc_tied(L, st);
   if (L.infer != 0) {
     if (cov == GMMXX_SPHERICAL && L.D == 64) return launch_sph_infer<1>(L, st);
     if (cov == GMMXX_SPHERICAL && L.D == 128) return launch_sph_infer<2>(L, st);

@@ -34,8 +34,27 @@
 // fp32 accumulation.  Statistics leave the kernel once per cluster as
 // partials that tc_reduce_kernel sums in a fixed order.
 //
+// Tied covariance, fp32 X (kTied): the same pipeline with
+//   TMA       X(t) fp32 as two 32-column boxes (32 KB staging)
+//   prep      x split exactly into three bf16 planes x_hi + x_mid + x_lo (24
+//             significant bits); the E-step operand [x_hi | x_mid | x_lo] in
+//             tensor memory; the M-step stage receives X(t) again by TMA and
+//             the prep turns it into the three planes in place
+//   MMA       E-step S(t) = x . (-2 P mu_k) over the plane / weight-term pairs
+//             whose term indices sum to <= 2 (6 products, 24 instructions), in
+//             the same instructions 16-64 extra columns y = L^-1 x (this
+//             rank's pieces of it, P = L^-T L^-1); M-step
+//             R^T . [x_hi | x_mid | x_lo | 1] (the diag kernel's N = 208 shape)
+//   softmax   logits without the per-row term x^T P x (it cancels in r), which
+//             enters the log-likelihood per row as -|y|^2 / 2, summed over the
+//             cluster ranks' pieces
+// so the distance is not clamped at zero as in the reference's
+// (x^T P x - 2 x.P mu + mu^T P mu).clamp_min(0): the unclamped value is a
+// positive definite quadratic form and differs from zero by rounding only.
+//
 // Reference semantics: gmmxx/torch_fallback.py:2508-2651 (diag E/M chunk
-// loop), expanded-distance logits 357-397.
+// loop), expanded-distance logits 357-397; tied 435-465 (logits), 2912-3139
+// (matrix E/M loop).
 #include "gmm_common.cuh"
 #include "tc_ptx.cuh"
 #include "tc_api.cuh"
@@ -59,10 +78,7 @@ constexpr int kPart = kKC / kSplit;      // components per softmax thread
 constexpr int kSoftWarps = 4 * kSplit;   // every TMEM lane quarter kSplit times
 constexpr int kBlock = 16384;   // one [128][64] bf16 swizzled block
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSCol = 0;     // E-step logits S (128 columns)
-constexpr uint32_t kDmCol = 128;  // M-step statistics [x | s_hi | s_lo (64 each) | 1 (16)]
-constexpr uint32_t kFCol = 336;   // E-step operand [x | s_hi | s_lo], 32 columns each
-constexpr int kFdm = 208;
+constexpr int kFdm = 208;       // M-step columns [x | s_hi | s_lo | 1] (tied: [x_hi | x_mid | x_lo | 1])
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (diag: s = 1)
@@ -73,23 +89,40 @@ enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpSoftmax0 = 6 };
 enum Mode { kModeEm = 0, kModeLse = 1, kModeArgmax = 2, kModeProba = 3 };
 constexpr int kThreads = (kWarpSoftmax0 + kSoftWarps) * 32;  // 22 warps, <= 88 registers each
 
-// shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
-constexpr int kParams = 0;                     // a_0 a_1 a_2 | v_0 v_1 v_2 (16 KB each)
-constexpr int kStaging = kParams + 2 * kNS * kBlock;  // X staging slot
-constexpr int kMX = kStaging + kBlock;         // M-step stage: x | s_hi | s_lo | ones
-                                               // (predict_proba: the tile's fp32 rows)
-constexpr int kMSH = kMX + kBlock;
-constexpr int kMSL = kMSH + kBlock;
-constexpr int kOnes = kMSL + kBlock;           // MN-major, column 0 = 1 (constant)
-constexpr int kR = kOnes + kBlock;             // R: two 64-component MN groups
-constexpr int kConsts = kR + 2 * kBlock;       // lz[128], c2[128]
-constexpr int kHalfX = kConsts + 2 * 128 * 4;  // [2 slots][kSplit parts][128 rows] float2
-constexpr int kXch = kHalfX + 2 * kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
-__host__ __device__ constexpr int bars_off(int c) { return kXch + 2 * c * 128 * 8; }
-__host__ __device__ constexpr int red_off(int c) { return bars_off(c) + 192; }
-__host__ __device__ constexpr int smem_total(int c) { return bars_off(c) + 256; }
-static_assert(smem_total(kMaxCluster) <= 232448, "shared memory budget");
-static_assert(kFCol + 96 <= kTmemCols && kDmCol + kFdm <= kFCol && kSCol + kKC <= kDmCol, "tensor memory budget");
+// Shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
+// and tensor memory columns; kTied: the tied-covariance layout.
+template <bool kTied>
+struct Lay {
+  // weights: diag a_0 a_1 a_2 | v_0 v_1 v_2 (16 KB each); tied three terms of
+  // [192 rows][64] (components, then this rank's rows of L^-1)
+  static constexpr int kWBytes = kTied ? kTiedTermBytes : kBlock;
+  static constexpr int kWBlocks = kTied ? kNS : 2 * kNS;
+  static constexpr int kParams = 0;
+  static constexpr int kStaging = kParams + kWBlocks * kWBytes;  // X staging slot (fp32: two boxes)
+  static constexpr int kMX = kStaging + (kTied ? 2 : 1) * kBlock;  // M-step stage: x | s_hi | s_lo | ones
+                                                                   // (tied: x_hi | x_mid | x_lo | ones;
+                                                                   // predict_proba: the tile's fp32 rows)
+  static constexpr int kMSH = kMX + kBlock;
+  static constexpr int kMSL = kMSH + kBlock;
+  static constexpr int kOnes = kMSL + kBlock;           // MN-major, column 0 = 1 (constant)
+  static constexpr int kR = kOnes + kBlock;             // R: two 64-component MN groups
+  static constexpr int kConsts = kR + 2 * kBlock;       // lz[128], c2[128]
+  static constexpr int kHalfX = kConsts + 2 * 128 * 4;  // [2 slots][kSplit parts][128 rows] float2
+  static constexpr int kXch = kHalfX + 2 * kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
+  __host__ __device__ static constexpr int bars(int c) { return kXch + 2 * c * 128 * 8; }
+  // the log-likelihood reduction slot: 4 doubles (diag), 16 (tied)
+  __host__ __device__ static constexpr int red(int c) { return bars(c) + 192; }
+  __host__ __device__ static constexpr int total(int c) { return bars(c) + (kTied ? 320 : 256); }
+  // tensor memory: S (+ tied: up to 64 columns of y) | M-step statistics | E-step operand
+  static constexpr uint32_t kSCol = 0;
+  static constexpr uint32_t kDmCol = kTied ? 192 : 128;
+  static constexpr uint32_t kFCol = kDmCol + kFdm;
+};
+static_assert(Lay<false>::total(kMaxCluster) <= 232448 && Lay<true>::total(kMaxCluster) <= 232448,
+              "shared memory budget");
+static_assert(Lay<false>::kFCol + 96 <= kTmemCols && Lay<true>::kFCol + 96 <= kTmemCols, "tensor memory budget");
+static_assert(Lay<true>::kStaging % 1024 == 0 && Lay<true>::kMX % 1024 == 0 && Lay<true>::kR % 1024 == 0,
+              "swizzled blocks need 1024-byte alignment");
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -133,10 +166,24 @@ __device__ __forceinline__ void square_split(uint32_t w, uint32_t& hi, uint32_t&
   lo = pack_bf16(s0 - bf16lo_to_f32(hi), s1 - bf16hi_to_f32(hi));
 }
 
-template <int kMode>
+// two fp32 values -> three packed bf16 pairs with x = hi + mid + lo to 24
+// significant bits (each residual is exact in fp32)
+__device__ __forceinline__ void split3(float x0, float x1, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+  hi = pack_bf16(x0, x1);
+  const float r0 = x0 - bf16lo_to_f32(hi), r1 = x1 - bf16hi_to_f32(hi);
+  mid = pack_bf16(r0, r1);
+  lo = pack_bf16(r0 - bf16lo_to_f32(mid), r1 - bf16hi_to_f32(mid));
+}
+
+template <int kMode, bool kTied>
 __global__ void __launch_bounds__(kThreads, 1)
     em_tc_diag_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
   constexpr bool kEm = kMode == kModeEm;
+  static_assert(kEm || !kTied, "the tied kernel computes EM statistics only");
+  using Y = Lay<kTied>;
+  constexpr int kParams = Y::kParams, kStaging = Y::kStaging, kMX = Y::kMX, kMSH = Y::kMSH, kMSL = Y::kMSL;
+  constexpr int kOnes = Y::kOnes, kR = Y::kR, kConsts = Y::kConsts, kHalfX = Y::kHalfX, kXch = Y::kXch;
+  constexpr uint32_t kSCol = Y::kSCol, kDmCol = Y::kDmCol, kFCol = Y::kFCol;
   extern __shared__ __align__(1024) char smem_raw[];
   char* sm = smem_raw;
   if ((smem_u32(smem_raw) & 1023u) != 0) {  // uniform across the grid: no CTA proceeds
@@ -144,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   const int nclus = a.cluster_size;
-  Bars* bars = reinterpret_cast<Bars*>(sm + bars_off(nclus));
+  Bars* bars = reinterpret_cast<Bars*>(sm + Y::bars(nclus));
   float* c_lz = reinterpret_cast<float*>(sm + kConsts);  // c2 - h mpm: the logit at S = 0
   float* c_c2 = c_lz + 128;
   float2* xch = reinterpret_cast<float2*>(sm + kXch);
@@ -157,6 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t ncl = ncluster_x();
   const int64_t ntiles = (a.N + kBM - 1) / kBM;
   const int T = (int)((ntiles > (int64_t)cid) ? (ntiles - 1 - cid) / ncl + 1 : 0);
+  // tied: this rank's pieces [p0, p1) of the 4 sixteen-column pieces of y = L^-1 x
+  const int ny = kTied ? 4 * ((int)rank + 1) / nclus - 4 * (int)rank / nclus : 0;
 
   if (tid == 0) {
     mbar_init(&bars->params, 1);
@@ -223,16 +272,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     // is done; add [s_hi | s_lo] (same swizzled layout)
     auto fill_mstage = [&](int u) -> bool {
       if (!mbar_wait_warp(&bars->mxfull, u & 1, abort, lim)) return false;
-      uint32_t w[32];
-      load_row(kMX, w);
+      if constexpr (kTied) {
+        // fp32 X(u) landed as two 32-column boxes in the x_hi and x_mid
+        // blocks; this thread's row is read whole, then its three bf16 planes
+        // overwrite it (rows are thread-private)
+        float f[64];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t hi[4], lo[4];
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) square_split(w[4 * c + i], hi[i], lo[i]);
-        const int off = r * 128 + (int)((c ^ swz) << 4);
-        *reinterpret_cast<uint4*>(sm + kMSH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(sm + kMSL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          for (int c = 0; c < 8; ++c) {
+            const float4 v = *reinterpret_cast<const float4*>(sm + (h ? kMSH : kMX) + r * 128 + ((c ^ swz) << 4));
+            f[32 * h + 4 * c] = v.x;
+            f[32 * h + 4 * c + 1] = v.y;
+            f[32 * h + 4 * c + 2] = v.z;
+            f[32 * h + 4 * c + 3] = v.w;
+          }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {  // features 8c .. 8c + 7
+          uint32_t hi[4], mid[4], lo[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) split3(f[8 * c + 2 * i], f[8 * c + 2 * i + 1], hi[i], mid[i], lo[i]);
+          const int off = r * 128 + (int)((c ^ swz) << 4);
+          *reinterpret_cast<uint4*>(sm + kMX + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(sm + kMSH + off) = make_uint4(mid[0], mid[1], mid[2], mid[3]);
+          *reinterpret_cast<uint4*>(sm + kMSL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+      } else {
+        uint32_t w[32];
+        load_row(kMX, w);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t hi[4], lo[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) square_split(w[4 * c + i], hi[i], lo[i]);
+          const int off = r * 128 + (int)((c ^ swz) << 4);
+          *reinterpret_cast<uint4*>(sm + kMSH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(sm + kMSL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
       }
       fence_proxy_async();
       __syncwarp();
@@ -242,19 +318,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int t = 0; t < T; ++t) {
       if (!mbar_wait_warp(&bars->xfull, t & 1, abort, lim)) { ok = false; break; }
-      uint32_t w[32];
-      load_row(kStaging, w);
-      // the E-step of t-1 read the operand region: wait for its completion
-      if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
-      tmem_fence_after();
-      tmem_st32(tmem + lane_addr + kFCol, w);
+      if constexpr (kTied) {
+        // the E-step of t-1 read the operand region: wait for its completion
+        if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
+        tmem_fence_after();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {  // s_hi / s_lo in 16-column pieces
-        uint32_t hi[16], lo[16];
+        for (int h = 0; h < 2; ++h) {  // fp32 box h: features 32h .. 32h + 31 -> operand words 16h .. 16h + 15
+          uint32_t hi[16], mid[16], lo[16];
+          const char* base = sm + kStaging + h * kBlock + r * 128;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) square_split(w[16 * h + i], hi[i], lo[i]);
-        tmem_st16(tmem + lane_addr + kFCol + 32 + 16 * h, hi);
-        tmem_st16(tmem + lane_addr + kFCol + 64 + 16 * h, lo);
+          for (int c = 0; c < 8; ++c) {
+            const float4 v = *reinterpret_cast<const float4*>(base + ((c ^ swz) << 4));
+            split3(v.x, v.y, hi[2 * c], mid[2 * c], lo[2 * c]);
+            split3(v.z, v.w, hi[2 * c + 1], mid[2 * c + 1], lo[2 * c + 1]);
+          }
+          tmem_st16(tmem + lane_addr + kFCol + 16 * h, hi);
+          tmem_st16(tmem + lane_addr + kFCol + 32 + 16 * h, mid);
+          tmem_st16(tmem + lane_addr + kFCol + 64 + 16 * h, lo);
+        }
+      } else {
+        uint32_t w[32];
+        load_row(kStaging, w);
+        // the E-step of t-1 read the operand region: wait for its completion
+        if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
+        tmem_fence_after();
+        tmem_st32(tmem + lane_addr + kFCol, w);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // s_hi / s_lo in 16-column pieces
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) square_split(w[16 * h + i], hi[i], lo[i]);
+          tmem_st16(tmem + lane_addr + kFCol + 32 + 16 * h, hi);
+          tmem_st16(tmem + lane_addr + kFCol + 64 + 16 * h, lo);
+        }
       }
       tmem_wait_st();
       // the TMA may now refill the staging slot.  Every thread releases it
@@ -276,18 +372,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- producer: weights once, then X tiles (staging slot and M-step stage) ----------------
     if (lane == 0) {
       prefetch_tmap(&tmap);
-      constexpr int kParamBlocks = 2 * kNS;
-      mbar_expect_tx(&bars->params, kParamBlocks * kBlock);
-      const char* src = a.params + (int64_t)rank * kParamBlocks * kBlock;
+      constexpr int kParamBlocks = Y::kWBlocks, kWBytes = Y::kWBytes;
+      mbar_expect_tx(&bars->params, kParamBlocks * kWBytes);
+      const char* src = a.params + (int64_t)rank * kParamBlocks * kWBytes;
       for (int i = 0; i < kParamBlocks; ++i)
-        bulk_load(sm + kParams + i * kBlock, src + (int64_t)i * kBlock, kBlock, &bars->params);
+        bulk_load(sm + kParams + i * kWBytes, src + (int64_t)i * kWBytes, kWBytes, &bars->params);
+      // one X tile: a bf16 box, or two fp32 boxes of 32 columns (tied)
+      constexpr uint32_t kTileBytes = (kTied ? 2 : 1) * kBlock;
+      auto load_tile = [&](int dst0, int dst1, int row, uint64_t* bar) {
+        tma_load_2d(sm + dst0, &tmap, 0, row, bar);
+        if constexpr (kTied) tma_load_2d(sm + dst1, &tmap, 32, row, bar);
+      };
       auto row0 = [&](int t) { return (int)((cid + (int64_t)t * ncl) * kBM); };
       int issued = 0, missued = 0;
       // X(u) into the M-step stage once the M-step of u-1 released it
       auto load_m = [&](int u) -> bool {
         if (u >= 1 && !mbar_wait(&bars->mfree, (u - 1) & 1, abort, lim)) return false;
-        mbar_expect_tx(&bars->mxfull, kBlock);
-        tma_load_2d(sm + kMX, &tmap, 0, row0(u), &bars->mxfull);
+        mbar_expect_tx(&bars->mxfull, kTileBytes);
+        load_tile(kMX, kMSH, row0(u), &bars->mxfull);
         missued = u + 1;
         return true;
       };
@@ -295,8 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < T && ok; ++t) {
         if (t >= 1 && !mbar_wait(&bars->sempty, (t - 1) & 1, abort, lim)) { ok = false; break; }
         if (a.test_stall) break;  // test hook: no X tile ever lands, every wait on it runs out
-        mbar_expect_tx(&bars->xfull, kBlock);
-        tma_load_2d(sm + kStaging, &tmap, 0, row0(t), &bars->xfull);
+        mbar_expect_tx(&bars->xfull, kTileBytes);
+        load_tile(kStaging, kStaging + kBlock, row0(t), &bars->xfull);
         issued = t + 1;
         if (kEm && t >= 1) ok = load_m(t - 1);
       }
@@ -311,7 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWarpMma) {
     // ---------------- MMA issuer (one thread) ----------------
     if (lane == 0) {
-      const uint32_t id_e = idesc_bf16(128, kKC, 0, 0);   // A (TMEM) x W^T (K-major)
+      // A (TMEM) x W^T (K-major); tied: N also covers this rank's y columns
+      const uint32_t id_e = idesc_bf16(128, kKC + 16 * ny, 0, 0);
       const uint32_t id_m = idesc_bf16(128, kFdm, 1, 1);  // R^T x [x | s_hi | s_lo | 1], both MN-major
       const uint32_t base = smem_u32(sm);
       bool ok = mbar_wait(&bars->params, 0, abort, lim);
@@ -320,8 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t wa[kNS], wv[kNS];
 #pragma unroll
       for (int j = 0; j < kNS; ++j) {
-        wa[j] = desc_kmajor(base + kParams + j * kBlock);
-        wv[j] = desc_kmajor(base + kParams + (kNS + j) * kBlock);
+        wa[j] = desc_kmajor(base + kParams + j * Y::kWBytes);
+        wv[j] = kTied ? 0 : desc_kmajor(base + kParams + (kNS + j) * Y::kWBytes);
       }
       // E-step of tile t into S: x.a_j, s_hi.v_j (j < 3), s_lo.v_j (j < 2)
       auto issue_e = [&](int t) -> bool {
@@ -337,14 +440,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_bf16_ts(d, tmem + kFCol + kk * 8, wa[j] + 2 * kk, id_e, acc);
             acc = 1;
           }
+        if constexpr (kTied) {  // x_mid . (w_0 + w_1), x_lo . w_0
 #pragma unroll
-        for (int j = 0; j < kNS; ++j)
+          for (int j = 0; j < 2; ++j)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 32 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+            for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 32 + kk * 8, wa[j] + 2 * kk, id_e, 1u);
 #pragma unroll
-        for (int j = 0; j < 2; ++j)
+          for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wa[0] + 2 * kk, id_e, 1u);
+        } else {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+          for (int j = 0; j < kNS; ++j)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 32 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+        }
         mma_commit(&bars->sfull);
         return true;
       };
@@ -432,11 +544,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
   #pragma unroll
         for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
+        float yv[16];  // tied: this part's piece of y = L^-1 x
+        if (kTied && qc < ny) tmem_ld16(tmem + lane_addr + kSCol + kKC + 16 * qc, yv);
         tmem_wait_ld();
         tmem_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->sfree);
+        float qy = 0.f;  // tied: the piece's share of |y|^2 = x^T P x
+        if (kTied && qc < ny) {
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) qy = fmaf(yv[i], yv[i], qy);
+        }
         // logits (log2 units) min(lz - h S, c2), h = log2(e)/2, and this part's max
+        // (tied: lz - h S, without the row's x^T P x and without the clamp)
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   #pragma unroll
         for (int k4 = 0; k4 < kPart / 4; ++k4) {
@@ -445,7 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int k = 4 * k4 + j;
-            const float l = fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
+            const float l = kTied ? fmaf(-kHalfLog2e, p[k], lz[j]) : fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
             p[k] = l;
             mx[j] = fmaxf(mx[j], l);
           }
@@ -525,6 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->rfull);
         if (valid && rank == 0 && qc == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
+        if (kTied && valid) ll_acc -= 0.5 * (double)qy;  // the row's -x^T P x / 2, piece by piece
         if (*abort) { ok = false; break; }
       }
       // the residual part of the last tile
@@ -555,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int k = 4 * k4 + j;
-            const float l = fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
+            const float l = kTied ? fmaf(-kHalfLog2e, p[k], lz[j]) : fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
             p[k] = l;
             mx[j] = fmaxf(mx[j], l);
           }
@@ -699,7 +820,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
       const uint32_t dm = tmem + lane_addr + kDmCol;
       float v[32];
-      if (qc < 2) {
+      if constexpr (kTied) {
+        // columns [x_hi | x_mid | x_lo | 1]: part qc sums features 16 qc .. 16 qc + 15
+        float v1[16], v2[16];
+        tmem_ld16(dm + 16 * qc, v);
+        tmem_ld16(dm + 64 + 16 * qc, v1);
+        tmem_ld16(dm + 128 + 16 * qc, v2);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) out[1 + 16 * qc + j] = v[j] + (v1[j] + v2[j]);
+        if (qc == 0) {
+          tmem_ld16(dm + 192, v);  // the first column is n_k
+          tmem_wait_ld();
+          out[0] = v[0];
+        }
+      } else if (qc < 2) {
         tmem_ld32(dm + 32 * qc, v);
         tmem_wait_ld();
 #pragma unroll
@@ -716,15 +851,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 16; ++j) out[1 + 64 + f0 + 16 * h + j] = v[j] + w2[j];
         }
       }
-      if (qc == 0) {
+      if (!kTied && qc == 0) {
         tmem_ld32(dm + 192, v);  // 32 columns; the first is n_k
         tmem_wait_ld();
         out[0] = v[0];
       }
     }
     tmem_fence_before();
-    if (kEm && qc == 0) {
-      double* red = reinterpret_cast<double*>(sm + red_off(nclus));
+    if constexpr (kTied) {  // every part of every rank holds log-likelihood terms
+      double* red = reinterpret_cast<double*>(sm + Y::red(nclus));
+      double v = ll_acc;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[warp - kWarpSoftmax0] = v;
+      asm volatile("bar.sync 2, %0;" ::"n"(kSoftWarps * 32) : "memory");
+      if (tid == kWarpSoftmax0 * 32) {
+        double t = 0.0;
+#pragma unroll
+        for (int i = 0; i < kSoftWarps; ++i) t += red[i];
+        a.part_ll[(int64_t)cid * nclus + rank] = t;
+      }
+    } else if (kEm && qc == 0) {
+      double* red = reinterpret_cast<double*>(sm + Y::red(nclus));
       double v = ll_acc;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -741,10 +889,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // no CTA exits while a peer may still write into its shared memory
 }
 
-template <int kMode>
+template <int kMode, bool kTied = false>
 static int launch_mode(const TcLaunch& L, const CUtensorMap& tmap, cudaStream_t st, int* ncl_out) {
-  auto kern = em_tc_diag_kernel<kMode>;
-  const int smem = smem_total(L.cluster_size);
+  auto kern = em_tc_diag_kernel<kMode, kTied>;
+  const int smem = Lay<kTied>::total(L.cluster_size);
   int ncl = 0;
   if (int rc = clustered_launch((const void*)kern, kThreads, smem, L, &ncl)) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -776,7 +924,8 @@ static int launch_mode(const TcLaunch& L, const CUtensorMap& tmap, cudaStream_t 
   args.out_i = L.out_i;
   args.out_vec = ((reinterpret_cast<uintptr_t>(L.out_f) & 15u) == 0 && (L.K & 3) == 0) ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
-  if (e != cudaSuccess) return set_error(GMMXX_ERR_CUDA, "em_tc_diag_kernel launch: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess)
+    return set_error(GMMXX_ERR_CUDA, "em_tc_diag_kernel%s launch: %s", kTied ? " (tied)" : "", cudaGetErrorString(e));
   *ncl_out = ncl;
   return GMMXX_OK;
 }
@@ -804,6 +953,20 @@ int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st) {
   }
   if (rc != GMMXX_OK || L.infer != kModeEm) return rc;
   return launch_tc_reduce(L, ncl, st);
+}
+
+// Tied covariance, fp32 X, D = 64, K <= 512: EM statistics (no inference
+// modes); the log-likelihood partials come one per cluster rank.
+int launch_em_tc_tied(const TcLaunch& L, cudaStream_t st) {
+  if (L.D != 64 || L.cluster_size < 1 || L.cluster_size > kMaxCluster || L.nchunks != L.cluster_size)
+    return set_error(GMMXX_ERR_UNSUPPORTED, "tied tensor-core kernel: D = 64, K <= %d", 128 * kMaxCluster);
+  if (L.infer != kModeEm) return set_error(GMMXX_ERR_UNSUPPORTED, "tied tensor-core kernel: EM statistics only");
+  if (int rc = launch_tc_pack(GMMXX_TIED, 1, L, st)) return rc;
+  CUtensorMap tmap;
+  if (int rc = make_x_tensor_map(L, &tmap, true)) return rc;
+  int ncl = 0;
+  if (int rc = launch_mode<kModeEm, true>(L, tmap, st, &ncl)) return rc;
+  return launch_tc_reduce(L, ncl, st, ncl * L.cluster_size);
 }
 
 }  // namespace tc

@@ -65,9 +65,10 @@ __host__ __device__ inline int stat_width(int cov, int D) {
   }
 }
 
-// Tensor-core path window (em_tc.cu, em_tc_diag.cu): bf16 X, B == 1,
-// N >= 64K, diag D == 64 with K <= 512, spherical D in {64, 128} with
-// K <= 16384 (one pass up to 1024 components, else two passes per group).
+// Tensor-core path window (em_tc.cu, em_tc_diag.cu): B == 1, N >= 64K;
+// bf16 X: diag D == 64 with K <= 512, spherical D in {64, 128} with
+// K <= 16384 (one pass up to 1024 components, else two passes per group);
+// fp32 X: tied D == 64 with K <= 512.
 constexpr int kTcMaxClusters = 160;
 constexpr int kMaxClusterDiag = 4;
 constexpr int kMaxClusterSph = 8;      // spherical one-pass: up to 8 CTAs (1024 components) per cluster
@@ -80,7 +81,12 @@ __host__ __device__ inline bool tc_eligible(int cov, int64_t B, int64_t N, int64
   if (B != 1 || N < 65536) return false;
   if (cov == GMMXX_DIAG) return D == 64 && K <= 128 * kMaxClusterDiag;
   if (cov == GMMXX_SPHERICAL) return (D == 64 || D == 128) && K <= kMaxComponentsSph;
+  if (cov == GMMXX_TIED) return D == 64 && K <= 128 * kMaxClusterDiag;
   return false;
+}
+// the X dtype each covariance type's tensor-core kernel reads
+__host__ __device__ inline bool tc_dtype_ok(int cov, int dt) {
+  return cov == GMMXX_TIED ? dt == GMMXX_FLOAT32 : dt == GMMXX_BFLOAT16;
 }
 // 128-component chunks per group of one tensor-core launch: all of K up to
 // 8 chunks (one pass), else kGroupChunks (spherical large K, two passes)
@@ -92,8 +98,14 @@ __host__ __device__ inline int tc_groups(int64_t K) {
   const int nch = (int)((K + 127) / 128), gc = tc_group_chunks(K);
   return (nch + gc - 1) / gc;
 }
-// three bf16 terms per weight: a_j (and v_j for diag)
-__host__ __device__ inline int tc_param_blocks(int cov, int D) { return (cov == GMMXX_DIAG ? 6 : 3) * (D / 64); }
+// three bf16 terms per weight: a_j (and v_j for diag), 16 KB blocks of
+// [128 components][64 features]; tied: three blocks of [192 rows][64] (the
+// components' weights and up to 64 rows of L^-1)
+constexpr int kTiedTermBytes = 192 * 128;
+__host__ __device__ inline int64_t tc_param_bytes(int cov, int D) {
+  if (cov == GMMXX_TIED) return 3 * kTiedTermBytes;
+  return (int64_t)(cov == GMMXX_DIAG ? 6 : 3) * (D / 64) * 16384;
+}
 
 // Row blocks of the CUDA-core M-step kernel (grid x): about 640 CTAs in total,
 // fixed so that the workspace size and the launch agree (deterministic partials).
@@ -128,6 +140,7 @@ struct Layout {
   int64_t cc;       // CompConst[B][K]
   int64_t wt;       // float[B][FE][Kp]  (feature-major component weights)
   int64_t prec;     // float[B][D][D] (tied) or float[B][K][D][D] (full)
+  int64_t linv;     // float[B][D][D] inverse Cholesky factor L^-1 of the tied covariance
   int64_t lse;      // float[B][max(N, K)] (per-row lse; per-matrix log det while preparing)
   int64_t qrow;     // float[B][N] x^T P x per row (tied)
   int64_t mpart;    // float[B][mstep_blocks][Kp][F]  CUDA-core M-step partials
@@ -159,6 +172,8 @@ inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   L.prec = off;
   if (cov == GMMXX_TIED) off += al(B * D * D * 4);
   else if (cov == GMMXX_FULL) off += al(B * K * D * D * 4);
+  L.linv = off;
+  if (cov == GMMXX_TIED) off += al(B * D * D * 4);
   L.lse = off; off += al(B * (N > K ? N : K) * 4);
   L.qrow = off;
   if (cov == GMMXX_TIED) off += al(B * N * 4);
@@ -174,10 +189,10 @@ inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
     const int C = tc_group_chunks(K);
     L.tc_cluster = C;
     L.tc_chunks = nch;
-    L.tc_params = off; off += al((int64_t)nch * tc_param_blocks(cov, (int)D) * 16384);
+    L.tc_params = off; off += al((int64_t)nch * tc_param_bytes(cov, (int)D));
     L.tc_consts = off; off += al((int64_t)nch * 3 * 128 * 4);
     L.tc_part = off; off += al((int64_t)kTcMaxClusters * C * 128 * stat_width(cov, (int)D) * 4);
-    L.tc_part_ll = off; off += al((int64_t)kTcMaxClusters * 8);
+    L.tc_part_ll = off; off += al((int64_t)kTcMaxClusters * kMaxClusterSph * 8);  // per cluster (and rank)
     if (G > 1) {
       L.tc_rowstat = off; off += al((int64_t)G * N * 8);
       L.tc_lse = off; off += al(N * 4);

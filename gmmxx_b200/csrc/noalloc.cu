@@ -111,6 +111,8 @@ Layout table_layout(int cov, int64_t B, int64_t D, int64_t K) {
   C.prec = off;
   if (cov == GMMXX_TIED) off += al(B * D * D * 4);
   else if (cov == GMMXX_FULL) off += al(B * K * D * D * 4);
+  C.linv = off;
+  if (cov == GMMXX_TIED) off += al(B * D * D * 4);
   C.lse = off; off += al(B * K * 4);
   C.mpart = C.llpart = C.xxpart = off;
   C.tc_cluster = 0;

@@ -100,10 +100,11 @@ __global__ void chol_level_kernel(const float* mats, int D, int* level_out) {
   if (threadIdx.x == 0 && found > 0) atomicMax(level_out, found);
 }
 
-// Factor at the batch-wide level; write precision = (L L^T)^-1 and
-// log det = 2 sum log L_ii.
+// Factor at the batch-wide level; write precision = (L L^T)^-1,
+// log det = 2 sum log L_ii and, when linv_out is given, L^-1 (row-major,
+// zero above the diagonal).
 __global__ void chol_factor_kernel(const float* mats, int D, const int* level_in, float* prec,
-                                   float* logdet, int* status) {
+                                   float* logdet, int* status, float* linv_out) {
   extern __shared__ __align__(16) float sa[];
   const int ld = D + 1;
   float* linv = sa + D * ld;
@@ -125,6 +126,8 @@ __global__ void chol_factor_kernel(const float* mats, int D, const int* level_in
     }
   }
   __syncthreads();
+  if (linv_out != nullptr)
+    for (int e = threadIdx.x; e < D * D; e += blockDim.x) linv_out[m * D * D + e] = linv[(e / D) * ld + e % D];
   float* pm = prec + m * D * D;
   for (int e = threadIdx.x; e < D * D; e += blockDim.x) {
     const int i = e / D, j = e - i * D;
@@ -358,7 +361,8 @@ int launch_prepare(int cov, int64_t B, int64_t D, int64_t K, float* means, float
     const int thr = D <= 32 ? 32 : 128;
     chol_level_kernel<<<(unsigned)nmat, thr, sm1, st>>>(covp, (int)D, status + 1);
     if (int rc = check_launch("chol_level_kernel")) return rc;
-    chol_factor_kernel<<<(unsigned)nmat, thr, sm2, st>>>(covp, (int)D, status + 1, prec, logdet, status);
+    float* linv = (cov == GMMXX_TIED) ? reinterpret_cast<float*>(ws + L.linv) : nullptr;
+    chol_factor_kernel<<<(unsigned)nmat, thr, sm2, st>>>(covp, (int)D, status + 1, prec, logdet, status, linv);
     if (int rc = check_launch("chol_factor_kernel")) return rc;
   }
   dim3 grid((unsigned)ceil_div(L.Kp, 8), (unsigned)B);

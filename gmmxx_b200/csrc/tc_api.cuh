@@ -52,6 +52,7 @@ struct TcLaunch {
   int nchunks;       // 128-component chunks of the weight images (>= cluster_size)
   const float* wt;
   const CompConst* cc;
+  const float* linv;  // tied: L^-1 of the covariance (D x D, row-major)
   char* params;
   float* consts;
   float* part;
@@ -75,9 +76,13 @@ int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st);
 
 // pieces shared by the tensor-core kernels (em_tc.cu, em_tc_diag.cu)
 int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st);
+int launch_em_tc_tied(const TcLaunch& L, cudaStream_t st);
 int launch_tc_pack(int cov, int db, const TcLaunch& L, cudaStream_t st);  // weight images + logit constants
-int make_x_tensor_map(const TcLaunch& L, CUtensorMap* tmap);             // 128 x 64 bf16 boxes, 128 B swizzle
-int launch_tc_reduce(const TcLaunch& L, int ncl, cudaStream_t st);       // fixed-order partials -> stats
+// X boxes of 128 rows x 128 bytes with 128-byte swizzle: 64 bf16 columns, or
+// (fp32) 32 columns -- an fp32 tile of 64 columns is two boxes
+int make_x_tensor_map(const TcLaunch& L, CUtensorMap* tmap, bool fp32 = false);
+// fixed-order partials -> stats; n_ll log-likelihood partials (default: one per cluster)
+int launch_tc_reduce(const TcLaunch& L, int ncl, cudaStream_t st, int n_ll = -1);
 // Sets the kernel's shared-memory attribute and returns in *ncl_out how many
 // clusters of L.cluster_size CTAs (threads x smem each) run at once, capped by
 // the partials buffer and the tile count.

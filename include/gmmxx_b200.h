@@ -93,8 +93,8 @@ GMMXX_API size_t gmmxx_workspace_bytes(int cov_type, int64_t B, int64_t N, int64
 
 /* Which statistics kernels gmmxx_em_accumulate launches for this shape:
  * *path_out = 1 for the tensor-core kernels (tc_pack_kernel, then
- * em_tc_diag_kernel for diag or em_tc_kernel for spherical, then
- * tc_reduce_kernel), 0 for the CUDA-core kernels (rows_kernel, mstep_kernel
+ * em_tc_diag_kernel for diag (bf16 X) and tied (fp32 X) or em_tc_kernel for
+ * spherical (bf16 X), then tc_reduce_kernel), 0 for the CUDA-core kernels (rows_kernel, mstep_kernel
  * and stats_reduce_kernel; em_small_kernel and stats_reduce_kernel when
  * K <= 64).  Honours GMMXX_B200_KERNEL.  A device that cannot
  * co-schedule the kernel's thread-block cluster falls back to the CUDA-core

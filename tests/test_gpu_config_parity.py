@@ -26,7 +26,7 @@ import pytest
 import torch
 
 import oracle
-from test_gpu_parity import _init_cov, _mixture, assert_parity
+from test_gpu_parity import _init_cov, _mixture, assert_bound_parity, assert_parity
 
 pytestmark = pytest.mark.gpu
 
@@ -43,36 +43,42 @@ def _config_case(index, n, seed=77):
     return cfg, x, means, cov, w
 
 
-def _check(got, ref32, ref64, lb_rtol, labels_min=0.999):
+def _check(got, ref32, ref64, lb_rtol, labels_min=0.999, ref32_alt=None):
     labels, means, cov, w, info = got
-    assert_parity(means.cpu().numpy(), ref32[1], ref64[1], name="means")
-    assert_parity(cov.cpu().numpy(), ref32[2], ref64[2], name="covariances")
-    assert_parity(w.cpu().numpy(), ref32[3], ref64[3], name="weights")
-    lb, ref = info["lower_bound"], ref32[4]["lower_bound"]
-    assert abs(lb - ref) <= lb_rtol * abs(ref), (lb, ref)
+    alt = (lambda i: None) if ref32_alt is None else (lambda i: ref32_alt[i])
+    assert_parity(means.cpu().numpy(), ref32[1], ref64[1], name="means", ref32_alt=alt(1))
+    assert_parity(cov.cpu().numpy(), ref32[2], ref64[2], name="covariances", ref32_alt=alt(2))
+    assert_parity(w.cpu().numpy(), ref32[3], ref64[3], name="weights", ref32_alt=alt(3))
+    assert_bound_parity(info["lower_bound"], ref32[4]["lower_bound"], ref64[4]["lower_bound"], lb_rtol,
+                        None if ref32_alt is None else ref32_alt[4]["lower_bound"])
     if labels is not None:
         assert (labels.cpu().numpy() == ref32[0]).mean() >= labels_min
 
 
 @pytest.mark.parametrize("index,n,iters,path", [
     (1, 131_072, 2, "tensor-core"),    # diag bf16, D=64, K=512
-    (2, 200_000, 3, None),             # tied fp32, D=64, K=256
+    (2, 200_000, 3, "tensor-core"),    # tied fp32, D=64, K=256
     (3, 4_096, 3, "cuda-core"),        # full fp32, B=64, D=16, K=32
     (4, 65_536, 2, "tensor-core"),     # spherical bf16, D=128, K=8192, Zipf(1.1)
 ])
 def test_config_shape_matches_oracle(cuda_device, index, n, iters, path):
+    """Config 3's Wishart(D + 2, I) components overlap heavily, so its EM
+    amplifies rounding; a second fp32 oracle run with another row chunking
+    measures how far the reference's own fp32 answer moves with summation
+    order."""
     from gmmxx_b200 import engine
 
     cfg, x, m, c, w = _config_case(index, n)
     xf = x.float().numpy()
     ref32 = oracle.fit(cfg.cov_type, xf, cfg.K, iters, 0.0, m, c, w)
     ref64 = oracle.fit(cfg.cov_type, xf, cfg.K, iters, 0.0, m, c, w, dtype=np.float64)
+    alt = oracle.fit(cfg.cov_type, xf, cfg.K, iters, 0.0, m, c, w, chunk_size_N=1000) if index == 3 else None
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
     got = engine.em_fit(cfg.cov_type, x.to(cuda_device), cfg.K, max_iters=iters, tol=0.0, init_means=t(m),
                         init_variances=t(c), init_weights=t(w))
     if path is not None:
         assert got[4]["kernel_path"] == path
-    _check(got, ref32, ref64, 1e-4 if cfg.dtype == torch.float32 else 1e-3)
+    _check(got, ref32, ref64, 1e-4 if cfg.dtype == torch.float32 else 1e-3, ref32_alt=alt)
     if index == 4:  # the case exercises components that end up (nearly) empty
         assert float(got[3].min()) < 1.0 / n
 

@@ -30,12 +30,25 @@ from test_gpu_parity import PARAM_TOL, _init_cov, _mixture, assert_parity
 pytestmark = pytest.mark.gpu
 
 
+def _separated(seed, n, d, k):
+    """Rows of k well-separated spherical clusters and initial means near the
+    true ones, so that the fits compared below are well conditioned (a
+    random-row initialisation can put two components on one cluster, whose
+    split then amplifies summation-order rounding)."""
+    rng = np.random.default_rng(seed)
+    mu = rng.uniform(-8, 8, (k, d))
+    z = rng.integers(0, k, n)
+    x = (mu[z] + rng.uniform(0.5, 1.2, k)[z, None] * rng.standard_normal((n, d))).astype(np.float32)[None]
+    init = (mu + 0.3 * rng.standard_normal(mu.shape)).astype(np.float32)[None]
+    return x, init
+
+
 @pytest.mark.parametrize("pinned", [True, False])
 @pytest.mark.parametrize("cov", ["spherical", "tied"])
 def test_streamed_passes_reuse_buffers_safely(cuda_device, pinned, cov):
     from gmmxx_b200 import engine, large_n
 
-    x, init = _mixture(61, 1, 16_000, 32, 48)
+    x, init = _separated(61, 16_000, 32, 48)
     icov = _init_cov(cov, x, 48)
     w = np.full((1, 48), 1 / 48, np.float32)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a))

@@ -176,3 +176,65 @@ def test_tc_grouped_repeat_bitwise_identical(cuda_device):
     b = _run("spherical", xb, init, icov, iw, 2, cuda_device, "tc")
     for u, v in zip(a[1:4], b[1:4]):
         assert torch.equal(u, v)
+
+
+def _tied_data(seed, n, d, k, spread=4.0):
+    """fp32 rows of a tied-covariance mixture (config 2's family: shared
+    covariance A A^T / D + 0.1 I, spread-out means, Dirichlet(0.5) weights so
+    that some components are nearly empty)."""
+    rng = np.random.default_rng(seed)
+    a = rng.normal(0, 1, (d, d))
+    cov = a @ a.T / d + 0.1 * np.eye(d)
+    chol = np.linalg.cholesky(cov)
+    mu = rng.normal(0, spread, (k, d))
+    w = rng.dirichlet(np.full(k, 0.5))
+    z = rng.choice(k, n, p=w)
+    x = (mu[z] + rng.standard_normal((n, d)) @ chol.T).astype(np.float32)[None]
+    init = (mu + 0.3 * rng.standard_normal(mu.shape)).astype(np.float32)[None]
+    icov = oracle.global_tied_covariance(x, 1e-6)
+    iw = np.full((1, k), 1.0 / k, np.float32)
+    return torch.from_numpy(x), init, icov, iw
+
+
+@pytest.mark.parametrize("n,k", [
+    (66_000, 40),     # one CTA: all four y pieces on rank 0
+    (150_000, 256),   # config-2 shape: cluster of 2, two pieces each
+    (70_001, 300),    # ragged N, padded components, cluster of 3 (pieces 1, 1, 2)
+    (80_000, 512),    # cluster of 4, one piece each
+])
+def test_tc_tied_matches_oracle(cuda_device, n, k):
+    """Tied covariance on the tensor cores (fp32 X split into three bf16
+    planes): fp32 tolerances -- parameters 1e-4, mean log-likelihood 1e-4."""
+    x, init, icov, iw = _tied_data(23 + k, n, 64, k)
+    iters = 3
+    xf = x.numpy()
+    r32 = oracle.fit("tied", xf, k, iters, 0.0, init, icov, iw)
+    r64 = oracle.fit("tied", xf, k, iters, 0.0, init, icov, iw, dtype=np.float64)
+    labels, means, c, w, info = _run("tied", x, init, icov, iw, iters, cuda_device, "tc")
+    assert info["kernel_path"] == "tensor-core"
+    assert_parity(means.cpu().numpy(), r32[1], r64[1], name="means")
+    assert_parity(c.cpu().numpy(), r32[2], r64[2], name="covariance")
+    assert_parity(w.cpu().numpy(), r32[3], r64[3], name="weights")
+    lb, ref = info["lower_bound"], r32[4]["lower_bound"]
+    assert abs(lb - ref) <= 1e-4 * abs(ref), (lb, ref)
+    assert (labels.cpu().numpy() == r32[0]).mean() >= 0.999
+
+
+def test_tc_tied_statistics_single_step(cuda_device):
+    """One accumulate call: the tensor-core sufficient statistics [n_k, sum r x]
+    and the log-likelihood (whose per-row x^T P x comes from the y columns)
+    equal the CUDA-core kernels' on the same rows."""
+    x, init, icov, iw = _tied_data(29, 131_072, 64, 256)
+    out = _stats_one_step("tied", x, init, icov, iw, 256, cuda_device)
+    st, sr = out["tc"][0], out["simt"][0]
+    scale = np.abs(sr).max(axis=1, keepdims=True) + 1e-6
+    assert np.max(np.abs(st - sr) / scale) < 1e-4
+    assert abs(out["tc"][1] - out["simt"][1]) <= 1e-5 * abs(out["simt"][1])
+
+
+def test_tc_tied_repeat_bitwise_identical(cuda_device):
+    x, init, icov, iw = _tied_data(31, 100_000, 64, 256)
+    a = _run("tied", x, init, icov, iw, 2, cuda_device, "tc")
+    b = _run("tied", x, init, icov, iw, 2, cuda_device, "tc")
+    for u, v in zip(a[1:4], b[1:4]):
+        assert torch.equal(u, v)
