@@ -6,8 +6,10 @@ A step is one full soft-EM iteration (prepare, fused E+M statistics, one
 allreduce when N > 1, finalize) over the configuration's whole synthetic
 dataset, which is resident in HBM and sharded by rows across the ranks
 (strong scaling: the total N is the configuration's N at every GPU count).
-Default workload: configs[1] of BASELINE.json -- diagonal GMM, bf16 X with
-fp32 accumulation, N = 50,000,000, D = 64, K = 512.
+Default workload: configs[4] of BASELINE.json, the largest configuration that
+fits one B200 and the one the north star's 1 -> 8 GPU scaling target names --
+spherical GMM, bf16 X with fp32 accumulation, N = 200,000,000, D = 128,
+K = 8192 (51.2 GB of X).  ``--config 1`` .. ``--config 3`` run the others.
 
 ``value``  samples/s per EM iteration, device-timed (CUDA events on the compute
            stream, barrier + synchronize on both sides, max over ranks).
@@ -296,7 +298,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--config", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=0, help="override total N (smaller runs)")
     ap.add_argument("--ref-rows", type=int, default=0,
