@@ -84,6 +84,11 @@ _SIGNATURES = {
     "gmmxx_resp": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "gmmxx_predict_proba": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
     "gmmxx_logsumexp_noalloc": (_I32, [_I32, _I32, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P]),
+    "gmmxx_kmeans_pp_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "gmmxx_kmeans_pp": (_I32, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _SZ, _P]),
+    "gmmxx_label_stats_width": (_I64, [_I32, _I64]),
+    "gmmxx_label_stats_workspace_bytes": (_SZ, [_I32, _I64, _I64, _I64, _I64]),
+    "gmmxx_label_stats": (_I32, [_I32, _P, _I64, _I64, _I64, _I64, _P, _P, _I32, _P, _P, _SZ, _P]),
 }
 
 
@@ -165,3 +170,15 @@ def workspace_bytes(cov: int, b: int, n: int, d: int, k: int) -> int:
 
 def topk_scratch_bytes(b: int, n: int, top_k: int) -> int:
     return int(load().gmmxx_topk_scratch_bytes(b, n, top_k))
+
+
+def kmeans_pp_workspace_bytes(b: int, s: int, trials: int) -> int:
+    return int(load().gmmxx_kmeans_pp_workspace_bytes(b, s, trials))
+
+
+def label_stats_width(mode: int, d: int) -> int:
+    return int(load().gmmxx_label_stats_width(mode, d))
+
+
+def label_stats_workspace_bytes(mode: int, b: int, n: int, d: int, k: int) -> int:
+    return int(load().gmmxx_label_stats_workspace_bytes(mode, b, n, d, k))

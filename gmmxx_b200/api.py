@@ -49,13 +49,14 @@ def _validate(x, n_components, max_iters, chunk_size_N, chunk_size_K, min_weight
 
 
 def _fit(cov_type, x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
-         init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k):
+         init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k,
+         kmeans=(10, 1e-4)):
     _validate(x, n_components, max_iters, chunk_size_N, chunk_size_K, min_weight, approx_top_k)
     return engine.em_fit(
         cov_type, x, n_components, max_iters=max_iters, tol=tol, init_means=init_means,
         init_variances=init_variances, init_weights=init_weights, init_params=init_params,
         reg_covar=reg_covar, min_weight=min_weight, compute_labels=compute_labels, verbose=verbose,
-        approx_top_k=approx_top_k)
+        approx_top_k=approx_top_k, kmeans_init_iters=int(kmeans[0]), kmeans_init_tol=float(kmeans[1]))
 
 
 def batch_gmm_Spherical(
@@ -81,7 +82,8 @@ def batch_gmm_Spherical(
 ):
     """Spherical soft EM (reference: torch_fallback.py:3339-3380, loop 1897-2397)."""
     return _fit("spherical", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
-                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k,
+                (kmeans_init_iters, kmeans_init_tol))
 
 
 def batch_gmm_Diagonal(
@@ -107,7 +109,8 @@ def batch_gmm_Diagonal(
 ):
     """Diagonal soft EM (reference: torch_fallback.py:3383-3424, loop 2401-2728)."""
     return _fit("diag", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
-                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k,
+                (kmeans_init_iters, kmeans_init_tol))
 
 
 def batch_gmm_Full(
@@ -133,7 +136,8 @@ def batch_gmm_Full(
 ):
     """Full-covariance soft EM (reference: torch_fallback.py:3427-3468, loop 2732-3244)."""
     return _fit("full", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
-                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k,
+                (kmeans_init_iters, kmeans_init_tol))
 
 
 def batch_gmm_Tied(
@@ -159,7 +163,8 @@ def batch_gmm_Tied(
 ):
     """Tied-covariance soft EM (reference: torch_fallback.py:3471-3512, loop 2732-3244)."""
     return _fit("tied", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
-                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k,
+                (kmeans_init_iters, kmeans_init_tol))
 
 
 batch_gmm_spherical = batch_gmm_Spherical
@@ -208,7 +213,8 @@ def batch_gmm_Spherical_torch_native(
     _check_switch("gmm_use_triton_estep", gmm_use_triton_estep)
     _check_switch("gmm_use_triton_streaming_update", gmm_use_triton_streaming_update)
     return _fit("spherical", x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
-                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+                init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k,
+                (kmeans_init_iters, kmeans_init_tol))
 
 
 def _matrix_native(cov_type, doc):
@@ -236,7 +242,8 @@ def _matrix_native(cov_type, doc):
     ):
         _check_switch("gmm_use_triton", gmm_use_triton)
         return _fit(cov_type, x, n_components, max_iters, tol, init_means, init_variances, init_weights, verbose,
-                    init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k)
+                    init_params, reg_covar, chunk_size_N, chunk_size_K, min_weight, compute_labels, approx_top_k,
+                (kmeans_init_iters, kmeans_init_tol))
 
     fit.__doc__ = doc
     return fit

@@ -370,10 +370,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float4* cm4 = reinterpret_cast<const float4*>(c_mpm + k0);
     const float4* ch4 = reinterpret_cast<const float4*>(c_h + k0);
     const float4* cc4 = reinterpret_cast<const float4*>(c_c2 + k0);
+    // passes from an external log-sum-exp: this row's value for the next tile
+    // is loaded one tile ahead, so its latency hides behind the current tile
+    constexpr bool kExt = MODE == kModeExtLse || MODE == kModeProba;
+    auto ext_lse = [&](int u) -> float {
+      const int64_t r = (cid + (int64_t)u * ncl) * kBM + row;
+      return (u < T && r < a.N) ? __ldg(a.lse_in + r) : 0.f;
+    };
+    float lse_next = kExt ? ext_lse(0) : 0.f;
     for (int t = 0; t < T; ++t) {
       const int s = t & 1;
       const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
       const bool valid = grow < a.N;
+      const float lse_t = lse_next;
+      if constexpr (kExt) lse_next = ext_lse(t + 1);
       if (!mbar_wait_warp(&bars->sfull[s], (t >> 1) & 1, abort)) { set_abort(bars, a.status); break; }
       tmem_fence_after();
       const uint32_t sc = tmem + lane_addr + (uint32_t)(s * kKC + k0);
@@ -450,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // responsibilities of this half's components from the row's
         // log-sum-exp over all K (log2 units), written as fp32 rows of K
         if (valid) {
-          const float lse = a.lse_in[grow];
+          const float lse = lse_t;
           const int comp0 = chunk * kKC + k0;
           float* orow = a.out_f + grow * (int64_t)a.K + comp0;
           if (a.out_vec && comp0 + kHalf <= a.K) {
@@ -471,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float M = 0.f, S = 1.f, f = 0.f;
       if constexpr (MODE == kModeExtLse) {
         // responsibilities from the row's log-sum-exp over all K (log2 units)
-        const float lse = valid ? a.lse_in[grow] : 0.f;
+        const float lse = lse_t;
 #pragma unroll
         for (int k = 0; k < kHalf; ++k) p[k] = ex2_approx(p[k] - lse);
         f = valid ? 1.f : 0.f;

@@ -144,12 +144,18 @@ def initial_parameters(
     init_weights: Optional[torch.Tensor],
     reg_covar: float,
     init_params: str = "kmeans",
+    kmeans_iters: int = 10,
+    kmeans_tol: float = 1e-4,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, str]:
-    """User init (clamp / renormalise as the reference does) or random init.
+    """User init (clamp / renormalise as the reference does), k-means or
+    random init (torch_fallback.py:1646-1894).
 
-    ``init_params="kmeans"`` needs the external flash_kmeans package in the
-    reference and falls back to random init without it
-    (torch_fallback.py:1571-1582); this engine does the same.
+    ``init_params="kmeans"``: k-means++ seeds, ``kmeans_iters`` Lloyd
+    iterations and the hard-label weights and covariances, all on the device
+    (``gmmxx_b200.kmeans``; the reference's path with its flash-kmeans
+    dependency, torch_fallback.py:1571-1623).  Where the reference's k-means++
+    declines (K > 256 or K > its row sample) both draw random rows instead
+    (_random_init_means, torch_fallback.py:1384-1387).
     """
     b, n, d = x.shape
     dev = x.device
@@ -164,12 +170,22 @@ def initial_parameters(
     else:
         if init_params not in {"kmeans", "random"}:
             raise ValueError("init_params must be 'kmeans' or 'random'")
-        # _random_init_means (torch_fallback.py:1384-1387)
-        idx = torch.randint(0, n, (b, k), device=dev)
-        means = torch.gather(x, 1, idx[..., None].expand(-1, -1, d)).to(torch.float32).contiguous()
-        source = "random"
-        init_cov = None
-        init_weights = None
+        km = None
+        if init_params == "kmeans" and x.is_cuda:  # host rows (CPU test doubles) take the random draw
+            from . import kmeans
+
+            km = kmeans.kmeans_initialize(cov_type, x, k, max_iters=kmeans_iters, tol=kmeans_tol,
+                                          reg_covar=reg_covar)
+        if km is not None:
+            means, init_cov, init_weights = km
+            source = "kmeans"
+        else:
+            # _random_init_means (torch_fallback.py:1384-1387)
+            idx = torch.randint(0, n, (b, k), device=dev)
+            means = torch.gather(x, 1, idx[..., None].expand(-1, -1, d)).to(torch.float32).contiguous()
+            source = "random"
+            init_cov = None
+            init_weights = None
     if init_weights is None:
         weights = torch.full((b, k), 1.0 / float(k), device=dev, dtype=torch.float32)
     else:
@@ -401,6 +417,8 @@ def em_fit(
     verbose: bool = False,
     comm: Optional[Comm] = None,
     approx_top_k: Optional[int] = None,
+    kmeans_init_iters: int = 10,
+    kmeans_init_tol: float = 1e-4,
 ):
     """Soft EM on the CUDA engine.  ``x`` (B, N_local, D) is this rank's row
     shard when ``comm`` is given (the fit is over the union of all shards;
@@ -426,8 +444,16 @@ def em_fit(
             n_total = int(nt.item())
         if n_total == 0:
             raise ValueError("x must contain at least one sample")
-        means, cov, weights, source = initial_parameters(
-            cov_type, x, n_components, init_means, init_variances, init_weights, reg_covar, init_params)
+        if comm is not None and init_means is None:  # one initialisation for every rank: rank 0's, broadcast
+            means, cov, weights, source = initial_parameters(
+                cov_type, x, n_components, None, init_variances, init_weights, reg_covar, init_params,
+                kmeans_init_iters, kmeans_init_tol)
+            for t in (means, cov, weights):
+                comm.broadcast_(t, 0)
+        else:
+            means, cov, weights, source = initial_parameters(
+                cov_type, x, n_components, init_means, init_variances, init_weights, reg_covar, init_params,
+                kmeans_init_iters, kmeans_init_tol)
         top_k = resolve_approx_top_k(approx_top_k, means.shape[1])
         ops = CudaOps(cov_type, x, means.shape[1], top_k)
         n_iter, hist, elapsed = em_loop(ops, cov_type, means, cov, weights, n_total=n_total, max_iters=max_iters,

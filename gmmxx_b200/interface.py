@@ -285,7 +285,8 @@ class GMMXX:
         torch.cuda.manual_seed_all(self.seed)
         kw = dict(max_iters=self.niter, tol=self.tol, init_means=init_means, init_variances=init_covariances,
                   init_weights=init_weights, init_params=self.init_params, reg_covar=self.reg_covar,
-                  compute_labels=self.compute_labels_on_fit, verbose=self.verbose, approx_top_k=self.approx_top_k)
+                  compute_labels=self.compute_labels_on_fit, verbose=self.verbose, approx_top_k=self.approx_top_k,
+                  kmeans_init_iters=self.init_kmeans_iters, kmeans_init_tol=self.init_kmeans_tol)
         if self._is_large_cpu_stream_input(x_b):
             if batch_size is not None and x_b.shape[0] != 1:
                 raise ValueError("large-N CPU streaming supports batch size 1")

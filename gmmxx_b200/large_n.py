@@ -134,6 +134,20 @@ class StreamedOps(engine.CudaOps):
             self.paths.add(nat.last_accumulate_path())
 
 
+def select_init_sample(x_host: torch.Tensor, n_components: int, max_init_samples: int, device: torch.device):
+    """The reference's initialisation sample of host rows (large_n.py:630-645):
+    ``min(N, max(K, min(max_init_samples, max(4096, 64 K, K))))`` rows drawn with
+    ``torch.randint`` (all rows when that is N), moved to ``device``.  Returns
+    (sample (1, S, D), whether it is a strict subset)."""
+    n = x_host.shape[1]
+    target = max(4096, n_components * 64, n_components)
+    sample_n = min(n, max(n_components, min(max_init_samples, target)))
+    if sample_n == n:
+        return x_host.to(device), False
+    idx = torch.randint(0, n, (sample_n,), device=x_host.device)
+    return x_host.index_select(1, idx).to(device), True
+
+
 def _device_ctx(device: torch.device):
     return torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext()
 
@@ -168,15 +182,25 @@ def em_fit_streamed(
     streamer: Optional[ChunkStreamer] = None,
     approx_top_k: Optional[int] = None,
     comm: Optional[engine.Comm] = None,
+    kmeans_init_iters: int = 10,
+    kmeans_init_tol: float = 1e-4,
+    max_init_samples: int = 65536,
 ):
     """Soft EM over host-resident X (B == 1), streamed chunk by chunk;
     ``approx_top_k`` as in engine.em_fit (the reference's large-N driver takes
     the same option, large_n.py:887-1005).
 
+    Without ``init_means`` the initial parameters come from a random row sample
+    moved to the device, as the reference's large-N driver draws them
+    (large_n.py:630-725): ``sample_n = min(N, max(K, min(max_init_samples,
+    max(4096, 64 K, K))))`` rows chosen with ``torch.randint``, then k-means or
+    random initialisation on the sample (``init_source`` gets "_sampled" when
+    the sample is a strict subset).
+
     With ``comm``, ``x_host`` is this rank's row shard: the fit is over the
     union of the shards (statistics allreduced once per iteration, the
-    finalize replicated), the initial means / covariances that are not given
-    are drawn on rank 0 and broadcast, and the returned labels are the
+    finalize replicated), initial parameters that are not given are drawn
+    from rank 0's shard and broadcast, and the returned labels are the
     shard's."""
     engine.cov_code(cov_type)
     device = torch.device(device)
@@ -195,26 +219,31 @@ def em_fit_streamed(
         if n_total == 0:
             raise ValueError("x must contain at least one sample")
         st = streamer or ChunkStreamer(x_host, chunk_rows, device)
+        shape = lambda k: {"spherical": (1, k), "diag": (1, k, d), "tied": (1, d, d), "full": (1, k, d, d)}[cov_type]
+        source = "user"
         if init_means is None:
             if init_params not in {"kmeans", "random"}:
                 raise ValueError("init_params must be 'kmeans' or 'random'")
-
-            def draw():  # _random_init_means (torch_fallback.py:1384-1387) over this shard's rows
-                idx = torch.randint(0, n, (1, n_components))
-                return torch.gather(st.x, 1, idx[..., None].expand(-1, -1, d)).float()
-
-            init_means = _from_rank0(comm, draw, (1, n_components, d), torch.float32, device)
+            sample, sampled = select_init_sample(st.x, n_components, max_init_samples, device)
+            k = int(n_components)
+            m0, c0, w0, source = engine.initial_parameters(
+                cov_type, sample, k, None, init_variances, init_weights, reg_covar, init_params, kmeans_init_iters,
+                kmeans_init_tol)
+            source = source + ("_sampled" if sampled else "")
+            init_means = _from_rank0(comm, lambda: m0, (1, k, d), torch.float32, device)
+            init_variances = _from_rank0(comm, lambda: c0, shape(k), torch.float32, device)
+            init_weights = _from_rank0(comm, lambda: w0, (1, k), torch.float32, device)
         k = init_means.shape[1]
         if init_variances is None:  # from a row sample of the (rank-0) data
             def gcov():
                 sample = st.x[:, :: max(1, n // (1 << 20))].to(device)
                 return engine.global_covariance(cov_type, sample, k, reg_covar)
 
-            shape = {"spherical": (1, k), "diag": (1, k, d), "tied": (1, d, d), "full": (1, k, d, d)}[cov_type]
-            init_variances = _from_rank0(comm, gcov, shape, torch.float32, device)
+            init_variances = _from_rank0(comm, gcov, shape(k), torch.float32, device)
         probe = st.bufs[0][:, :1]
-        means, cov, weights, source = engine.initial_parameters(
+        means, cov, weights, user = engine.initial_parameters(
             cov_type, probe, n_components, init_means, init_variances, init_weights, reg_covar, init_params)
+        source = source if source != "user" else user
         top_k = engine.resolve_approx_top_k(approx_top_k, k)
         ops = StreamedOps(cov_type, st, k, top_k)
         n_iter, hist, elapsed = engine.em_loop(ops, cov_type, means, cov, weights, n_total=n_total,
@@ -334,7 +363,7 @@ def batch_gmm_largeN_cpu(
     reference's own kernels and initialisation and are validated, not needed;
     initial means are ``n_components`` rows drawn with ``seed`` (the
     reference's fallback when flash_kmeans is absent)."""
-    del kmeans_init_iters, kmeans_init_tol, kmeans_use_triton, gmm_use_triton, max_init_samples, legacy_no_triton
+    del kmeans_use_triton, gmm_use_triton, legacy_no_triton
     device = _validate_large_n_input(x_cpu, device)
     if covariance_type not in _COV_TYPES:
         raise ValueError("covariance_type must be 'spherical', 'diag', 'tied', or 'full'")
@@ -352,7 +381,8 @@ def batch_gmm_largeN_cpu(
     labels, means, cov, weights, info = em_fit_streamed(
         covariance_type, x, int(n_components), device=device, chunk_rows=int(chunk_size_N), max_iters=max_iters,
         tol=tol, init_params=init_params, reg_covar=reg_covar, min_weight=min_weight,
-        compute_labels=compute_labels, verbose=verbose, approx_top_k=approx_top_k)
+        compute_labels=compute_labels, verbose=verbose, approx_top_k=approx_top_k,
+        kmeans_init_iters=kmeans_init_iters, kmeans_init_tol=kmeans_init_tol, max_init_samples=max_init_samples)
     info = dict(info, fallback_reason=None)
     return (None if labels is None else labels.cpu()), means, cov, weights, info
 

@@ -237,6 +237,40 @@ GMMXX_API int gmmxx_logsumexp_noalloc(int cov_type, int x_dtype, const void* x,
                                       const float* means, const float* cov, const float* weights,
                                       float* lse_out, void* stream);
 
+/* ---- k-means initialisation (init_params="kmeans") ---------------------- */
+
+/* Greedy k-means++ centroids of a row sample (torch_fallback.py:1390-1451,
+ * _kmeans_plus_plus_init_means): sample (B, S, D) float32; the first centre
+ * of problem b is row first_idx[b] (int64 device array); centre c >= 1 takes
+ * `trials` candidates, candidate t the first row whose running sum of squared
+ * distances to the closest centre reaches uniforms[c-1][b][t] * total
+ * (uniforms (K-1, B, trials) float32 in [0, 1), row 0 when every distance is
+ * zero), and keeps the candidate of smallest potential
+ * sum_n min(closest_n, |s_n - cand|^2), the first on ties.  centers_out
+ * (B, K, D) float32.  1 <= K <= S, 1 <= trials <= 16; workspace 256-byte
+ * aligned, gmmxx_kmeans_pp_workspace_bytes(B, S, trials) bytes.  Every sum is
+ * a fixed-order reduction (bitwise repeatable).  Replaces the reference's
+ * torch loop (its flash-kmeans seeding step). */
+GMMXX_API size_t gmmxx_kmeans_pp_workspace_bytes(int64_t B, int64_t S, int64_t trials);
+GMMXX_API int gmmxx_kmeans_pp(const float* sample, int64_t B, int64_t S, int64_t D, int64_t K, int64_t trials,
+                              const int64_t* first_idx, const float* uniforms, float* centers_out,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Per-label sums over the rows of x (B, N, D) with labels (B, N) int64 in
+ * [0, K): stats_out (B, K, F) float32 with, by `mode`, 0: [count, sum x]
+ * (F = 1 + D), 1: [count, sum x, sum (x - means[label])^2 per dimension]
+ * (F = 1 + 2D; means (B, K, D) float32), 2: [count, sum x, sum x_i x_j for
+ * i <= j] (F = 1 + D + D(D+1)/2, D <= 26).  K <= 1024.  Fixed-order sums
+ * through `workspace` (gmmxx_label_stats_workspace_bytes bytes).  The
+ * centroid update of Lloyd's k-means (the reference's flash-kmeans step,
+ * torch_fallback.py:1585-1623) and the sums of its hard-label initial
+ * parameters (torch_fallback.py:1454-1569). */
+GMMXX_API int64_t gmmxx_label_stats_width(int mode, int64_t D);
+GMMXX_API size_t gmmxx_label_stats_workspace_bytes(int mode, int64_t B, int64_t N, int64_t D, int64_t K);
+GMMXX_API int gmmxx_label_stats(int x_dtype, const void* x, int64_t B, int64_t N, int64_t D, int64_t K,
+                                const int64_t* labels, const float* means, int mode, float* stats_out,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

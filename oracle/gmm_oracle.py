@@ -43,6 +43,11 @@ __all__ = [
     "global_diag_variance",
     "global_tied_covariance",
     "global_full_covariance",
+    "kmeans_pp_sample_size",
+    "kmeans_plus_plus",
+    "nearest_centroid",
+    "lloyd",
+    "hard_label_init",
 ]
 
 LOG_2PI = math.log(2.0 * math.pi)
@@ -558,3 +563,129 @@ def predict_proba(cov_type, x, means, cov, weights, *, chunk_size_N=32768, chunk
             k1 = min(k0 + chunk_size_K, k)
             out[:, n0:n1, k0:k1] = np.exp(model.logits(xc, xs, k0, k1) - lse[:, :, None])
     return out
+
+
+# ---------------------------------------------------------------------------
+# k-means initialisation (init_params="kmeans")
+# ---------------------------------------------------------------------------
+
+
+def kmeans_pp_sample_size(n, n_components):
+    """torch_fallback.py:1392-1398: rows of the k-means++ sample, or None
+    where the reference declines (K > 256 or K > sample size)."""
+    target = max(4096, 64 * n_components)
+    sample_n = min(n, 65536, target)
+    if n_components <= 0 or n_components > sample_n or n_components > 256:
+        return None
+    return sample_n
+
+
+def kmeans_plus_plus(sample, n_components, first_idx, uniforms, dtype=np.float32):
+    """torch_fallback.py:1390-1451 (_kmeans_plus_plus_init_means) with its
+    random draws given: ``sample`` (B, S, D) is the row sample, ``first_idx``
+    (B,) the first centres' rows, ``uniforms`` (K-1, B, L) the per-centre
+    draws in [0, 1).  Candidate t of centre c is the first row whose running
+    sum of closest squared distances reaches u * total (clamped to the last
+    row, row 0 when the total is 0); the candidate of least potential (first
+    on ties) is kept.  The running sums are accumulated in float64 and
+    rounded to float32 per row, as torch's CPU cumsum of float32 does (its
+    accumulator type is double); totals and potentials likewise."""
+    s = np.asarray(sample, dtype)
+    b, n, d = s.shape
+    centers = np.empty((b, n_components, d), dtype)
+    for bi in range(b):
+        sf = s[bi]
+        centers[bi, 0] = sf[first_idx[bi]]
+        closest = np.square(sf - sf[first_idx[bi]]).sum(axis=-1, dtype=dtype)
+        for c in range(1, n_components):
+            total = np.asarray(closest.sum(dtype=np.float64), dtype)
+            cum = np.cumsum(closest, dtype=np.float64).astype(dtype)
+            cand = np.searchsorted(cum, np.asarray(uniforms[c - 1, bi], dtype) * total, side="left")
+            cand = np.minimum(cand, n - 1)
+            if not total > 0:
+                cand[:] = 0
+            new = np.square(sf[None, :, :] - sf[cand][:, None, :]).sum(axis=-1, dtype=dtype)
+            trial = np.minimum(closest[None], new)
+            best = int(np.argmin(trial.sum(axis=1, dtype=np.float64).astype(dtype)))
+            centers[bi, c] = sf[cand[best]]
+            closest = trial[best]
+    return centers
+
+
+def nearest_centroid(x, means, dtype=np.float32):
+    """Index of each row's nearest centroid in the expanded-distance form of
+    the spherical logits (torch_fallback.py:337-354 with unit variances and
+    equal weights), first on ties."""
+    xf = np.asarray(x, dtype)
+    m = np.asarray(means, dtype)
+    dist = np.square(xf).sum(-1, dtype=dtype)[..., None] - 2.0 * np.einsum("bnd,bkd->bnk", xf, m) + \
+        np.square(m).sum(-1, dtype=dtype)[:, None, :]
+    return np.argmin(np.maximum(dist, 0.0), axis=-1)
+
+
+def lloyd(x, means, max_iters, tol, dtype=np.float32):
+    """Lloyd's k-means (the algorithm of the reference's flash-kmeans step,
+    torch_fallback.py:1585-1623): nearest-centroid labels, every centroid moved
+    to the mean of its rows (an empty one stays), at most ``max_iters`` rounds,
+    stopping once no centroid moves by more than ``tol``; returns (labels of
+    the final centroids, centroids)."""
+    xf = np.asarray(x, dtype)
+    m = np.asarray(means, dtype).copy()
+    b, n, d = xf.shape
+    k = m.shape[1]
+    for _ in range(max(0, int(max_iters))):
+        lab = nearest_centroid(xf, m, dtype)
+        new = m.copy()
+        for bi in range(b):
+            cnt = np.bincount(lab[bi], minlength=k).astype(dtype)
+            sums = np.zeros((k, d), dtype)
+            np.add.at(sums, lab[bi], xf[bi])
+            live = cnt > 0
+            new[bi, live] = sums[live] / cnt[live, None]
+        shift = float(np.sqrt(np.square(new - m).sum(-1)).max())
+        m = new
+        if shift <= tol:
+            break
+    return nearest_centroid(xf, m, dtype), m
+
+
+def hard_label_init(cov_type, x, means, labels, reg_covar, dtype=np.float32):
+    """(weights, covariances) from hard labels: torch_fallback.py:1454-1481
+    (spherical), 1483-1508 (diag), 1511-1543 (full), 1546-1569 (tied)."""
+    xf = np.asarray(x, dtype)
+    m = np.asarray(means, dtype)
+    b, n, d = xf.shape
+    k = m.shape[1]
+    counts = np.zeros((b, k), dtype)
+    for bi in range(b):
+        counts[bi] = np.bincount(labels[bi], minlength=k)
+    safe = np.maximum(counts, 1.0)
+    weights = safe / safe.sum(-1, keepdims=True)
+    diffs = xf - np.take_along_axis(m, labels[..., None], axis=1)
+    eye = np.eye(d, dtype=dtype)
+    if cov_type in ("spherical", "diag"):
+        sq = np.zeros((b, k, d), dtype)
+        for bi in range(b):
+            np.add.at(sq[bi], labels[bi], np.square(diffs[bi]))
+        if cov_type == "spherical":
+            var = sq.sum(-1) / safe / float(d)
+            gv = global_spherical_variance(xf, k, reg_covar, dtype)
+            cov = np.where(counts > 0, var, gv)
+        else:
+            var = sq / safe[..., None]
+            gv = global_diag_variance(xf, k, reg_covar, dtype)
+            cov = np.where(counts[..., None] > 0, var, gv)
+        return weights, np.maximum(cov, reg_covar).astype(dtype)
+    if cov_type == "tied":
+        cov = np.einsum("bnd,bne->bde", diffs, diffs) / float(n) + reg_covar * eye
+        return weights, _sym(cov).astype(dtype)
+    onehot = np.zeros((b, n, k), dtype)
+    for bi in range(b):
+        onehot[bi, np.arange(n), labels[bi]] = 1.0
+    sum_x = np.einsum("bnk,bnd->bkd", onehot, xf)
+    sum_xx = np.einsum("bnk,bnd,bne->bkde", onehot, xf, xf)
+    mc, mr = m[..., :, None], m[..., None, :]
+    scatter = sum_xx - mc * sum_x[..., None, :] - sum_x[..., :, None] * mr + counts[..., None, None] * (mc * mr)
+    cov = scatter / safe[..., None, None] + reg_covar * eye
+    cov = np.where(counts[..., None, None] > 0, cov, global_full_covariance(xf, k, reg_covar, dtype))
+    return weights, _sym(cov).astype(dtype)

@@ -58,9 +58,9 @@ def test_user_matrix_init_is_symmetrised():
 
 
 def test_random_init_draws_rows():
-    """init_params "random" (and "kmeans" without flash_kmeans) draws K rows of
-    x (torch_fallback.py:1384-1387, 1571-1582); covariances are the global
-    ones and the weights uniform."""
+    """init_params "random" draws K rows of x (torch_fallback.py:1384-1387);
+    covariances are the global ones and the weights uniform.  ("kmeans" runs
+    on the device; host rows, as here, take the same random draw.)"""
     x = _data()
     torch.manual_seed(0)
     m, c, w, source = engine.initial_parameters("diag", x, 5, None, None, None, 1e-6, "kmeans")

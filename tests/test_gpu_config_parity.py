@@ -145,20 +145,26 @@ def test_estimator_batched_and_streamed_match_oracle(cuda_device):
 @pytest.mark.parametrize("cov", ["spherical", "diag", "tied", "full"])
 def test_largeN_entry_point_matches_oracle(cuda_device, cov):
     """batch_gmm_largeN_cpu (host rows, chunk_size_N-row chunks) from its
-    documented initialisation -- torch.manual_seed(seed), K rows drawn with
-    torch.randint, the global covariance of the rows, uniform weights -- equals
-    the oracle started from the same parameters."""
+    documented initialisation -- the reference's large-N sample
+    (large_n.py:630-645: torch.manual_seed(seed), then min(N, max(K, min(65536,
+    max(4096, 64 K, K)))) rows drawn with torch.randint), random rows of that
+    sample moved to the device (torch_fallback.py:1384-1387), its global
+    covariance, uniform weights -- equals the oracle started from the same
+    parameters."""
     import gmmxx_b200 as G
 
     d, k, n, seed = (7, 5, 12_000, 11) if cov != "full" else (4, 3, 12_000, 11)
     x, _ = _mixture(51 + d, 1, n, d, k)
     xt = torch.from_numpy(x)
     out = G.batch_gmm_largeN_cpu(xt, k, covariance_type=cov, device=cuda_device, dtype=torch.float32, max_iters=4,
-                                 tol=0.0, chunk_size_N=3000, seed=seed)
+                                 tol=0.0, chunk_size_N=3000, seed=seed, init_params="random")
+    assert out[4]["init_source"] == "random_sampled"
     torch.manual_seed(seed)
-    idx = torch.randint(0, n, (1, k))
-    m0 = x[:, idx[0].numpy()]
-    c0 = _init_cov(cov, x, k)
+    s = min(n, max(k, min(65536, max(4096, 64 * k, k))))
+    sample = x[:, torch.randint(0, n, (s,)).numpy()]
+    ridx = torch.randint(0, s, (1, k), device=cuda_device)
+    m0 = sample[:, ridx[0].cpu().numpy()]
+    c0 = _init_cov(cov, sample, k)
     w0 = np.full((1, k), 1.0 / k, np.float32)
     ref32 = oracle.fit(cov, x, k, 4, 0.0, m0, c0, w0)
     ref64 = oracle.fit(cov, x, k, 4, 0.0, m0, c0, w0, dtype=np.float64)
