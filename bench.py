@@ -475,7 +475,8 @@ def main():
             with open(tpath) as f:
                 tr = json.load(f).get(f"config{cfg.index}")
             if tr and tr.get("path", "tensor-core") == kernel_path:
-                traffic = tr["read_bytes_per_row"] * n_local * cfg.B + tr["write_bytes_per_launch"]
+                traffic = (tr["read_bytes_per_row"] + tr.get("write_bytes_per_row", 0.0)) * n_local * cfg.B + \
+                    tr["write_bytes_per_launch"]
         kernel_names = {"diag": "em_tc_diag_kernel", "spherical": "em_tc_kernel", "tied": "em_tc_diag_kernel<tied>"}
         line = {
             "metric": "EM samples/s per iteration", "value": value, "unit": "samples/s", "n_gpus": world,

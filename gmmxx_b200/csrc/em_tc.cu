@@ -768,6 +768,14 @@ __global__ void tc_ll_sum_kernel(const double* ll_part, int n, double* ll) {
 // host side
 // ---------------------------------------------------------------------------
 
+// GMMXX_B200_SPH_KERNEL=legacy keeps spherical D = 128 EM on em_tc_kernel
+// (the A/B switch of the two tensor-core layouts); anything else uses the
+// diag-kernel layout where it applies.
+bool sph128_enabled() {
+  const char* e = getenv("GMMXX_B200_SPH_KERNEL");
+  return !(e != nullptr && strcmp(e, "legacy") == 0);
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -937,11 +945,7 @@ static int launch_grouped(const TcLaunch& L, cudaStream_t st) {
                                                                  L.rowstat + (int64_t)g * L.N, &ncl, st))
       return rc;
   }
-  const int nb = std::min<int>(kMaxClusters, 148);
-  tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.lse, L.part_ll);
-  if (int rc = check_launch("tc_lse_combine_kernel")) return rc;
-  tc_ll_sum_kernel<<<1, 32, 0, st>>>(L.part_ll, nb, L.ll);
-  if (int rc = check_launch("tc_ll_sum_kernel")) return rc;
+  if (int rc = launch_rowstat_combine(L, groups, st)) return rc;
   for (int g = 0; g < groups; ++g) {
     const int csize = std::min(gc, L.nchunks - g * gc);
     if (int rc = launch_mode<GMMXX_SPHERICAL, DB, kModeExtLse>(L, g * gc, csize, L.lse, nullptr, &ncl, st))
@@ -1009,9 +1013,22 @@ static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
   return GMMXX_OK;
 }
 
+int launch_rowstat_combine(const TcLaunch& L, int groups, cudaStream_t st) {
+  const int nb = std::min<int>(kMaxClusters, 148);
+  tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.lse, L.part_ll);
+  if (int rc = check_launch("tc_lse_combine_kernel")) return rc;
+  tc_ll_sum_kernel<<<1, 32, 0, st>>>(L.part_ll, nb, L.ll);
+  return check_launch("tc_ll_sum_kernel");
+}
+
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st) {
   if (cov == GMMXX_DIAG && L.D == 64 && L.cluster_size <= kMaxClusterDiag) return launch_em_tc_diag(L, st);
   if (cov == GMMXX_TIED) return launch_em_tc_tied(L, st);
+  // spherical D = 128 EM (K <= 512 in one pass, K > 1024 in groups of 512):
+  // the diag kernel's layout; 512 < K <= 1024 and inference take em_tc_kernel
+  if (cov == GMMXX_SPHERICAL && L.D == 128 && L.infer == 0 && sph128_enabled() &&
+      (L.nchunks <= kMaxClusterDiag || L.nchunks > kMaxClusterSph))
+    return launch_em_tc_sph128(L, st);
   if (L.infer != 0) {
     if (cov == GMMXX_SPHERICAL && L.D == 64) return launch_sph_infer<1>(L, st);
     if (cov == GMMXX_SPHERICAL && L.D == 128) return launch_sph_infer<2>(L, st);

@@ -85,43 +85,61 @@ constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (
 constexpr int kMaxCluster = kMaxClusterDiag;
 
 enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpSoftmax0 = 6 };
-// EM statistics, or inference without the M-step (TcLaunch::infer)
-enum Mode { kModeEm = 0, kModeLse = 1, kModeArgmax = 2, kModeProba = 3 };
+// EM statistics, or inference without the M-step (TcLaunch::infer); the
+// spherical large-K passes: each row's (max, scaled sum) over the cluster's
+// components (kModeRowStat), then the M-step with r = 2^(l - lse) from the
+// row's log-sum-exp over all K (kModeExtLse: no exchange)
+enum Mode { kModeEm = 0, kModeLse = 1, kModeArgmax = 2, kModeProba = 3, kModeRowStat = 4, kModeExtLse = 5 };
 constexpr int kThreads = (kWarpSoftmax0 + kSoftWarps) * 32;  // 22 warps, <= 88 registers each
 
 // Shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
-// and tensor memory columns; kTied: the tied-covariance layout.
-template <bool kTied>
+// and tensor memory columns of each covariance type's layout: diag (bf16 X,
+// D = 64), tied (fp32 X, D = 64), spherical (bf16 X, D = 128).
+template <int kCov>
 struct Lay {
+  static constexpr bool kTied = kCov == GMMXX_TIED;
+  static constexpr bool kSph = kCov == GMMXX_SPHERICAL;
   // weights: diag a_0 a_1 a_2 | v_0 v_1 v_2 (16 KB each); tied three terms of
-  // [192 rows][64] (components, then this rank's rows of L^-1)
+  // [192 rows][64] (components, then this rank's rows of L^-1); spherical
+  // three terms of two [128][64] feature halves
   static constexpr int kWBytes = kTied ? kTiedTermBytes : kBlock;
   static constexpr int kWBlocks = kTied ? kNS : 2 * kNS;
   static constexpr int kParams = 0;
-  static constexpr int kStaging = kParams + kWBlocks * kWBytes;  // X staging slot (fp32: two boxes)
-  static constexpr int kMX = kStaging + (kTied ? 2 : 1) * kBlock;  // M-step stage: x | s_hi | s_lo | ones
-                                                                   // (tied: x_hi | x_mid | x_lo | ones;
-                                                                   // predict_proba: the tile's fp32 rows)
+  // X staging slot: one bf16 box (diag), two fp32 boxes (tied), two bf16 boxes (spherical D = 128)
+  static constexpr int kStaging = kParams + kWBlocks * kWBytes;
+  // M-step stage: diag x | s_hi | s_lo | ones; tied x_hi | x_mid | x_lo | ones;
+  // spherical x[0:64] | x[64:128] | aux (column 0 = 1, columns 1-3 = |x|^2 in
+  // three bf16 terms); predict_proba: the tile's fp32 rows
+  static constexpr int kMX = kStaging + (kCov == GMMXX_DIAG ? 1 : 2) * kBlock;
   static constexpr int kMSH = kMX + kBlock;
   static constexpr int kMSL = kMSH + kBlock;
-  static constexpr int kOnes = kMSL + kBlock;           // MN-major, column 0 = 1 (constant)
-  static constexpr int kR = kOnes + kBlock;             // R: two 64-component MN groups
-  static constexpr int kConsts = kR + 2 * kBlock;       // lz[128], c2[128]
-  static constexpr int kHalfX = kConsts + 2 * 128 * 4;  // [2 slots][kSplit parts][128 rows] float2
+  static constexpr int kOnes = kMSL + kBlock;                   // MN-major, column 0 = 1 (constant)
+  static constexpr int kR = kMX + (kSph ? 3 : 4) * kBlock;      // R: two 64-component MN groups
+  static constexpr int kConsts = kR + 2 * kBlock;               // lz[128], c2[128] (spherical: c2, h, mpm)
+  static constexpr int kQ = kConsts + 3 * 128 * 4;              // spherical: |x|^2 [2 tile slots][128 rows]
+  static constexpr int kHalfX = kQ + (kSph ? 2 * 128 * 4 : 0);  // [2 slots][kSplit parts][128 rows] float2
   static constexpr int kXch = kHalfX + 2 * kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
   __host__ __device__ static constexpr int bars(int c) { return kXch + 2 * c * 128 * 8; }
   // the log-likelihood reduction slot: 4 doubles (diag), 16 (tied)
   __host__ __device__ static constexpr int red(int c) { return bars(c) + 192; }
   __host__ __device__ static constexpr int total(int c) { return bars(c) + (kTied ? 320 : 256); }
   // tensor memory: S (+ tied: up to 64 columns of y) | M-step statistics | E-step operand
+  // (diag [x | s_hi | s_lo], tied [x_hi | x_mid | x_lo]: 96 columns; spherical x: 64)
+  static constexpr int kFdmCols = kSph ? 144 : kFdm;  // spherical [x (128) | aux (16)]
   static constexpr uint32_t kSCol = 0;
   static constexpr uint32_t kDmCol = kTied ? 192 : 128;
-  static constexpr uint32_t kFCol = kDmCol + kFdm;
+  static constexpr uint32_t kFCol = kDmCol + kFdmCols;
+  static constexpr uint32_t kFEnd = kFCol + (kSph ? 64 : 96);
 };
-static_assert(Lay<false>::total(kMaxCluster) <= 232448 && Lay<true>::total(kMaxCluster) <= 232448,
+static_assert(Lay<GMMXX_DIAG>::total(kMaxCluster) <= 232448 && Lay<GMMXX_TIED>::total(kMaxCluster) <= 232448 &&
+                  Lay<GMMXX_SPHERICAL>::total(kMaxCluster) <= 232448,
               "shared memory budget");
-static_assert(Lay<false>::kFCol + 96 <= kTmemCols && Lay<true>::kFCol + 96 <= kTmemCols, "tensor memory budget");
-static_assert(Lay<true>::kStaging % 1024 == 0 && Lay<true>::kMX % 1024 == 0 && Lay<true>::kR % 1024 == 0,
+static_assert(Lay<GMMXX_DIAG>::kFEnd <= kTmemCols && Lay<GMMXX_TIED>::kFEnd <= kTmemCols &&
+                  Lay<GMMXX_SPHERICAL>::kFEnd <= kTmemCols,
+              "tensor memory budget");
+static_assert(Lay<GMMXX_TIED>::kStaging % 1024 == 0 && Lay<GMMXX_TIED>::kMX % 1024 == 0 &&
+                  Lay<GMMXX_TIED>::kR % 1024 == 0 && Lay<GMMXX_SPHERICAL>::kMX % 1024 == 0 &&
+                  Lay<GMMXX_SPHERICAL>::kR % 1024 == 0,
               "swizzled blocks need 1024-byte alignment");
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -147,6 +165,7 @@ struct Bars {
   uint64_t mdone;      // MMA: all MMAs complete
   uint64_t pfull;      // predict_proba: the tile's rows staged in shared memory (16 warps)
   uint64_t pfree;      // predict_proba: the staged rows stored to global memory (16 warps)
+  uint64_t qfull[2];   // spherical: |x|^2 of the tile in slot s written (4 prep warps)
   uint32_t tmem_base;
   int abort;
 };
@@ -175,12 +194,17 @@ __device__ __forceinline__ void split3(float x0, float x1, uint32_t& hi, uint32_
   lo = pack_bf16(r0 - bf16lo_to_f32(mid), r1 - bf16hi_to_f32(mid));
 }
 
-template <int kMode, bool kTied>
+template <int kMode, int kCov>
 __global__ void __launch_bounds__(kThreads, 1)
     em_tc_diag_kernel(const __grid_constant__ CUtensorMap tmap, TcArgs a) {
-  constexpr bool kEm = kMode == kModeEm;
-  static_assert(kEm || !kTied, "the tied kernel computes EM statistics only");
-  using Y = Lay<kTied>;
+  constexpr bool kTied = kCov == GMMXX_TIED;
+  constexpr bool kSph = kCov == GMMXX_SPHERICAL;
+  constexpr bool kExt = kMode == kModeExtLse;             // r from the row's external log-sum-exp
+  constexpr bool kEm = kMode == kModeEm || kExt;          // the M-step runs
+  static_assert(kCov == GMMXX_DIAG ? kMode <= kModeProba
+                                   : (kMode == kModeEm || (kSph && (kMode == kModeRowStat || kExt))),
+                "modes of each covariance type");
+  using Y = Lay<kCov>;
   constexpr int kParams = Y::kParams, kStaging = Y::kStaging, kMX = Y::kMX, kMSH = Y::kMSH, kMSL = Y::kMSL;
   constexpr int kOnes = Y::kOnes, kR = Y::kR, kConsts = Y::kConsts, kHalfX = Y::kHalfX, kXch = Y::kXch;
   constexpr uint32_t kSCol = Y::kSCol, kDmCol = Y::kDmCol, kFCol = Y::kFCol;
@@ -192,8 +216,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int nclus = a.cluster_size;
   Bars* bars = reinterpret_cast<Bars*>(sm + Y::bars(nclus));
-  float* c_lz = reinterpret_cast<float*>(sm + kConsts);  // c2 - h mpm: the logit at S = 0
-  float* c_c2 = c_lz + 128;
+  float* c_lz = reinterpret_cast<float*>(sm + kConsts);  // c2 - h mpm: the logit at S = 0 (spherical: c2)
+  float* c_c2 = c_lz + 128;                               // (spherical: h = log2(e) / (2 var))
+  float* c_mpm = c_lz + 256;                              // spherical: |mu|^2
+  float* qbuf = reinterpret_cast<float*>(sm + Y::kQ);     // spherical: |x|^2 per row, two tile slots
   float2* xch = reinterpret_cast<float2*>(sm + kXch);
   volatile int* abort = &bars->abort;
   const uint64_t lim = a.wait_ns;  // every wait below gives up after this long
@@ -226,23 +252,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->mdone, 1);
     mbar_init(&bars->pfull, kSoftWarps);
     mbar_init(&bars->pfree, kSoftWarps);
+    mbar_init(&bars->qfull[0], 4);
+    mbar_init(&bars->qfull[1], 4);
     bars->abort = 0;
     fence_barrier_init();
   }
   if (warp == kWarpMma) tmem_alloc(&bars->tmem_base, kTmemCols);
   // logit = c2 - h max(S + mpm, 0) = min(lz - h S, c2) with lz = c2 - h mpm
-  // (h > 0); a padding component has c2 = -inf, so lz = -inf too
+  // (h > 0); a padding component has c2 = -inf, so lz = -inf too.  Spherical:
+  // c2 - h_k max(S + |x|^2 + mpm_k, 0), per-component h and mpm.
+  // (grouped passes: this CTA's chunk of 128 components is a.chunk0 + rank)
+  const int chunk = a.chunk0 + (int)rank;
   for (int i = tid; i < 128; i += kThreads) {
-    const float* cs = a.consts + (int64_t)rank * 3 * 128;
-    c_lz[i] = fmaf(-kHalfLog2e, cs[i], cs[256 + i]);
-    c_c2[i] = cs[256 + i];
+    const float* cs = a.consts + (int64_t)chunk * 3 * 128;
+    if constexpr (kSph) {
+      c_lz[i] = cs[256 + i];
+      c_c2[i] = cs[128 + i];
+      c_mpm[i] = cs[i];
+    } else {
+      c_lz[i] = fmaf(-kHalfLog2e, cs[i], cs[256 + i]);
+      c_c2[i] = cs[256 + i];
+    }
   }
   // ones group of the M-step operand (n_k): MN-major like X, element (row, 0)
   // = 1 and the rest 0, i.e. 16-byte chunk 0 of every row holds bf16 1.0 in
-  // its first element; the chunk sits at position (row & 7) after the swizzle
+  // its first element; the chunk sits at position (row & 7) after the swizzle.
+  // Spherical: the aux group (kMSL) starts the same; the prep warps then
+  // write |x|^2 into columns 1-3 of each tile's rows.
   for (int i = tid; i < kBlock / 16; i += kThreads) {
-    const int row = i >> 3, chunk = i & 7;
-    reinterpret_cast<uint4*>(sm + kOnes)[i] = make_uint4(chunk == (row & 7) ? 0x3F80u : 0u, 0u, 0u, 0u);
+    const int row = i >> 3, chunk16 = i & 7;
+    reinterpret_cast<uint4*>(sm + (kSph ? kMSL : kOnes))[i] =
+        make_uint4(chunk16 == (row & 7) ? 0x3F80u : 0u, 0u, 0u, 0u);
   }
   fence_proxy_async();
   tmem_fence_before();
@@ -269,10 +309,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     // M-step stage of tile u: X(u) lands there by TMA once the M-step of u-1
-    // is done; add [s_hi | s_lo] (same swizzled layout)
-    auto fill_mstage = [&](int u) -> bool {
+    // is done; add [s_hi | s_lo] (same swizzled layout).  Spherical: the row's
+    // |x|^2 (qu, kept since the tile's E-step operand was written) into the
+    // aux group as three bf16 terms next to the constant 1.
+    auto fill_mstage = [&](int u, float qu) -> bool {
       if (!mbar_wait_warp(&bars->mxfull, u & 1, abort, lim)) return false;
-      if constexpr (kTied) {
+      if constexpr (kSph) {
+        const float q0 = __bfloat162float(__float2bfloat16(qu));
+        const float q1 = __bfloat162float(__float2bfloat16(qu - q0));
+        const uint32_t w0 = pack_bf16(1.f, q0), w1 = pack_bf16(q1, qu - q0 - q1);
+        *reinterpret_cast<uint4*>(sm + kMSL + r * 128 + (int)(swz << 4)) = make_uint4(w0, w1, 0u, 0u);
+      } else if constexpr (kTied) {
         // fp32 X(u) landed as two 32-column boxes in the x_hi and x_mid
         // blocks; this thread's row is read whole, then its three bf16 planes
         // overwrite it (rows are thread-private)
@@ -316,9 +363,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     bool ok = true;
+    float q_cur = 0.f, q_prev = 0.f;  // spherical: |x|^2 of this row in tiles t and t - 1
     for (int t = 0; t < T; ++t) {
       if (!mbar_wait_warp(&bars->xfull, t & 1, abort, lim)) { ok = false; break; }
-      if constexpr (kTied) {
+      if constexpr (kSph) {
+        // the E-step of t-1 read the operand region: wait for its completion
+        if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
+        tmem_fence_after();
+        float q = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // bf16 box h: features 64h .. 64h + 63 -> operand columns 32h .. 32h + 31
+          uint32_t w[32];
+          load_row(kStaging + h * kBlock, w);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
+            q = fmaf(x0, x0, q);
+            q = fmaf(x1, x1, q);
+          }
+          tmem_st32(tmem + lane_addr + kFCol + 32 * h, w);
+        }
+        q_prev = q_cur;
+        q_cur = q;
+        // the softmax reads the slot of tile t before it releases S(t), which
+        // the E-step of t+1 (and so the prep of t+2) waits for
+        qbuf[(t & 1) * 128 + r] = q;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->qfull[t & 1]);
+      } else if constexpr (kTied) {
         // the E-step of t-1 read the operand region: wait for its completion
         if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
         tmem_fence_after();
@@ -363,10 +435,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->ffull);
-      if (kEm && t >= 1 && !fill_mstage(t - 1)) { ok = false; break; }
+      if (kEm && t >= 1 && !fill_mstage(t - 1, q_prev)) { ok = false; break; }
       if (*abort) { ok = false; break; }
     }
-    if (kEm && ok && T >= 1 && !fill_mstage(T - 1)) ok = false;
+    if (kEm && ok && T >= 1 && !fill_mstage(T - 1, q_cur)) ok = false;
     if (!ok) set_abort(bars, a.status);
   } else if (warp == kWarpTma) {
     // ---------------- producer: weights once, then X tiles (staging slot and M-step stage) ----------------
@@ -374,14 +446,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmap);
       constexpr int kParamBlocks = Y::kWBlocks, kWBytes = Y::kWBytes;
       mbar_expect_tx(&bars->params, kParamBlocks * kWBytes);
-      const char* src = a.params + (int64_t)rank * kParamBlocks * kWBytes;
+      const char* src = a.params + (int64_t)chunk * kParamBlocks * kWBytes;
       for (int i = 0; i < kParamBlocks; ++i)
         bulk_load(sm + kParams + i * kWBytes, src + (int64_t)i * kWBytes, kWBytes, &bars->params);
-      // one X tile: a bf16 box, or two fp32 boxes of 32 columns (tied)
-      constexpr uint32_t kTileBytes = (kTied ? 2 : 1) * kBlock;
+      // one X tile: a bf16 box (diag), two fp32 boxes of 32 columns (tied) or
+      // two bf16 boxes of 64 columns (spherical D = 128)
+      constexpr uint32_t kTileBytes = (kCov == GMMXX_DIAG ? 1 : 2) * kBlock;
       auto load_tile = [&](int dst0, int dst1, int row, uint64_t* bar) {
         tma_load_2d(sm + dst0, &tmap, 0, row, bar);
-        if constexpr (kTied) tma_load_2d(sm + dst1, &tmap, 32, row, bar);
+        if constexpr (kCov != GMMXX_DIAG) tma_load_2d(sm + dst1, &tmap, kTied ? 32 : 64, row, bar);
       };
       auto row0 = [&](int t) { return (int)((cid + (int64_t)t * ncl) * kBM); };
       int issued = 0, missued = 0;
@@ -415,16 +488,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // A (TMEM) x W^T (K-major); tied: N also covers this rank's y columns
       const uint32_t id_e = idesc_bf16(128, kKC + 16 * ny, 0, 0);
-      const uint32_t id_m = idesc_bf16(128, kFdm, 1, 1);  // R^T x [x | s_hi | s_lo | 1], both MN-major
+      // R^T x [x | s_hi | s_lo | 1] (spherical [x | x | aux]), both MN-major
+      const uint32_t id_m = idesc_bf16(128, Y::kFdmCols, 1, 1);
       const uint32_t base = smem_u32(sm);
       bool ok = mbar_wait(&bars->params, 0, abort, lim);
       tmem_fence_after();
       // weight descriptors: K-major blocks, +32 B per 16-feature step
+      // (spherical: wa the features 0-63 of term j, wv the features 64-127)
       uint64_t wa[kNS], wv[kNS];
 #pragma unroll
       for (int j = 0; j < kNS; ++j) {
-        wa[j] = desc_kmajor(base + kParams + j * Y::kWBytes);
-        wv[j] = kTied ? 0 : desc_kmajor(base + kParams + (kNS + j) * Y::kWBytes);
+        wa[j] = desc_kmajor(base + kParams + (kSph ? 2 * j : j) * Y::kWBytes);
+        wv[j] = kTied ? 0 : desc_kmajor(base + kParams + (kSph ? 2 * j + 1 : kNS + j) * Y::kWBytes);
       }
       // E-step of tile t into S: x.a_j, s_hi.v_j (j < 3), s_lo.v_j (j < 2)
       auto issue_e = [&](int t) -> bool {
@@ -447,15 +522,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 32 + kk * 8, wa[j] + 2 * kk, id_e, 1u);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wa[0] + 2 * kk, id_e, 1u);
-        } else {
+        } else {  // diag s_hi . v_j, spherical x[64:128] . a_j
 #pragma unroll
           for (int j = 0; j < kNS; ++j)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 32 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+          if constexpr (!kSph) {  // diag s_lo . v_j (j < 2)
 #pragma unroll
-          for (int j = 0; j < 2; ++j)
+            for (int j = 0; j < 2; ++j)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+              for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
+          }
         }
         mma_commit(&bars->sfull);
         return true;
@@ -520,6 +597,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t slot_stride = (uint32_t)(nclus * 128 * 8);
     const float4* cz4 = reinterpret_cast<const float4*>(c_lz + k0);
     const float4* cc4 = reinterpret_cast<const float4*>(c_c2 + k0);
+    const float4* cm4 = reinterpret_cast<const float4*>(c_mpm + k0);  // spherical
+    // this part's logits (log2 units) from S in place, and its four-way max:
+    // diag min(lz - h S, c2) with h = log2(e)/2; tied lz - h S (without the
+    // row's x^T P x, no clamp); spherical c2 - h_k max(S + |x|^2 + mpm_k, 0)
+    auto logits = [&](float qn, float (&mx)[4]) {
+#pragma unroll
+      for (int k4 = 0; k4 < kPart / 4; ++k4) {
+        const float4 vz = cz4[k4], vc = cc4[k4];
+        const float lz[4] = {vz.x, vz.y, vz.z, vz.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
+        float mm[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (kSph) {
+          const float4 vm = cm4[k4];
+          mm[0] = vm.x; mm[1] = vm.y; mm[2] = vm.z; mm[3] = vm.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k = 4 * k4 + j;
+          float l;
+          if constexpr (kSph) l = fmaf(-cc[j], fmaxf(p[k] + (mm[j] + qn), 0.f), lz[j]);
+          else if constexpr (kTied) l = fmaf(-kHalfLog2e, p[k], lz[j]);
+          else l = fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
+          p[k] = l;
+          mx[j] = fmaxf(mx[j], l);
+        }
+      }
+    };
+    // this row's |x|^2 for tile t (spherical; written by the prep warps)
+    auto row_q = [&](int t, float& qn) -> bool {
+      if constexpr (kSph) {
+        if (!mbar_wait_warp(&bars->qfull[t & 1], (t >> 1) & 1, abort, lim)) return false;
+        qn = qbuf[(t & 1) * 128 + row];
+      }
+      return true;
+    };
+    // kModeExtLse: the row's log-sum-exp over all K (log2 units), loaded one
+    // tile ahead so that its latency hides behind the current tile
+    auto ext_lse = [&](int u) -> float {
+      const int64_t r = (cid + (int64_t)u * ncl) * kBM + row;
+      return (u < T && r < a.N) ? __ldg(a.lse_in + r) : 0.f;
+    };
+    float lse_next = kExt ? ext_lse(0) : 0.f;
     // R holds two 64-component MN groups; this part's components are 16-byte
     // chunks rc0 .. rc0 + kPart / 8 - 1 of group k0 / 64
     char* rg = sm + kR + (k0 / 64) * kBlock;
@@ -546,6 +664,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
         float yv[16];  // tied: this part's piece of y = L^-1 x
         if (kTied && qc < ny) tmem_ld16(tmem + lane_addr + kSCol + kKC + 16 * qc, yv);
+        const float lse_t = lse_next;
+        if constexpr (kExt) lse_next = ext_lse(t + 1);
+        float qn = 0.f;
+        if (!row_q(t, qn)) { ok = false; break; }  // read before S(t) is released
         tmem_wait_ld();
         tmem_fence_before();
         __syncwarp();
@@ -555,27 +677,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
           for (int i = 0; i < 16; ++i) qy = fmaf(yv[i], yv[i], qy);
         }
-        // logits (log2 units) min(lz - h S, c2), h = log2(e)/2, and this part's max
-        // (tied: lz - h S, without the row's x^T P x and without the clamp)
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-  #pragma unroll
-        for (int k4 = 0; k4 < kPart / 4; ++k4) {
-          const float4 vz = cz4[k4], vc = cc4[k4];
-          const float lz[4] = {vz.x, vz.y, vz.z, vz.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
-  #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int k = 4 * k4 + j;
-            const float l = kTied ? fmaf(-kHalfLog2e, p[k], lz[j]) : fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
-            p[k] = l;
-            mx[j] = fmaxf(mx[j], l);
-          }
-        }
+        logits(qn, mx);
         // residual part of the previous tile (the M-step's high part of t-1 ran meanwhile)
         if (t >= 1) {
           if (!mbar_wait_warp(&bars->rfree, 0u, abort, lim)) { ok = false; break; }  // M_hi(t-1)
           store_r(lo);
         }
         const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        float f = 0.f, M = 0.f, S = 1.f;
+        if constexpr (kExt) {  // r = 2^(l - lse): no row reduction, no exchange
+  #pragma unroll
+          for (int k = 0; k < kPart; ++k) p[k] = ex2_approx(p[k] - lse_t);
+          f = valid ? 1.f : 0.f;
+        } else {
         const float mref = (m == -INFINITY) ? 0.f : m;  // an all-padding part has p = 0
         float sm4[4] = {0.f, 0.f, 0.f, 0.f};
   #pragma unroll
@@ -617,14 +732,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
         for (int q = 0; q < kMaxCluster; ++q)
           e[q] = q < nclus ? xch[(s * nclus + q) * 128 + row] : make_float2(-INFINITY, 0.f);
-        float M = e[0].x;
+        M = e[0].x;
   #pragma unroll
         for (int q = 1; q < kMaxCluster; ++q) M = fmaxf(M, e[q].x);
-        float S = 0.f;
+        S = 0.f;
   #pragma unroll
         for (int q = 0; q < kMaxCluster; ++q)
           if (q < nclus) S += e[q].y * ex2_approx(e[q].x - M);
-        const float f = valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f;
+        f = valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f;
+        }
         // high part of tile t now (after the M-step's residual part of t-1);
         // the residual words stay in registers for the next iteration
         if (t >= 1 && !mbar_wait_warp(&bars->rfree, 1u, abort, lim)) { ok = false; break; }  // M_lo(t-1)
@@ -644,7 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->rfull);
-        if (valid && rank == 0 && qc == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
+        if (!kExt && valid && rank == 0 && qc == 0) ll_acc += (double)((M + log2f(S)) * kLn2);
         if (kTied && valid) ll_acc -= 0.5 * (double)qy;  // the row's -x^T P x / 2, piece by piece
         if (*abort) { ok = false; break; }
       }
@@ -664,23 +780,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
 #pragma unroll
         for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
+        float qn = 0.f;
+        if (!row_q(t, qn)) { ok = false; break; }  // read before S(t) is released
         tmem_wait_ld();
         tmem_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->sfree);
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int k4 = 0; k4 < kPart / 4; ++k4) {
-          const float4 vz = cz4[k4], vc = cc4[k4];
-          const float lz[4] = {vz.x, vz.y, vz.z, vz.w}, cc[4] = {vc.x, vc.y, vc.z, vc.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int k = 4 * k4 + j;
-            const float l = kTied ? fmaf(-kHalfLog2e, p[k], lz[j]) : fminf(fmaf(-kHalfLog2e, p[k], lz[j]), cc[j]);
-            p[k] = l;
-            mx[j] = fmaxf(mx[j], l);
-          }
-        }
+        logits(qn, mx);
         float2* hxs = halfx + s * kSplit * 128;
         const int comp0 = (int)rank * kKC + k0;  // global index of p[0]
         float m = 0.f, sum = 0.f;
@@ -754,7 +861,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 0; q < kMaxCluster; ++q)
             if (q < nclus) S += e[q].y * ex2_approx(e[q].x - M);
-          if constexpr (kMode == kModeLse) {
+          if constexpr (kMode == kModeRowStat) {
+            // the row's (max, scaled sum) over this group's components (log2 units)
+            if (valid && rank == 0 && qc == 0) a.rowstat[grow] = make_float2(M, S);
+          } else if constexpr (kMode == kModeLse) {
             if (valid && rank == 0 && qc == 0) a.out_f[grow] = (M + log2f(S)) * kLn2;
           } else if (a.out_vec) {
             // responsibilities, fp32 [N][K]: the tile's rows are staged in the
@@ -820,7 +930,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* out = a.part + ((int64_t)cid * a.Kp + comp) * a.F;
       const uint32_t dm = tmem + lane_addr + kDmCol;
       float v[32];
-      if constexpr (kTied) {
+      if constexpr (kSph) {
+        // columns [x (128) | 1 | |x|^2 in three terms]: part qc writes the
+        // sums of r x for features 32 qc .. 32 qc + 31, part 0 also n_k and
+        // sum r |x|^2
+        tmem_ld32(dm + 32 * qc, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) out[1 + 32 * qc + j] = v[j];
+        if (qc == 0) {
+          tmem_ld16(dm + 128, v);
+          tmem_wait_ld();
+          out[0] = v[0];
+          out[1 + 128] = v[1] + (v[2] + v[3]);
+        }
+      } else if constexpr (kTied) {
         // columns [x_hi | x_mid | x_lo | 1]: part qc sums features 16 qc .. 16 qc + 15
         float v1[16], v2[16];
         tmem_ld16(dm + 16 * qc, v);
@@ -851,7 +975,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 16; ++j) out[1 + 64 + f0 + 16 * h + j] = v[j] + w2[j];
         }
       }
-      if (!kTied && qc == 0) {
+      if (kCov == GMMXX_DIAG && qc == 0) {
         tmem_ld32(dm + 192, v);  // 32 columns; the first is n_k
         tmem_wait_ld();
         out[0] = v[0];
@@ -871,7 +995,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kSoftWarps; ++i) t += red[i];
         a.part_ll[(int64_t)cid * nclus + rank] = t;
       }
-    } else if (kEm && qc == 0) {
+    } else if (kMode == kModeEm && qc == 0) {
       double* red = reinterpret_cast<double*>(sm + Y::red(nclus));
       double v = ll_acc;
 #pragma unroll
@@ -889,10 +1013,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // no CTA exits while a peer may still write into its shared memory
 }
 
-template <int kMode, bool kTied = false>
-static int launch_mode(const TcLaunch& L, const CUtensorMap& tmap, cudaStream_t st, int* ncl_out) {
-  auto kern = em_tc_diag_kernel<kMode, kTied>;
-  const int smem = Lay<kTied>::total(L.cluster_size);
+// One clustered launch.  The grouped spherical passes cover chunks
+// [chunk0, chunk0 + csize) of 128 components (csize < 0: the whole of L).
+template <int kMode, int kCov = GMMXX_DIAG>
+static int launch_mode(const TcLaunch& L0, const CUtensorMap& tmap, cudaStream_t st, int* ncl_out, int chunk0 = 0,
+                       int csize = -1, const float* lse_in = nullptr, float2* rowstat = nullptr) {
+  TcLaunch L = L0;
+  if (csize > 0) {
+    L.cluster_size = csize;
+    L.Kp_part = (int64_t)csize * kKC;
+  }
+  auto kern = em_tc_diag_kernel<kMode, kCov>;
+  const int smem = Lay<kCov>::total(L.cluster_size);
   int ncl = 0;
   if (int rc = clustered_launch((const void*)kern, kThreads, smem, L, &ncl)) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -923,9 +1055,12 @@ static int launch_mode(const TcLaunch& L, const CUtensorMap& tmap, cudaStream_t 
   args.out_f = L.out_f;
   args.out_i = L.out_i;
   args.out_vec = ((reinterpret_cast<uintptr_t>(L.out_f) & 15u) == 0 && (L.K & 3) == 0) ? 1 : 0;
+  args.chunk0 = chunk0;
+  args.lse_in = lse_in;
+  args.rowstat = rowstat;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
   if (e != cudaSuccess)
-    return set_error(GMMXX_ERR_CUDA, "em_tc_diag_kernel%s launch: %s", kTied ? " (tied)" : "", cudaGetErrorString(e));
+    return set_error(GMMXX_ERR_CUDA, "em_tc_diag_kernel<%d, %d> launch: %s", kMode, kCov, cudaGetErrorString(e));
   *ncl_out = ncl;
   return GMMXX_OK;
 }
@@ -965,8 +1100,52 @@ int launch_em_tc_tied(const TcLaunch& L, cudaStream_t st) {
   CUtensorMap tmap;
   if (int rc = make_x_tensor_map(L, &tmap, true)) return rc;
   int ncl = 0;
-  if (int rc = launch_mode<kModeEm, true>(L, tmap, st, &ncl)) return rc;
+  if (int rc = launch_mode<kModeEm, GMMXX_TIED>(L, tmap, st, &ncl)) return rc;
   return launch_tc_reduce(L, ncl, st, ncl * L.cluster_size);
+}
+
+// Spherical, bf16 X, D = 128, EM statistics: K <= 512 in one pass over a
+// cluster of ceil(K / 128) CTAs; K > 1024 in groups of 4 chunks (512
+// components) in two passes -- row statistics per group, their combination
+// into each row's log-sum-exp and the log-likelihood, then per group the
+// responsibilities from it and the M-step (no cluster exchange).
+int launch_em_tc_sph128(const TcLaunch& L, cudaStream_t st) {
+  if (L.D != 128 || L.infer != 0) return set_error(GMMXX_ERR_UNSUPPORTED, "spherical kernel: D = 128, EM only");
+  const int nch = L.nchunks;
+  const bool one_pass = nch <= kMaxCluster && L.cluster_size == nch;
+  const bool grouped = nch > kMaxClusterSph && L.cluster_size == kGroupChunks;
+  if (!one_pass && !grouped) return set_error(GMMXX_ERR_UNSUPPORTED, "spherical kernel: %d chunks", nch);
+  if (grouped && (L.rowstat == nullptr || L.lse == nullptr))
+    return set_error(GMMXX_ERR_WORKSPACE, "grouped pass buffers missing");
+  if (int rc = launch_tc_pack(GMMXX_SPHERICAL, 2, L, st)) return rc;
+  CUtensorMap tmap;
+  if (int rc = make_x_tensor_map(L, &tmap)) return rc;
+  int ncl = 0;
+  if (one_pass) {
+    if (int rc = launch_mode<kModeEm, GMMXX_SPHERICAL>(L, tmap, st, &ncl)) return rc;
+    return launch_tc_reduce(L, ncl, st);
+  }
+  const int gc = kGroupChunks, groups = (nch + gc - 1) / gc;
+  for (int g = 0; g < groups; ++g) {
+    const int csize = std::min(gc, nch - g * gc);
+    if (int rc = launch_mode<kModeRowStat, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, nullptr,
+                                                            L.rowstat + (int64_t)g * L.N))
+      return rc;
+  }
+  if (int rc = launch_rowstat_combine(L, groups, st)) return rc;
+  for (int g = 0; g < groups; ++g) {
+    const int csize = std::min(gc, nch - g * gc);
+    if (int rc = launch_mode<kModeExtLse, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, L.lse, nullptr))
+      return rc;
+    TcLaunch Lg = L;  // statistics rows of this group's components
+    const int k0 = g * gc * kKC;
+    Lg.stats = L.stats + (int64_t)k0 * L.F;
+    Lg.K = std::min(gc * kKC, L.K - k0);
+    Lg.Kp_part = (int64_t)csize * kKC;
+    Lg.ll = nullptr;
+    if (int rc = launch_tc_reduce(Lg, ncl, st)) return rc;
+  }
+  return GMMXX_OK;
 }
 
 }  // namespace tc

@@ -238,3 +238,35 @@ def test_tc_tied_repeat_bitwise_identical(cuda_device):
     b = _run("tied", x, init, icov, iw, 2, cuda_device, "tc")
     for u, v in zip(a[1:4], b[1:4]):
         assert torch.equal(u, v)
+
+
+@pytest.mark.parametrize("n,k", [
+    (80_000, 256),    # one pass, cluster of 2
+    (70_001, 512),    # one pass, cluster of 4, ragged N
+    (65_536, 2304),   # grouped: 5 groups of 4 chunks, the last of 2
+])
+def test_tc_sph128_layouts_agree(cuda_device, n, k):
+    """Spherical D = 128 EM runs on the diag kernel's layout (one pass for
+    K <= 512; row statistics, combine and external-log-sum-exp passes for
+    K > 1024); GMMXX_B200_SPH_KERNEL=legacy keeps em_tc_kernel.  One step's
+    statistics and log-likelihood of the two agree, and both fits match the
+    oracle."""
+    xb, init, icov, iw = _data(37 + k, n, 128, k, "spherical", spread=2.0)
+    new = _stats_one_step("spherical", xb, init, icov, iw, k, cuda_device)
+    os.environ["GMMXX_B200_SPH_KERNEL"] = "legacy"
+    try:
+        old = _stats_one_step("spherical", xb, init, icov, iw, k, cuda_device)
+    finally:
+        os.environ.pop("GMMXX_B200_SPH_KERNEL", None)
+    st, so = new["tc"][0], old["tc"][0]
+    scale = np.abs(so).max(axis=1, keepdims=True) + 1e-6
+    assert np.max(np.abs(st - so) / scale) < 1e-4
+    assert abs(new["tc"][1] - old["tc"][1]) <= 1e-5 * abs(old["tc"][1])
+    xf = xb.float().numpy()
+    r32 = oracle.fit("spherical", xf, k, 2, 0.0, init, icov, iw)
+    r64 = oracle.fit("spherical", xf, k, 2, 0.0, init, icov, iw, dtype=np.float64)
+    labels, means, c, w, info = _run("spherical", xb, init, icov, iw, 2, cuda_device, "tc")
+    assert_parity(means.cpu().numpy(), r32[1], r64[1], name="means")
+    assert_parity(c.cpu().numpy(), r32[2], r64[2], name="covariances")
+    assert_parity(w.cpu().numpy(), r32[3], r64[3], name="weights")
+    assert abs(info["lower_bound"] - r32[4]["lower_bound"]) <= 1e-3 * abs(r32[4]["lower_bound"])
