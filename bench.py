@@ -477,7 +477,12 @@ def main():
             if tr and tr.get("path", "tensor-core") == kernel_path:
                 traffic = (tr["read_bytes_per_row"] + tr.get("write_bytes_per_row", 0.0)) * n_local * cfg.B + \
                     tr["write_bytes_per_launch"]
-        kernel_names = {"diag": "em_tc_diag_kernel", "spherical": "em_tc_kernel", "tied": "em_tc_diag_kernel<tied>"}
+        nch = (K + 127) // 128
+        sph_new = D == 128 and (nch <= 4 or nch > 8) and os.environ.get("GMMXX_B200_SPH_KERNEL") != "legacy"
+        kernel_names = {"diag": "em_tc_diag_kernel", "tied": "em_tc_diag_kernel<tied>",
+                        "spherical": ("em_tc_diag_kernel<spherical> (row-statistics + external-lse passes)"
+                                      if sph_new and nch > 8 else "em_tc_diag_kernel<spherical>" if sph_new
+                                      else "em_tc_kernel")}
         line = {
             "metric": "EM samples/s per iteration", "value": value, "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
