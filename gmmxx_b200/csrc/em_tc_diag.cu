@@ -225,9 +225,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint64_t lim = a.wait_ns;  // every wait below gives up after this long
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t rank = cluster_rank();
-  const uint32_t cid = cluster_id_x();
-  const uint32_t ncl = ncluster_x();
+  // hardware cluster, or (kModeExtLse, which exchanges nothing) a virtual one
+  // of a.vcluster consecutive CTAs of a cluster-free launch
+  const int vc = kExt ? a.vcluster : 0;
+  const uint32_t rank = vc > 0 ? blockIdx.x % (uint32_t)vc : cluster_rank();
+  const uint32_t cid = vc > 0 ? blockIdx.x / (uint32_t)vc : cluster_id_x();
+  const uint32_t ncl = vc > 0 ? gridDim.x / (uint32_t)vc : ncluster_x();
   const int64_t ntiles = (a.N + kBM - 1) / kBM;
   const int T = (int)((ntiles > (int64_t)cid) ? (ntiles - 1 - cid) / ncl + 1 : 0);
   // tied: this rank's pieces [p0, p1) of the 4 sixteen-column pieces of y = L^-1 x
@@ -1025,12 +1028,19 @@ static int launch_mode(const TcLaunch& L0, const CUtensorMap& tmap, cudaStream_t
   }
   auto kern = em_tc_diag_kernel<kMode, kCov>;
   const int smem = Lay<kCov>::total(L.cluster_size);
+  // kModeExtLse exchanges nothing within a cluster: it runs as virtual
+  // clusters of single CTAs on every SM instead of the co-resident clusters
+  const bool virt = kMode == kModeExtLse && L.cluster_size > 1;
+  TcLaunch Lq = L;
+  if (virt) Lq.cluster_size = 1;
   int ncl = 0;
-  if (int rc = clustered_launch((const void*)kern, kThreads, smem, L, &ncl)) return rc;
+  if (int rc = clustered_launch((const void*)kern, kThreads, smem, Lq, &ncl)) return rc;
+  if (virt) ncl /= L.cluster_size;  // whole virtual clusters
+  if (ncl < 1) return set_error(GMMXX_ERR_UNSUPPORTED, "too few co-resident CTAs for %d-chunk groups", L.cluster_size);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = L.cluster_size;
+  attr[0].val.clusterDim.x = virt ? 1 : L.cluster_size;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(kThreads);
@@ -1058,6 +1068,7 @@ static int launch_mode(const TcLaunch& L0, const CUtensorMap& tmap, cudaStream_t
   args.chunk0 = chunk0;
   args.lse_in = lse_in;
   args.rowstat = rowstat;
+  args.vcluster = virt ? L.cluster_size : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmap, args);
   if (e != cudaSuccess)
     return set_error(GMMXX_ERR_CUDA, "em_tc_diag_kernel<%d, %d> launch: %s", kMode, kCov, cudaGetErrorString(e));

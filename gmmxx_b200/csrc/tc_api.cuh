@@ -39,6 +39,9 @@ struct TcArgs {
   // natural-log log-sum-exp, 2: out_f[row] = log-sum-exp in log2 units,
   // 3: out_i[row] = label
   int row_out;
+  // > 0: launched without thread-block clusters, CTA i acting as rank
+  // i % vcluster of cluster i / vcluster (passes that exchange nothing)
+  int vcluster;
 };
 
 struct TcLaunch {
