@@ -238,6 +238,9 @@ def run_infer(args, cfg, x, means, cov, weights):
     dev = x.device
     tc_path = nat.accumulate_path(engine.cov_code(cfg.cov_type), nat.BFLOAT16 if x.dtype == torch.bfloat16
                                   else nat.FLOAT32, B, N, D, K) == 1
+    nch = (K + 127) // 128  # spherical D = 128: the diag kernel's layout for K <= 512 and K > 1024
+    sph_new = (cfg.cov_type == "spherical" and D == 128 and (nch <= 4 or nch > 8)
+               and os.environ.get("GMMXX_B200_SPH_KERNEL") != "legacy")
     out = torch.empty((B, N, K), dtype=torch.float32, device=dev) if args.infer == "proba" else None
     call = {"predict": lambda: engine.assign(cfg.cov_type, x, means, cov, weights),
             "score": lambda: engine.score_samples(cfg.cov_type, x, means, cov, weights),
@@ -268,7 +271,7 @@ def run_infer(args, cfg, x, means, cov, weights):
         "value": rows / (ms / 1e3), "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
         "config": workload_config(cfg, args),
-        "kernel": ("em_tc_diag_kernel, inference mode (tensor cores)" if cfg.cov_type == "diag" and tc_path
+        "kernel": ("em_tc_diag_kernel, inference mode (tensor cores)" if (cfg.cov_type == "diag" or sph_new) and tc_path
                    else "em_tc_kernel, per-row inference passes (tensor cores)" if tc_path
                    else "rows_kernel (CUDA cores)"),
         "roofline": {"bound": "hbm" if hbm else "tensor", "achieved": gbs if hbm else tflops,

@@ -1013,6 +1013,17 @@ static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
   return GMMXX_OK;
 }
 
+int launch_infer_combine(const TcLaunch& L, int groups, int infer, cudaStream_t st) {
+  const int nb = std::min<int>(kMaxClusters, 148);
+  if (infer == 2) {
+    tc_argmax_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.out_i);
+    return check_launch("tc_argmax_combine_kernel");
+  }
+  if (infer == 1) tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.out_f, nullptr, kLn2);
+  else tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.lse, nullptr, 1.f);
+  return check_launch("tc_lse_combine_kernel");
+}
+
 int launch_rowstat_combine(const TcLaunch& L, int groups, cudaStream_t st) {
   const int nb = std::min<int>(kMaxClusters, 148);
   tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.lse, L.part_ll);
@@ -1024,9 +1035,9 @@ int launch_rowstat_combine(const TcLaunch& L, int groups, cudaStream_t st) {
 int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st) {
   if (cov == GMMXX_DIAG && L.D == 64 && L.cluster_size <= kMaxClusterDiag) return launch_em_tc_diag(L, st);
   if (cov == GMMXX_TIED) return launch_em_tc_tied(L, st);
-  // spherical D = 128 EM (K <= 512 in one pass, K > 1024 in groups of 512):
-  // the diag kernel's layout; 512 < K <= 1024 and inference take em_tc_kernel
-  if (cov == GMMXX_SPHERICAL && L.D == 128 && L.infer == 0 && sph128_enabled() &&
+  // spherical D = 128 EM and inference (K <= 512 in one pass, K > 1024 in
+  // groups of 512): the diag kernel's layout; 512 < K <= 1024 takes em_tc_kernel
+  if (cov == GMMXX_SPHERICAL && L.D == 128 && sph128_enabled() &&
       (L.nchunks <= kMaxClusterDiag || L.nchunks > kMaxClusterSph))
     return launch_em_tc_sph128(L, st);
   if (L.infer != 0) {

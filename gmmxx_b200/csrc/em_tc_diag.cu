@@ -88,8 +88,12 @@ enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpSoftmax0 = 6 };
 // EM statistics, or inference without the M-step (TcLaunch::infer); the
 // spherical large-K passes: each row's (max, scaled sum) over the cluster's
 // components (kModeRowStat), then the M-step with r = 2^(l - lse) from the
-// row's log-sum-exp over all K (kModeExtLse: no exchange)
-enum Mode { kModeEm = 0, kModeLse = 1, kModeArgmax = 2, kModeProba = 3, kModeRowStat = 4, kModeExtLse = 5 };
+// row's log-sum-exp over all K (kModeExtLse: no exchange); grouped
+// predict_proba: the responsibilities from that log-sum-exp, written as
+// kModeProba writes them (kModeProbaExt: no exchange either)
+enum Mode {
+  kModeEm = 0, kModeLse = 1, kModeArgmax = 2, kModeProba = 3, kModeRowStat = 4, kModeExtLse = 5, kModeProbaExt = 6
+};
 constexpr int kThreads = (kWarpSoftmax0 + kSoftWarps) * 32;  // 22 warps, <= 88 registers each
 
 // Shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
@@ -201,8 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool kSph = kCov == GMMXX_SPHERICAL;
   constexpr bool kExt = kMode == kModeExtLse;             // r from the row's external log-sum-exp
   constexpr bool kEm = kMode == kModeEm || kExt;          // the M-step runs
-  static_assert(kCov == GMMXX_DIAG ? kMode <= kModeProba
-                                   : (kMode == kModeEm || (kSph && (kMode == kModeRowStat || kExt))),
+  constexpr bool kNoXch = kExt || kMode == kModeProbaExt;  // passes that exchange nothing in the cluster
+  static_assert(kCov == GMMXX_DIAG ? kMode <= kModeProba : (kSph || kMode == kModeEm),
                 "modes of each covariance type");
   using Y = Lay<kCov>;
   constexpr int kParams = Y::kParams, kStaging = Y::kStaging, kMX = Y::kMX, kMSH = Y::kMSH, kMSL = Y::kMSL;
@@ -227,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // hardware cluster, or (kModeExtLse, which exchanges nothing) a virtual one
   // of a.vcluster consecutive CTAs of a cluster-free launch
-  const int vc = kExt ? a.vcluster : 0;
+  const int vc = kNoXch ? a.vcluster : 0;
   const uint32_t rank = vc > 0 ? blockIdx.x % (uint32_t)vc : cluster_rank();
   const uint32_t cid = vc > 0 ? blockIdx.x / (uint32_t)vc : cluster_id_x();
   const uint32_t ncl = vc > 0 ? gridDim.x / (uint32_t)vc : ncluster_x();
@@ -640,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t r = (cid + (int64_t)u * ncl) * kBM + row;
       return (u < T && r < a.N) ? __ldg(a.lse_in + r) : 0.f;
     };
-    float lse_next = kExt ? ext_lse(0) : 0.f;
+    float lse_next = kNoXch ? ext_lse(0) : 0.f;
     // R holds two 64-component MN groups; this part's components are 16-byte
     // chunks rc0 .. rc0 + kPart / 8 - 1 of group k0 / 64
     char* rg = sm + kR + (k0 / 64) * kBlock;
@@ -773,6 +777,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         else ok = false;
       }
     } else {
+      // responsibilities p[k] * f of tile t, fp32 [N][K]: the tile's rows are
+      // staged in the (here unused) M-step stage and R buffer, [128 rows][128
+      // components] with the 16-byte chunks of a row permuted by row & 7, then
+      // every warp stores 8 whole rows of this CTA's components as 512-byte
+      // runs (an unaligned output or K % 4 != 0: each thread its own values)
+      auto store_proba = [&](int t, float f) -> bool {
+        const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
+        const int comp0 = chunk * kKC + k0;
+        if (!a.out_vec) {
+          if (grow < a.N) {
+            float* orow = a.out_f + grow * (int64_t)a.K + comp0;
+#pragma unroll
+            for (int k = 0; k < kPart; ++k)
+              if (comp0 + k < a.K) orow[k] = p[k] * f;
+          }
+          return true;
+        }
+        float* stg = reinterpret_cast<float*>(sm + kMX);
+        if (t >= 1 && !mbar_wait_warp(&bars->pfree, (t - 1) & 1, abort, lim)) return false;
+#pragma unroll
+        for (int c = 0; c < kPart / 4; ++c) {
+          const int pos = ((k0 >> 2) + c) ^ (row & 7);
+          *reinterpret_cast<float4*>(stg + row * kKC + pos * 4) =
+              make_float4(p[4 * c] * f, p[4 * c + 1] * f, p[4 * c + 2] * f, p[4 * c + 3] * f);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->pfull);
+        if (!mbar_wait_warp(&bars->pfull, t & 1, abort, lim)) return false;
+        const int sw = warp - kWarpSoftmax0;
+        const int comp = chunk * kKC + 4 * lane;
+#pragma unroll 2
+        for (int i = 0; i < kBM / kSoftWarps; ++i) {
+          const int r = sw * (kBM / kSoftWarps) + i;
+          const int64_t gr = (cid + (int64_t)t * ncl) * kBM + r;
+          const float4 v = *reinterpret_cast<const float4*>(stg + r * kKC + ((lane ^ (r & 7)) * 4));
+          if (gr < a.N) {
+            float* o = a.out_f + gr * (int64_t)a.K + comp;
+            if (comp + 3 < a.K) {
+              *reinterpret_cast<float4*>(o) = v;
+            } else {
+              if (comp < a.K) o[0] = v.x;
+              if (comp + 1 < a.K) o[1] = v.y;
+              if (comp + 2 < a.K) o[2] = v.z;
+            }
+          }
+        }
+        // the staged values went into the stores above: the stage is free
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->pfree);
+        return true;
+      };
       // inference: the logits and the row's cluster-wide reduction only
       for (int t = 0; t < T; ++t) {
         const int s = t & 1;
@@ -783,6 +838,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
 #pragma unroll
         for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
+        const float lse_t = lse_next;
+        if constexpr (kNoXch) lse_next = ext_lse(t + 1);
         float qn = 0.f;
         if (!row_q(t, qn)) { ok = false; break; }  // read before S(t) is released
         tmem_wait_ld();
@@ -792,7 +849,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         logits(qn, mx);
         float2* hxs = halfx + s * kSplit * 128;
-        const int comp0 = (int)rank * kKC + k0;  // global index of p[0]
+        const int comp0 = chunk * kKC + k0;  // global index of p[0]
+        if constexpr (kMode == kModeProbaExt) {
+          // r = 2^(l - lse) from the row's log-sum-exp over all K
+#pragma unroll
+          for (int k = 0; k < kPart; ++k) p[k] = ex2_approx(p[k] - lse_t);
+          if (!store_proba(t, valid ? 1.f : 0.f)) { ok = false; break; }
+          if (*abort) { ok = false; break; }
+          continue;
+        }
         float m = 0.f, sum = 0.f;
         float2 mine;
         if constexpr (kMode == kModeArgmax) {
@@ -855,7 +920,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 1; q < kMaxCluster; ++q)
             if (q < nclus && e[q].x > best.x) best = e[q];
-          if (valid && rank == 0 && qc == 0) a.out_i[grow] = (int64_t)__float_as_int(best.y);
+          if (valid && rank == 0 && qc == 0) {
+            if (a.rowstat != nullptr) a.rowstat[grow] = best;  // grouped: (max, first component) of the group
+            else a.out_i[grow] = (int64_t)__float_as_int(best.y);
+          }
         } else {
           float M = e[0].x;
 #pragma unroll
@@ -869,50 +937,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (valid && rank == 0 && qc == 0) a.rowstat[grow] = make_float2(M, S);
           } else if constexpr (kMode == kModeLse) {
             if (valid && rank == 0 && qc == 0) a.out_f[grow] = (M + log2f(S)) * kLn2;
-          } else if (a.out_vec) {
-            // responsibilities, fp32 [N][K]: the tile's rows are staged in the
-            // (here unused) M-step stage, [128 rows][128 components] with the
-            // 16-byte chunks of a row permuted by row & 7, then every warp
-            // stores 8 whole rows of this CTA's components as 512-byte runs
-            const float f = valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f;
-            float* stg = reinterpret_cast<float*>(sm + kMX);
-            if (t >= 1 && !mbar_wait_warp(&bars->pfree, (t - 1) & 1, abort, lim)) { ok = false; break; }
-#pragma unroll
-            for (int c = 0; c < kPart / 4; ++c) {
-              const int pos = ((k0 >> 2) + c) ^ (row & 7);
-              *reinterpret_cast<float4*>(stg + row * kKC + pos * 4) =
-                  make_float4(p[4 * c] * f, p[4 * c + 1] * f, p[4 * c + 2] * f, p[4 * c + 3] * f);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->pfull);
-            if (!mbar_wait_warp(&bars->pfull, t & 1, abort, lim)) { ok = false; break; }
-            const int sw = warp - kWarpSoftmax0;
-            const int comp = (int)rank * kKC + 4 * lane;
-#pragma unroll 2
-            for (int i = 0; i < kBM / kSoftWarps; ++i) {
-              const int r = sw * (kBM / kSoftWarps) + i;
-              const int64_t gr = (cid + (int64_t)t * ncl) * kBM + r;
-              const float4 v = *reinterpret_cast<const float4*>(stg + r * kKC + ((lane ^ (r & 7)) * 4));
-              if (gr < a.N) {
-                float* o = a.out_f + gr * (int64_t)a.K + comp;
-                if (comp + 3 < a.K) {
-                  *reinterpret_cast<float4*>(o) = v;
-                } else {
-                  if (comp < a.K) o[0] = v.x;
-                  if (comp + 1 < a.K) o[1] = v.y;
-                  if (comp + 2 < a.K) o[2] = v.z;
-                }
-              }
-            }
-            // the staged values went into the stores above: the stage is free
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->pfree);
-          } else if (valid) {  // unaligned output or K % 4 != 0: this thread's components
-            const float f = ex2_approx(m - M) * __frcp_rn(S);
-            float* orow = a.out_f + grow * (int64_t)a.K + comp0;
-#pragma unroll
-            for (int k = 0; k < kPart; ++k)
-              if (comp0 + k < a.K) orow[k] = p[k] * f;
+          } else {
+            if (!store_proba(t, valid ? ex2_approx(m - M) * __frcp_rn(S) : 0.f)) { ok = false; break; }
           }
         }
         if (*abort) { ok = false; break; }
@@ -1028,9 +1054,9 @@ static int launch_mode(const TcLaunch& L0, const CUtensorMap& tmap, cudaStream_t
   }
   auto kern = em_tc_diag_kernel<kMode, kCov>;
   const int smem = Lay<kCov>::total(L.cluster_size);
-  // kModeExtLse exchanges nothing within a cluster: it runs as virtual
+  // kModeExtLse and kModeProbaExt exchange nothing within a cluster: they run as virtual
   // clusters of single CTAs on every SM instead of the co-resident clusters
-  const bool virt = kMode == kModeExtLse && L.cluster_size > 1;
+  const bool virt = (kMode == kModeExtLse || kMode == kModeProbaExt) && L.cluster_size > 1;
   TcLaunch Lq = L;
   if (virt) Lq.cluster_size = 1;
   int ncl = 0;
@@ -1115,22 +1141,61 @@ int launch_em_tc_tied(const TcLaunch& L, cudaStream_t st) {
   return launch_tc_reduce(L, ncl, st, ncl * L.cluster_size);
 }
 
+// Spherical inference, one pass (K <= 512) or grouped: labels from each
+// group's (max, first component), the log-sum-exp from each group's row
+// statistics, the responsibilities of each group from the combined log2
+// log-sum-exp (no cluster exchange).
+static int sph128_infer(const TcLaunch& L, const CUtensorMap& tmap, bool one_pass, cudaStream_t st) {
+  int ncl = 0;
+  if (one_pass) {
+    switch (L.infer) {
+      case kModeLse: return launch_mode<kModeLse, GMMXX_SPHERICAL>(L, tmap, st, &ncl);
+      case kModeArgmax: return launch_mode<kModeArgmax, GMMXX_SPHERICAL>(L, tmap, st, &ncl);
+      default: return launch_mode<kModeProba, GMMXX_SPHERICAL>(L, tmap, st, &ncl);
+    }
+  }
+  const int nch = L.nchunks, gc = kGroupChunks, groups = (nch + gc - 1) / gc;
+  for (int g = 0; g < groups; ++g) {
+    const int csize = std::min(gc, nch - g * gc);
+    float2* rs = L.rowstat + (int64_t)g * L.N;
+    const int rc = L.infer == kModeArgmax
+                       ? launch_mode<kModeArgmax, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, nullptr, rs)
+                       : launch_mode<kModeRowStat, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, nullptr, rs);
+    if (rc) return rc;
+  }
+  if (int rc = launch_infer_combine(L, groups, L.infer, st)) return rc;
+  if (L.infer != kModeProba) return GMMXX_OK;
+  for (int g = 0; g < groups; ++g) {
+    const int csize = std::min(gc, nch - g * gc);
+    if (int rc = launch_mode<kModeProbaExt, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, L.lse, nullptr))
+      return rc;
+  }
+  return GMMXX_OK;
+}
+
 // Spherical, bf16 X, D = 128, EM statistics: K <= 512 in one pass over a
 // cluster of ceil(K / 128) CTAs; K > 1024 in groups of 4 chunks (512
 // components) in two passes -- row statistics per group, their combination
 // into each row's log-sum-exp and the log-likelihood, then per group the
-// responsibilities from it and the M-step (no cluster exchange).
+// responsibilities from it and the M-step (no cluster exchange).  Inference
+// (TcLaunch::infer 1-3) runs on the same layouts.
 int launch_em_tc_sph128(const TcLaunch& L, cudaStream_t st) {
-  if (L.D != 128 || L.infer != 0) return set_error(GMMXX_ERR_UNSUPPORTED, "spherical kernel: D = 128, EM only");
+  if (L.D != 128 || L.infer < 0 || L.infer > 3)
+    return set_error(GMMXX_ERR_UNSUPPORTED, "spherical kernel: D = 128, mode %d", L.infer);
   const int nch = L.nchunks;
   const bool one_pass = nch <= kMaxCluster && L.cluster_size == nch;
   const bool grouped = nch > kMaxClusterSph && L.cluster_size == kGroupChunks;
   if (!one_pass && !grouped) return set_error(GMMXX_ERR_UNSUPPORTED, "spherical kernel: %d chunks", nch);
   if (grouped && (L.rowstat == nullptr || L.lse == nullptr))
     return set_error(GMMXX_ERR_WORKSPACE, "grouped pass buffers missing");
+  if ((L.infer == kModeLse || L.infer == kModeProba) && L.out_f == nullptr)
+    return set_error(GMMXX_ERR_INVALID, "spherical kernel: no output buffer");
+  if (L.infer == kModeArgmax && L.out_i == nullptr)
+    return set_error(GMMXX_ERR_INVALID, "spherical kernel: no label buffer");
   if (int rc = launch_tc_pack(GMMXX_SPHERICAL, 2, L, st)) return rc;
   CUtensorMap tmap;
   if (int rc = make_x_tensor_map(L, &tmap)) return rc;
+  if (L.infer != kModeEm) return sph128_infer(L, tmap, one_pass, st);
   int ncl = 0;
   if (one_pass) {
     if (int rc = launch_mode<kModeEm, GMMXX_SPHERICAL>(L, tmap, st, &ncl)) return rc;

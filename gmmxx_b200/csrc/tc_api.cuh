@@ -80,10 +80,13 @@ int launch_em_tc(int cov, const TcLaunch& L, cudaStream_t st);
 // pieces shared by the tensor-core kernels (em_tc.cu, em_tc_diag.cu)
 int launch_em_tc_diag(const TcLaunch& L, cudaStream_t st);
 int launch_em_tc_tied(const TcLaunch& L, cudaStream_t st);
-int launch_em_tc_sph128(const TcLaunch& L, cudaStream_t st);  // spherical D = 128 EM, diag-kernel layout
+int launch_em_tc_sph128(const TcLaunch& L, cudaStream_t st);  // spherical D = 128 EM and inference, diag-kernel layout
 // grouped large-K passes: each row's log-sum-exp over the groups' row
 // statistics into L.lse (log2 units) and the log-likelihood into *L.ll
 int launch_rowstat_combine(const TcLaunch& L, int groups, cudaStream_t st);
+// grouped inference: fold the groups' row statistics into labels (infer 2),
+// the natural-log log-sum-exp in L.out_f (1) or the log2 one in L.lse (3)
+int launch_infer_combine(const TcLaunch& L, int groups, int infer, cudaStream_t st);
 int launch_tc_pack(int cov, int db, const TcLaunch& L, cudaStream_t st);  // weight images + logit constants
 // X boxes of 128 rows x 128 bytes with 128-byte swizzle: 64 bf16 columns, or
 // (fp32) 32 columns -- an fp32 tile of 64 columns is two boxes

@@ -1,6 +1,7 @@
 """Inference on the tensor-core kernels (bf16 X): the diag kernel (D = 64,
-K <= 512, one pass per call) and the spherical kernel (D = 64 / 128, per-row
-passes per group of 1024 components): labels, score_samples and
+K <= 512, one pass per call; also spherical D = 128 with K <= 512 or in
+groups of 512 components) and em_tc_kernel (spherical D = 64, and D = 128
+with 512 < K <= 1024: per-row passes per group of 1024 components): labels, score_samples and
 predict_proba against the numpy oracle of the reference's chunked torch
 functions (torch_fallback.py:780-821, 824-871, 983-1056, 1133-1237) and
 against the exact-fp32 CUDA-core kernels on the same inputs.
@@ -144,10 +145,11 @@ def test_tc_spherical_inference_matches_cuda_cores(cuda_device):
     np.testing.assert_allclose(pr_tc, pr_s, atol=1e-4)
 
 
-def test_tc_spherical_labels_first_of_equal_components(cuda_device):
+@pytest.mark.parametrize("d", [64, 128])
+def test_tc_spherical_labels_first_of_equal_components(cuda_device, d):
     """Identical components across halves, cluster ranks and groups: the
     first one wins (torch_fallback.py:814-817)."""
-    xb, means, cov, wts = _case(4, 65_536, 64, 2304, "spherical")
+    xb, means, cov, wts = _case(4, 65_536, d, 2304, "spherical")
     counts = np.bincount(oracle.assign("spherical", xb.float().numpy(), means, cov, wts)[0], minlength=2304)
     # the most populated component of a range, duplicated `offset` later
     spans = ((0, 64, 64), (128, 256, 128), (256, 512, 1024), (1024, 1280, 512))
@@ -165,7 +167,37 @@ def test_tc_spherical_labels_first_of_equal_components(cuda_device):
         assert not (lab == b).any()
 
 
-@pytest.mark.parametrize("cov_type,d,k", [("diag", 64, 512), ("spherical", 128, 1100)])
+@pytest.mark.parametrize("n,k", [
+    (80_000, 256),    # one pass, cluster of 2
+    (70_001, 512),    # one pass, cluster of 4, ragged N
+    (66_000, 2304),   # grouped: 5 groups of 4 chunks, the last of 2
+    (65_536, 1030),   # grouped, K % 4 != 0: per-element stores of responsibilities
+])
+def test_tc_sph128_inference_layouts_agree(cuda_device, n, k):
+    """Spherical D = 128 inference on the diag kernel's layout (one pass for
+    K <= 512; per-group row statistics or labels, their combination, and for
+    predict_proba a pass per group from the combined log-sum-exp) agrees with
+    em_tc_kernel (GMMXX_B200_SPH_KERNEL=legacy) and with the oracle."""
+    xb, means, cov, wts = _case(51 + k, n, 128, k, "spherical")
+    path, (lab, lse, proba) = _infer(cuda_device, xb, means, cov, wts, "tc", "spherical")
+    os.environ["GMMXX_B200_SPH_KERNEL"] = "legacy"
+    try:
+        p_old, (lab_o, lse_o, pr_o) = _infer(cuda_device, xb, means, cov, wts, "tc", "spherical")
+    finally:
+        os.environ.pop("GMMXX_B200_SPH_KERNEL", None)
+    assert path == 1 and p_old == 1
+    assert (lab == lab_o).mean() >= 0.9999
+    np.testing.assert_allclose(lse, lse_o, rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(proba, pr_o, atol=1e-5)
+    x = xb.float().numpy()
+    assert (lab == oracle.assign("spherical", x, means, cov, wts)).mean() >= 0.999
+    np.testing.assert_allclose(lse, oracle.score_samples("spherical", x, means, cov, wts), rtol=2e-4, atol=2e-3)
+    np.testing.assert_allclose(proba.sum(-1), 1.0, atol=1e-4)
+    sl = slice(0, 2048)
+    np.testing.assert_allclose(proba[:, sl], oracle.predict_proba("spherical", x[:, sl], means, cov, wts), atol=1e-4)
+
+
+@pytest.mark.parametrize("cov_type,d,k", [("diag", 64, 512), ("spherical", 128, 1100), ("spherical", 128, 256)])
 def test_tc_predict_proba_unaligned_output(cuda_device, cov_type, d, k):
     """predict_proba into a caller buffer that starts 4 bytes off a 16-byte
     boundary: the kernels take their per-element store path (the host checks
