@@ -186,9 +186,12 @@ def test_tc_sph128_inference_layouts_agree(cuda_device, n, k):
     finally:
         os.environ.pop("GMMXX_B200_SPH_KERNEL", None)
     assert path == 1 and p_old == 1
-    assert (lab == lab_o).mean() >= 0.9999
-    np.testing.assert_allclose(lse, lse_o, rtol=1e-5, atol=1e-4)
-    np.testing.assert_allclose(proba, pr_o, atol=1e-5)
+    # the two layouts form |x|^2 differently (fp32 in the prep warps against
+    # three bf16 terms through the tensor cores): agreement to the path's
+    # tolerance against the oracle
+    assert (lab == lab_o).mean() >= 0.999
+    np.testing.assert_allclose(lse, lse_o, rtol=2e-4, atol=2e-3)
+    np.testing.assert_allclose(proba, pr_o, atol=1e-4)
     x = xb.float().numpy()
     assert (lab == oracle.assign("spherical", x, means, cov, wts)).mean() >= 0.999
     np.testing.assert_allclose(lse, oracle.score_samples("spherical", x, means, cov, wts), rtol=2e-4, atol=2e-3)
