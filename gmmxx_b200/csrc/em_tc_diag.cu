@@ -1211,8 +1211,10 @@ int launch_em_tc_sph128(const TcLaunch& L, cudaStream_t st) {
   if (int rc = launch_rowstat_combine(L, groups, st)) return rc;
   for (int g = 0; g < groups; ++g) {
     const int csize = std::min(gc, nch - g * gc);
-    if (int rc = launch_mode<kModeExtLse, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, L.lse, nullptr))
-      return rc;
+    const int rc = sph_ext_enabled()
+                       ? launch_sph_ext(L, tmap, g * gc, csize, st, &ncl)
+                       : launch_mode<kModeExtLse, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, L.lse, nullptr);
+    if (rc) return rc;
     TcLaunch Lg = L;  // statistics rows of this group's components
     const int k0 = g * gc * kKC;
     Lg.stats = L.stats + (int64_t)k0 * L.F;

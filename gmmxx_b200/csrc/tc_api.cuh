@@ -88,6 +88,12 @@ int launch_rowstat_combine(const TcLaunch& L, int groups, cudaStream_t st);
 // the natural-log log-sum-exp in L.out_f (1) or the log2 one in L.lse (3)
 int launch_infer_combine(const TcLaunch& L, int groups, int infer, cudaStream_t st);
 int launch_tc_pack(int cov, int db, const TcLaunch& L, cudaStream_t st);  // weight images + logit constants
+// spherical D = 128, grouped second pass over chunks [chunk0, chunk0 + csize):
+// responsibilities from L.lse and the group's M-step statistics partials
+// (em_tc_sph_ext_kernel, components on the MMA's M dimension); *ncl_out
+// receives the number of virtual clusters (partials rows)
+int launch_sph_ext(const TcLaunch& L, const CUtensorMap& tmap, int chunk0, int csize, cudaStream_t st, int* ncl_out);
+bool sph_ext_enabled();  // GMMXX_B200_SPH_PASS2=diag keeps em_tc_diag_kernel's pass
 // X boxes of 128 rows x 128 bytes with 128-byte swizzle: 64 bf16 columns, or
 // (fp32) 32 columns -- an fp32 tile of 64 columns is two boxes
 int make_x_tensor_map(const TcLaunch& L, CUtensorMap* tmap, bool fp32 = false);

@@ -270,3 +270,32 @@ def test_tc_sph128_layouts_agree(cuda_device, n, k):
     assert_parity(c.cpu().numpy(), r32[2], r64[2], name="covariances")
     assert_parity(w.cpu().numpy(), r32[3], r64[3], name="weights")
     assert abs(info["lower_bound"] - r32[4]["lower_bound"]) <= 1e-3 * abs(r32[4]["lower_bound"])
+
+
+@pytest.mark.parametrize("n,k,zipf", [
+    (65_536, 2304, False),   # 5 groups, the last of 2 chunks
+    (70_001, 8192, True),    # config-4 shape: 16 groups, Zipf weights, ragged N
+])
+def test_tc_sph_pass2_layouts_agree(cuda_device, n, k, zipf):
+    """The grouped spherical second pass on em_tc_sph_ext_kernel (components
+    on the MMA's M dimension, R in tensor memory) against the diag-layout
+    external-log-sum-exp pass (GMMXX_B200_SPH_PASS2=diag): one step's
+    statistics agree, and sum_k n_k = N (each row's responsibilities sum to
+    one over all K groups)."""
+    xb, init, icov, iw = _data(41 + k, n, 128, k, "spherical", spread=2.0)
+    if zipf:
+        w = 1.0 / np.arange(1, k + 1) ** 1.1
+        iw = (w / w.sum()).astype(np.float32)[None]
+    new = _stats_one_step("spherical", xb, init, icov, iw, k, cuda_device)
+    os.environ["GMMXX_B200_SPH_PASS2"] = "diag"
+    try:
+        old = _stats_one_step("spherical", xb, init, icov, iw, k, cuda_device)
+    finally:
+        os.environ.pop("GMMXX_B200_SPH_PASS2", None)
+    st, so = new["tc"][0], old["tc"][0]
+    scale = np.abs(so).max(axis=1, keepdims=True) + 1e-6
+    assert np.max(np.abs(st - so) / scale) < 2e-5
+    assert new["tc"][1] == old["tc"][1]  # the log-likelihood comes from the first pass
+    assert abs(st[0, :, 0].astype(np.float64).sum() - n) <= 1e-4 * n
+    sr = new["simt"][0]
+    assert np.max(np.abs(st - sr) / (np.abs(sr).max(axis=1, keepdims=True) + 1e-6)) < 1e-4
