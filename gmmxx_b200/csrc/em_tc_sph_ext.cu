@@ -24,10 +24,10 @@
 //            64-feature groups); 16 instructions of N = 128 features
 //
 // Tensor memory holds three S^T / R^T buffers of 128 columns and the M-step
-// accumulator (128), so the E-step of tile t+2 is queued right behind the
-// M-step of t and the tensor pipe does not wait for the softmax of the tile
-// in between; four X slots give each TMA load about two tile periods.
-// Shared memory: weights 96 KB + X slots 128 KB + the row tables.
+// accumulator (128), so the E-steps run up to three tiles ahead of the
+// M-steps and the tensor pipe does not wait for the softmax; four X slots
+// give each TMA load about two tile periods.  Shared memory: weights 96 KB
+// + X slots 128 KB + the row tables.
 //
 // The logits repeat the first pass's arithmetic (em_tc_diag.cu, spherical
 // layout): the same E-step instruction order over the weight terms and
@@ -62,9 +62,14 @@ constexpr int kSR = 3;        // S^T / R^T buffers in tensor memory
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kDmCol = kSR * 128;  // M-step accumulator [comp][feature]
 
-enum Warp { kWarpTma = 0, kWarpMma = 1, kWarpPrep0 = 2, kWarpSoft0 = 6 };
+// The E-steps and the M-steps are issued by threads of two warps on
+// different SM sub-partitions (warp % 4): each sub-partition also runs four
+// softmax warps, and one issuing thread there for all MMAs of a tile was
+// measured to hold the tensor pipe at about half its rate while the softmax
+// ran.
+enum Warp { kWarpTma = 0, kWarpMma = 1, kWarpPrep0 = 2, kWarpSoft0 = 6, kWarpMmaM = 22 };
 constexpr int kSoftWarps = 16;
-constexpr int kThreads = (kWarpSoft0 + kSoftWarps) * 32;  // 22 warps
+constexpr int kThreads = (kWarpMmaM + 1) * 32;  // 23 warps
 
 // shared memory (byte offsets from the 1024-aligned dynamic block)
 constexpr int kW = 0;                              // term j, features 64h.. at (2j + h) * kBlock
@@ -85,7 +90,7 @@ struct Bars {
   uint64_t sfull[kSR];        // MMA: S^T(t) complete
   uint64_t rfull[kSR];        // softmax: R^T(t) written (16 warps)
   uint64_t mfree[kSR];        // MMA: the M-step read R^T(t): the buffer is free
-  uint64_t mdone;             // MMA: every MMA complete
+  uint64_t mdone;             // MMA: every MMA complete (both issuing threads)
   uint32_t tmem_base;
   int abort;
 };
@@ -143,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->rfull[i], kSoftWarps);
       mbar_init(&bars->mfree[i], 1);
     }
-    mbar_init(&bars->mdone, 1);
+    mbar_init(&bars->mdone, 2);
     bars->abort = 0;
     fence_barrier_init();
   }
@@ -180,70 +185,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = std::max(0, issued - kXSlots); u < issued; ++u)
         mbar_wait(&bars->xfull[u % kXSlots], (u / kXSlots) & 1, nullptr, lim);
     }
-  } else if (warp == kWarpMma) {
-    // ---------------- MMA issuer (one thread) ----------------
+  } else if (warp == kWarpMma || warp == kWarpMmaM) {
+    // ---------------- MMA issuers: E-steps (warp kWarpMma), M-steps (warp kWarpMmaM) ----------------
     if (lane == 0) {
-      const uint32_t id_e = idesc_bf16(128, 128, 0, 0);  // W (K-major) x X^T (K-major)
-      const uint32_t id_m = idesc_bf16(128, 128, 0, 1);  // R^T (tensor memory) x X (MN-major)
       const uint32_t base = smem_u32(sm);
-      bool ok = mbar_wait(&bars->params, 0, abort, lim);
-      tmem_fence_after();
-      uint64_t wd[kNS][2];
-#pragma unroll
-      for (int j = 0; j < kNS; ++j)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) wd[j][h] = desc_kmajor(base + kW + (2 * j + h) * kBlock);
-      // E-step of tile t into buffer t % 3, in the first pass's order: the
-      // weight terms over features 0-63, then over features 64-127
-      auto issue_e = [&](int t) -> bool {
-        const int s = t % kXSlots, b = t % kSR;
-        if (!mbar_wait(&bars->xfull[s], (t / kXSlots) & 1, abort, lim)) return false;
-        if (t >= kSR && !mbar_wait(&bars->mfree[b], ((t / kSR) - 1) & 1, abort, lim)) return false;
+      bool ok = true;
+      if (warp == kWarpMma) {
+        const uint32_t id_e = idesc_bf16(128, 128, 0, 0);  // W (K-major) x X^T (K-major)
+        ok = mbar_wait(&bars->params, 0, abort, lim);
         tmem_fence_after();
-        const uint32_t d = tmem + (uint32_t)(b * 128);
-        const uint32_t xs = base + kX + s * 2 * kBlock;
-        uint32_t acc = 0;
+        uint64_t wd[kNS][2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint64_t xd = desc_kmajor(xs + h * kBlock);
+        for (int j = 0; j < kNS; ++j)
 #pragma unroll
-          for (int j = 0; j < kNS; ++j)
+          for (int h = 0; h < 2; ++h) wd[j][h] = desc_kmajor(base + kW + (2 * j + h) * kBlock);
+        // E-step of tile t into buffer t % 3 once the M-step of t - 3 has read
+        // it, in the first pass's order: the weight terms over features 0-63,
+        // then over features 64-127
+        for (int t = 0; ok && t < T; ++t) {
+          const int s = t % kXSlots, b = t % kSR;
+          if (!mbar_wait(&bars->xfull[s], (t / kXSlots) & 1, abort, lim)) { ok = false; break; }
+          if (t >= kSR && !mbar_wait(&bars->mfree[b], ((t / kSR) - 1) & 1, abort, lim)) { ok = false; break; }
+          tmem_fence_after();
+          const uint32_t d = tmem + (uint32_t)(b * 128);
+          const uint32_t xs = base + kX + s * 2 * kBlock;
+          uint32_t acc = 0;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {  // 16 features per instruction: +32 B
-              mma_bf16(d, wd[j][h] + 2 * kk, xd + 2 * kk, id_e, acc);
-              acc = 1;
-            }
-        }
-        mma_commit(&bars->sfull[b]);
-        return true;
-      };
-      // M-step of tile t: A = R^T(t) in the buffer's columns, part p of 32
-      // rows at columns 32 p (r_hi, 16 columns of row pairs) and 32 p + 16
-      // (r_lo); 16 rows per instruction
-      auto issue_m = [&](int t) -> bool {
-        const int s = t % kXSlots, b = t % kSR;
-        if (!mbar_wait(&bars->rfull[b], (t / kSR) & 1, abort, lim)) return false;
-        tmem_fence_after();
-        const uint64_t xm = desc_mnmajor(base + kX + s * 2 * kBlock, kBlock);
-        const uint32_t rb = tmem + (uint32_t)(b * 128);
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t xd = desc_kmajor(xs + h * kBlock);
 #pragma unroll
-        for (int part = 0; part < 2; ++part)
+            for (int j = 0; j < kNS; ++j)
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {  // rows 16 ks .. 16 ks + 15: +2048 B (MN-major)
-            const uint32_t acol = (uint32_t)(32 * (ks >> 1) + 8 * (ks & 1) + 16 * part);
-            mma_bf16_ts(tmem + kDmCol, rb + acol, xm + (uint64_t)(ks * 128), id_m,
-                        (t == 0 && part == 0 && ks == 0) ? 0u : 1u);
+              for (int kk = 0; kk < 4; ++kk) {  // 16 features per instruction: +32 B
+                mma_bf16(d, wd[j][h] + 2 * kk, xd + 2 * kk, id_e, acc);
+                acc = 1;
+              }
           }
-        mma_commit(&bars->mfree[b]);
-        mma_commit(&bars->xfree[s]);
-        return true;
-      };
-      // E(0), E(1), then per tile M(t), E(t+2)
-      if (ok && T > 0) ok = issue_e(0);
-      if (ok && T > 1) ok = issue_e(1);
-      for (int t = 0; ok && t < T; ++t) {
-        if (!issue_m(t)) { ok = false; break; }
-        if (t + 2 < T && !issue_e(t + 2)) { ok = false; break; }
+          mma_commit(&bars->sfull[b]);
+        }
+      } else {
+        // M-step of tile t: A = R^T(t) in the buffer's columns, part p of 32
+        // rows at columns 32 p (r_hi, 16 columns of row pairs) and 32 p + 16
+        // (r_lo); 16 rows per instruction
+        const uint32_t id_m = idesc_bf16(128, 128, 0, 1);  // R^T (tensor memory) x X (MN-major)
+        for (int t = 0; ok && t < T; ++t) {
+          const int s = t % kXSlots, b = t % kSR;
+          if (!mbar_wait(&bars->rfull[b], (t / kSR) & 1, abort, lim)) { ok = false; break; }
+          tmem_fence_after();
+          const uint64_t xm = desc_mnmajor(base + kX + s * 2 * kBlock, kBlock);
+          const uint32_t rb = tmem + (uint32_t)(b * 128);
+#pragma unroll
+          for (int part = 0; part < 2; ++part)
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {  // rows 16 ks .. 16 ks + 15: +2048 B (MN-major)
+              const uint32_t acol = (uint32_t)(32 * (ks >> 1) + 8 * (ks & 1) + 16 * part);
+              mma_bf16_ts(tmem + kDmCol, rb + acol, xm + (uint64_t)(ks * 128), id_m,
+                          (t == 0 && part == 0 && ks == 0) ? 0u : 1u);
+            }
+          mma_commit(&bars->mfree[b]);
+          mma_commit(&bars->xfree[s]);
+        }
       }
       if (!ok) set_abort(bars, a.status);
       mma_commit(&bars->mdone);
@@ -288,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (!ok) set_abort(bars, a.status);
   } else {
-    // ---------------- softmax: 16 warps, thread = component ----------------
+    // ---------------- softmax: 16 warps (6 .. 21), thread = component ----------------
     // warp w reads lanes 32 (w % 4) .. + 31 (the tensor-memory access rule):
     // components 32 (w % 4) + lane; part p owns rows 32 p .. 32 p + 31
     const int q4 = warp & 3;
