@@ -125,8 +125,8 @@ struct Lay {
   static constexpr int kXch = kHalfX + 2 * kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
   __host__ __device__ static constexpr int bars(int c) { return kXch + 2 * c * 128 * 8; }
   // the log-likelihood reduction slot: 4 doubles (diag), 16 (tied)
-  __host__ __device__ static constexpr int red(int c) { return bars(c) + 192; }
-  __host__ __device__ static constexpr int total(int c) { return bars(c) + (kTied ? 320 : 256); }
+  __host__ __device__ static constexpr int red(int c) { return bars(c) + 224; }
+  __host__ __device__ static constexpr int total(int c) { return bars(c) + (kTied ? 352 : 256); }
   // tensor memory: S (+ tied: up to 64 columns of y) | M-step statistics | E-step operand
   // (diag [x | s_hi | s_lo], tied [x_hi | x_mid | x_lo]: 96 columns; spherical x: 64)
   static constexpr int kFdmCols = kSph ? 144 : kFdm;  // spherical [x (128) | aux (16)]
@@ -154,8 +154,8 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 struct Bars {
   uint64_t params;
-  uint64_t xfull;      // TMA: staging slot holds X(t)
-  uint64_t sempty;     // prep: staging slot read (128 threads)
+  uint64_t xfull[3];   // TMA: staging slot holds X(t) (slots 1, 2: spherical kModeRowStat only)
+  uint64_t sempty[3];  // prep: staging slot read (128 threads)
   uint64_t mxfull;     // TMA: M-step stage holds X(t)
   uint64_t ffull;      // prep: E-step operand of tile t in tensor memory (4 warps)
   uint64_t mfull;      // prep: M-step stage holds [x | s_hi | s_lo] of tile t (4 warps)
@@ -165,7 +165,7 @@ struct Bars {
   uint64_t rfull;      // softmax: an R part written (16 warps)
   uint64_t rfree;      // MMA: that R part consumed
   uint64_t xch[2];     // cluster exchange of (row max, row sum)
-  uint64_t hx[2];      // every part of the row wrote its (max, sum) (16 warps)
+  uint64_t hx[3];      // every part of the row wrote its (max, sum) (16 warps; kModeRowStat: three slots)
   uint64_t mdone;      // MMA: all MMAs complete
   uint64_t pfull;      // predict_proba: the tile's rows staged in shared memory (16 warps)
   uint64_t pfree;      // predict_proba: the staged rows stored to global memory (16 warps)
@@ -173,7 +173,7 @@ struct Bars {
   uint32_t tmem_base;
   int abort;
 };
-static_assert(sizeof(Bars) <= 192, "barrier block overlaps the reduction slot");
+static_assert(sizeof(Bars) <= 224, "barrier block overlaps the reduction slot");
 
 __device__ __forceinline__ void set_abort(Bars* b, int* status) {
   b->abort = 1;
@@ -210,6 +210,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 "modes of each covariance type");
   using Y = Lay<kCov>;
   constexpr int kParams = Y::kParams, kStaging = Y::kStaging, kMX = Y::kMX, kMSH = Y::kMSH, kMSL = Y::kMSL;
+  // X staging slots: one, or (spherical row statistics, which has no M-step)
+  // three -- the M-step stage and the R buffer's first block hold slots 1
+  // and 2 -- so that the TMA loads run two tiles ahead of the prep warps
+  // instead of exposing one HBM round trip per tile
+  constexpr int kNStage = (kSph && kMode == kModeRowStat) ? 3 : 1;
+  // with the ring, the E-step reads X straight from its staging slot (A from
+  // shared memory) and the slot is freed by the prep warps and the E-step's
+  // completion; otherwise the prep warps copy X into tensor memory
+  constexpr bool kRing = kNStage > 1;
+  auto stage_off = [](int slot) { return slot == 0 ? kStaging : kMX + (slot - 1) * 2 * kBlock; };
   constexpr int kOnes = Y::kOnes, kR = Y::kR, kConsts = Y::kConsts, kHalfX = Y::kHalfX, kXch = Y::kXch;
   constexpr uint32_t kSCol = Y::kSCol, kDmCol = Y::kDmCol, kFCol = Y::kFCol;
   extern __shared__ __align__(1024) char smem_raw[];
@@ -242,15 +252,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(&bars->params, 1);
-    mbar_init(&bars->xfull, 1);
-    mbar_init(&bars->sempty, 128);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bars->xfull[i], 1);
+      mbar_init(&bars->sempty[i], kRing ? 129 : 128);
+    }
     mbar_init(&bars->mxfull, 1);
     mbar_init(&bars->sfull, 1);
     mbar_init(&bars->sfree, kSoftWarps);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->xch[i], 1);
-      mbar_init(&bars->hx[i], kSoftWarps);
-    }
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->xch[i], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bars->hx[i], kSoftWarps);
     mbar_init(&bars->ffull, 4);
     mbar_init(&bars->mfull, 4);
     mbar_init(&bars->mfree, 1);
@@ -372,28 +382,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     float q_cur = 0.f, q_prev = 0.f;  // spherical: |x|^2 of this row in tiles t and t - 1
     for (int t = 0; t < T; ++t) {
-      if (!mbar_wait_warp(&bars->xfull, t & 1, abort, lim)) { ok = false; break; }
+      const int xs = t % kNStage;
+      if (!mbar_wait_warp(&bars->xfull[xs], (t / kNStage) & 1, abort, lim)) { ok = false; break; }
       if constexpr (kSph) {
-        // the E-step of t-1 read the operand region: wait for its completion
-        if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
-        tmem_fence_after();
+        if constexpr (kRing) {
+          // the |x|^2 slot of tile t was last read by the softmax for tile
+          // t-2, before it released S(t-2); wait for S(t-1) released (the
+          // softmax waits for this tile's |x|^2 before releasing S(t), so
+          // this barrier cannot be a phase ahead)
+          if (t >= 1 && !mbar_wait_warp(&bars->sfree, (t - 1) & 1, abort, lim)) { ok = false; break; }
+        } else {
+          // the E-step of t-1 read the operand region: wait for its completion
+          if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
+          tmem_fence_after();
+        }
         float q = 0.f;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {  // bf16 box h: features 64h .. 64h + 63 -> operand columns 32h .. 32h + 31
           uint32_t w[32];
-          load_row(kStaging + h * kBlock, w);
+          load_row(stage_off(xs) + h * kBlock, w);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float x0 = bf16lo_to_f32(w[i]), x1 = bf16hi_to_f32(w[i]);
             q = fmaf(x0, x0, q);
             q = fmaf(x1, x1, q);
           }
-          tmem_st32(tmem + lane_addr + kFCol + 32 * h, w);
+          if constexpr (!kRing) tmem_st32(tmem + lane_addr + kFCol + 32 * h, w);
         }
         q_prev = q_cur;
         q_cur = q;
         // the softmax reads the slot of tile t before it releases S(t), which
-        // the E-step of t+1 (and so the prep of t+2) waits for
+        // the E-step of t+1 (and so the prep of t+2) waits for (ring: see above)
         qbuf[(t & 1) * 128 + r] = q;
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->qfull[t & 1]);
@@ -438,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // arrive after __syncwarp, let the next TMA copy (async proxy) overtake
       // loads still in flight -- rows of the next tile then leaked into this
       // one when the softmax ran slow (measured with predict_proba).
-      mbar_arrive(&bars->sempty);
+      mbar_arrive(&bars->sempty[xs]);
       tmem_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->ffull);
@@ -475,10 +494,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       bool ok = true;
       for (int t = 0; t < T && ok; ++t) {
-        if (t >= 1 && !mbar_wait(&bars->sempty, (t - 1) & 1, abort, lim)) { ok = false; break; }
+        const int xs = t % kNStage;
+        if (t >= kNStage && !mbar_wait(&bars->sempty[xs], ((t / kNStage) - 1) & 1, abort, lim)) { ok = false; break; }
         if (a.test_stall) break;  // test hook: no X tile ever lands, every wait on it runs out
-        mbar_expect_tx(&bars->xfull, kTileBytes);
-        load_tile(kStaging, kStaging + kBlock, row0(t), &bars->xfull);
+        mbar_expect_tx(&bars->xfull[xs], kTileBytes);
+        load_tile(stage_off(xs), stage_off(xs) + kBlock, row0(t), &bars->xfull[xs]);
         issued = t + 1;
         if (kEm && t >= 1) ok = load_m(t - 1);
       }
@@ -487,7 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // before the CTA can exit, every copy it started has landed (bounded,
       // also after an abort): the weights and the last load of each buffer
       mbar_wait(&bars->params, 0, nullptr, lim);
-      if (issued > 0) mbar_wait(&bars->xfull, (issued - 1) & 1, nullptr, lim);
+      for (int u = issued > kNStage ? issued - kNStage : 0; u < issued; ++u)
+        mbar_wait(&bars->xfull[u % kNStage], (u / kNStage) & 1, nullptr, lim);
       if (missued > 0) mbar_wait(&bars->mxfull, (missued - 1) & 1, nullptr, lim);
     }
   } else if (warp == kWarpMma) {
@@ -510,6 +531,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // E-step of tile t into S: x.a_j, s_hi.v_j (j < 3), s_lo.v_j (j < 2)
       auto issue_e = [&](int t) -> bool {
+        if constexpr (kRing) {
+          // A = X(t) in its staging slot (K-major, rows x features), the
+          // instruction order of the tensor-memory form below; the commit on
+          // the slot's barrier frees it once the E-step has read it
+          const int xs = t % kNStage;
+          if (!mbar_wait(&bars->xfull[xs], (t / kNStage) & 1, abort, lim)) return false;
+          if (t >= 1 && !mbar_wait(&bars->sfree, (t - 1) & 1, abort, lim)) return false;
+          tmem_fence_after();
+          const uint32_t d = tmem + kSCol;
+          const uint32_t xa = base + (uint32_t)stage_off(xs);
+          uint32_t acc = 0;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t xd = desc_kmajor(xa + (uint32_t)(h * kBlock));
+#pragma unroll
+            for (int j = 0; j < kNS; ++j)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                mma_bf16(d, xd + 2 * kk, (h ? wv[j] : wa[j]) + 2 * kk, id_e, acc);
+                acc = 1;
+              }
+          }
+          mma_commit(&bars->sfull);
+          mma_commit(&bars->sempty[xs]);
+          return true;
+        }
         if (!mbar_wait(&bars->ffull, t & 1, abort, lim)) return false;
         if (t >= 1 && !mbar_wait(&bars->sfree, (t - 1) & 1, abort, lim)) return false;
         tmem_fence_after();
@@ -829,6 +876,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       // inference: the logits and the row's cluster-wide reduction only
+      if constexpr (kMode == kModeRowStat) {
+        // Software-pipelined over three tiles, so that the wait for the row's
+        // other parts and the cluster exchange overlap the next tile's
+        // logits.  Iteration t: A(t) this part's (max, sum) of tile t into
+        // slot t % 3 of the part table; C(t - 2) the cluster's (max, sum) of
+        // tile t - 2 into rowstat; B(t - 1) the row's four parts of tile t - 1
+        // combined and sent to the cluster.  The part table lives in the R
+        // buffer (no M-step here).  Reuse: a part writes slot t % 3 once S(t)
+        // is complete, i.e. after every warp loaded S(t - 1), which part 0
+        // does only after its B(t - 3); the cluster writes exchange slot
+        // (t + 1) & 1 of this CTA after its own C(t) (B after C within an
+        // iteration), which follows this CTA's B(t) and so its C(t - 1).
+        // (The R buffer's first block is staging slot 2.)
+        float2* parts = reinterpret_cast<float2*>(sm + kR + kBlock);  // [3][kSplit][128]
+        static_assert(3 * kSplit * 128 * 8 <= kBlock, "part table in the R buffer's second block");
+        for (int t = 0; t < T + 2; ++t) {
+          if (t < T) {  // A(t)
+            if (!mbar_wait_warp(&bars->sfull, t & 1, abort, lim)) { ok = false; break; }
+            tmem_fence_after();
+            const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
+#pragma unroll
+            for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
+            float qn = 0.f;
+            if (!row_q(t, qn)) { ok = false; break; }  // read before S(t) is released
+            tmem_wait_ld();
+            tmem_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->sfree);
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            logits(qn, mx);
+            const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+            const float mref = (m == -INFINITY) ? 0.f : m;
+            float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int k = 0; k < kPart; ++k) sm4[k & 3] += ex2_approx(p[k] - mref);
+            parts[((t % 3) * kSplit + qc) * 128 + row] = make_float2(m, (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->hx[t % 3]);
+          }
+          if (qc == 0 && t >= 2) {  // C(t - 2)
+            const int u = t - 2, su = u & 1;
+            if (!mbar_wait_warp(&bars->xch[su], (u >> 1) & 1, abort, lim)) { ok = false; break; }
+            float2 e[kMaxCluster];
+#pragma unroll
+            for (int q = 0; q < kMaxCluster; ++q)
+              e[q] = q < nclus ? xch[(su * nclus + q) * 128 + row] : make_float2(-INFINITY, 0.f);
+            float M = e[0].x;
+#pragma unroll
+            for (int q = 1; q < kMaxCluster; ++q) M = fmaxf(M, e[q].x);
+            float S = 0.f;
+#pragma unroll
+            for (int q = 0; q < kMaxCluster; ++q)
+              if (q < nclus) S += e[q].y * ex2_approx(e[q].x - M);
+            const int64_t gu = (cid + (int64_t)u * ncl) * kBM + row;
+            if (gu < a.N && rank == 0) a.rowstat[gu] = make_float2(M, S);  // log2 units
+          }
+          if (qc == 0 && t >= 1 && t <= T) {  // B(t - 1)
+            const int u = t - 1, hu = u % 3, su = u & 1;
+            if (!mbar_wait_warp(&bars->hx[hu], (u / 3) & 1, abort, lim)) { ok = false; break; }
+            float2 o[kSplit];
+#pragma unroll
+            for (int q = 0; q < kSplit; ++q) o[q] = parts[(hu * kSplit + q) * 128 + row];
+            float mc = o[0].x;
+#pragma unroll
+            for (int q = 1; q < kSplit; ++q) mc = fmaxf(mc, o[q].x);
+            float sc2 = 0.f;
+#pragma unroll
+            for (int q = 0; q < kSplit; ++q) sc2 += o[q].y * ex2_approx(o[q].x - mc);
+            if (tid == kWarpSoftmax0 * 32) mbar_expect_tx(&bars->xch[su], (uint32_t)(nclus * 128 * 8));
+#pragma unroll
+            for (int q = 0; q < kMaxCluster; ++q)
+              if (q < nclus)
+                st_async_f2(map_shared(xch_mine + su * slot_stride, q), mc, sc2,
+                            map_shared(smem_u32(&bars->xch[su]), q));
+          }
+          if (*abort) { ok = false; break; }
+        }
+      } else
       for (int t = 0; t < T; ++t) {
         const int s = t & 1;
         const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
