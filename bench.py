@@ -483,7 +483,9 @@ def main():
         nch = (K + 127) // 128
         sph_new = D == 128 and (nch <= 4 or nch > 8) and os.environ.get("GMMXX_B200_SPH_KERNEL") != "legacy"
         kernel_names = {"diag": "em_tc_diag_kernel", "tied": "em_tc_diag_kernel<tied>",
-                        "spherical": ("em_tc_diag_kernel<spherical> (row-statistics + external-lse passes)"
+                        "spherical": (("em_tc_diag_kernel<spherical> row statistics + em_tc_sph_ext_kernel"
+                                       if os.environ.get("GMMXX_B200_SPH_PASS2") != "diag" else
+                                       "em_tc_diag_kernel<spherical> (row-statistics + external-lse passes)")
                                       if sph_new and nch > 8 else "em_tc_diag_kernel<spherical>" if sph_new
                                       else "em_tc_kernel")}
         line = {

@@ -125,8 +125,8 @@ struct Lay {
   static constexpr int kXch = kHalfX + 2 * kSplit * 128 * 8;  // [2 slots][C][128 rows] float2
   __host__ __device__ static constexpr int bars(int c) { return kXch + 2 * c * 128 * 8; }
   // the log-likelihood reduction slot: 4 doubles (diag), 16 (tied)
-  __host__ __device__ static constexpr int red(int c) { return bars(c) + 224; }
-  __host__ __device__ static constexpr int total(int c) { return bars(c) + (kTied ? 352 : 256); }
+  __host__ __device__ static constexpr int red(int c) { return bars(c) + 256; }
+  __host__ __device__ static constexpr int total(int c) { return bars(c) + (kTied ? 384 : 288); }
   // tensor memory: S (+ tied: up to 64 columns of y) | M-step statistics | E-step operand
   // (diag [x | s_hi | s_lo], tied [x_hi | x_mid | x_lo]: 96 columns; spherical x: 64)
   static constexpr int kFdmCols = kSph ? 144 : kFdm;  // spherical [x (128) | aux (16)]
@@ -160,12 +160,12 @@ struct Bars {
   uint64_t ffull;      // prep: E-step operand of tile t in tensor memory (4 warps)
   uint64_t mfull;      // prep: M-step stage holds [x | s_hi | s_lo] of tile t (4 warps)
   uint64_t mfree;      // MMA: M-step of tile t done reading the stage
-  uint64_t sfull;      // MMA: S(t) complete (the E-step operand is free again)
-  uint64_t sfree;      // softmax: S(t) loaded (16 warps)
+  uint64_t sfull[2];   // MMA: S(t) complete (the E-step operand is free again); slot 1: ring mode
+  uint64_t sfree[2];   // softmax: S(t) loaded (16 warps)
   uint64_t rfull;      // softmax: an R part written (16 warps)
   uint64_t rfree;      // MMA: that R part consumed
   uint64_t xch[2];     // cluster exchange of (row max, row sum)
-  uint64_t hx[3];      // every part of the row wrote its (max, sum) (16 warps; kModeRowStat: three slots)
+  uint64_t hx[4];      // every part of the row wrote its (max, sum) (16 warps; kModeRowStat: four slots)
   uint64_t mdone;      // MMA: all MMAs complete
   uint64_t pfull;      // predict_proba: the tile's rows staged in shared memory (16 warps)
   uint64_t pfree;      // predict_proba: the staged rows stored to global memory (16 warps)
@@ -173,7 +173,7 @@ struct Bars {
   uint32_t tmem_base;
   int abort;
 };
-static_assert(sizeof(Bars) <= 224, "barrier block overlaps the reduction slot");
+static_assert(sizeof(Bars) <= 256, "barrier block overlaps the reduction slot");
 
 __device__ __forceinline__ void set_abort(Bars* b, int* status) {
   b->abort = 1;
@@ -219,6 +219,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // shared memory) and the slot is freed by the prep warps and the E-step's
   // completion; otherwise the prep warps copy X into tensor memory
   constexpr bool kRing = kNStage > 1;
+  // ring mode: a second S slot in the (unused) M-step accumulator columns
+  constexpr uint32_t kS1Off = kRing ? Y::kDmCol - Y::kSCol : 0;
+  static_assert(!kRing || Y::kDmCol + 128 <= Y::kFCol, "second S slot in the M-step columns");
   auto stage_off = [](int slot) { return slot == 0 ? kStaging : kMX + (slot - 1) * 2 * kBlock; };
   constexpr int kOnes = Y::kOnes, kR = Y::kR, kConsts = Y::kConsts, kHalfX = Y::kHalfX, kXch = Y::kXch;
   constexpr uint32_t kSCol = Y::kSCol, kDmCol = Y::kDmCol, kFCol = Y::kFCol;
@@ -257,10 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->sempty[i], kRing ? 129 : 128);
     }
     mbar_init(&bars->mxfull, 1);
-    mbar_init(&bars->sfull, 1);
-    mbar_init(&bars->sfree, kSoftWarps);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->sfull[i], 1);
+      mbar_init(&bars->sfree[i], kSoftWarps);
+    }
     for (int i = 0; i < 2; ++i) mbar_init(&bars->xch[i], 1);
-    for (int i = 0; i < 3; ++i) mbar_init(&bars->hx[i], kSoftWarps);
+    for (int i = 0; i < 4; ++i) mbar_init(&bars->hx[i], kSoftWarps);
     mbar_init(&bars->ffull, 4);
     mbar_init(&bars->mfull, 4);
     mbar_init(&bars->mfree, 1);
@@ -390,10 +395,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // t-2, before it released S(t-2); wait for S(t-1) released (the
           // softmax waits for this tile's |x|^2 before releasing S(t), so
           // this barrier cannot be a phase ahead)
-          if (t >= 1 && !mbar_wait_warp(&bars->sfree, (t - 1) & 1, abort, lim)) { ok = false; break; }
+          if (t >= 1 && !mbar_wait_warp(&bars->sfree[(t - 1) & 1], ((t - 1) >> 1) & 1, abort, lim)) { ok = false; break; }
         } else {
           // the E-step of t-1 read the operand region: wait for its completion
-          if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
+          if (t >= 1 && !mbar_wait_warp(&bars->sfull[0], (t - 1) & 1, abort, lim)) { ok = false; break; }
           tmem_fence_after();
         }
         float q = 0.f;
@@ -418,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&bars->qfull[t & 1]);
       } else if constexpr (kTied) {
         // the E-step of t-1 read the operand region: wait for its completion
-        if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
+        if (t >= 1 && !mbar_wait_warp(&bars->sfull[0], (t - 1) & 1, abort, lim)) { ok = false; break; }
         tmem_fence_after();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {  // fp32 box h: features 32h .. 32h + 31 -> operand words 16h .. 16h + 15
@@ -438,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t w[32];
         load_row(kStaging, w);
         // the E-step of t-1 read the operand region: wait for its completion
-        if (t >= 1 && !mbar_wait_warp(&bars->sfull, (t - 1) & 1, abort, lim)) { ok = false; break; }
+        if (t >= 1 && !mbar_wait_warp(&bars->sfull[0], (t - 1) & 1, abort, lim)) { ok = false; break; }
         tmem_fence_after();
         tmem_st32(tmem + lane_addr + kFCol, w);
 #pragma unroll
@@ -537,9 +542,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // the slot's barrier frees it once the E-step has read it
           const int xs = t % kNStage;
           if (!mbar_wait(&bars->xfull[xs], (t / kNStage) & 1, abort, lim)) return false;
-          if (t >= 1 && !mbar_wait(&bars->sfree, (t - 1) & 1, abort, lim)) return false;
+          // two S slots: S(t) overwrites S(t-2) once the softmax loaded it
+          if (t >= 2 && !mbar_wait(&bars->sfree[t & 1], ((t >> 1) - 1) & 1, abort, lim)) return false;
           tmem_fence_after();
-          const uint32_t d = tmem + kSCol;
+          const uint32_t d = tmem + kSCol + (uint32_t)((t & 1) * kS1Off);
           const uint32_t xa = base + (uint32_t)stage_off(xs);
           uint32_t acc = 0;
 #pragma unroll
@@ -553,12 +559,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc = 1;
               }
           }
-          mma_commit(&bars->sfull);
+          mma_commit(&bars->sfull[t & 1]);
           mma_commit(&bars->sempty[xs]);
           return true;
         }
         if (!mbar_wait(&bars->ffull, t & 1, abort, lim)) return false;
-        if (t >= 1 && !mbar_wait(&bars->sfree, (t - 1) & 1, abort, lim)) return false;
+        if (t >= 1 && !mbar_wait(&bars->sfree[0], (t - 1) & 1, abort, lim)) return false;
         tmem_fence_after();
         const uint32_t d = tmem + kSCol;
         uint32_t acc = 0;
@@ -588,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int kk = 0; kk < 4; ++kk) mma_bf16_ts(d, tmem + kFCol + 64 + kk * 8, wv[j] + 2 * kk, id_e, 1u);
           }
         }
-        mma_commit(&bars->sfull);
+        mma_commit(&bars->sfull[0]);
         return true;
       };
       const uint64_t r0 = desc_mnmajor(base + kR, kBlock);
@@ -711,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = t & 1;
         const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
         const bool valid = grow < a.N;
-        if (!mbar_wait_warp(&bars->sfull, t & 1, abort, lim)) { ok = false; break; }
+        if (!mbar_wait_warp(&bars->sfull[0], t & 1, abort, lim)) { ok = false; break; }
         tmem_fence_after();
         const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
   #pragma unroll
@@ -725,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         tmem_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->sfree);
+        if (lane == 0) mbar_arrive(&bars->sfree[0]);
         float qy = 0.f;  // tied: the piece's share of |y|^2 = x^T P x
         if (kTied && qc < ny) {
   #pragma unroll
@@ -880,22 +886,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Software-pipelined over three tiles, so that the wait for the row's
         // other parts and the cluster exchange overlap the next tile's
         // logits.  Iteration t: A(t) this part's (max, sum) of tile t into
-        // slot t % 3 of the part table; C(t - 2) the cluster's (max, sum) of
+        // slot t % 4 of the part table; C(t - 2) the cluster's (max, sum) of
         // tile t - 2 into rowstat; B(t - 1) the row's four parts of tile t - 1
         // combined and sent to the cluster.  The part table lives in the R
-        // buffer (no M-step here).  Reuse: a part writes slot t % 3 once S(t)
-        // is complete, i.e. after every warp loaded S(t - 1), which part 0
-        // does only after its B(t - 3); the cluster writes exchange slot
+        // buffer's second block (no M-step here; the first block is staging
+        // slot 2).  Reuse: a part writes slot t % 4 once S(t) is complete,
+        // i.e. after every warp loaded S(t - 2) (two S slots), which part 0
+        // does only after its B(t - 4); the cluster writes exchange slot
         // (t + 1) & 1 of this CTA after its own C(t) (B after C within an
         // iteration), which follows this CTA's B(t) and so its C(t - 1).
-        // (The R buffer's first block is staging slot 2.)
-        float2* parts = reinterpret_cast<float2*>(sm + kR + kBlock);  // [3][kSplit][128]
-        static_assert(3 * kSplit * 128 * 8 <= kBlock, "part table in the R buffer's second block");
+        float2* parts = reinterpret_cast<float2*>(sm + kR + kBlock);  // [4][kSplit][128]
+        static_assert(4 * kSplit * 128 * 8 <= kBlock, "part table in the R buffer's second block");
         for (int t = 0; t < T + 2; ++t) {
           if (t < T) {  // A(t)
-            if (!mbar_wait_warp(&bars->sfull, t & 1, abort, lim)) { ok = false; break; }
+            if (!mbar_wait_warp(&bars->sfull[t & 1], (t >> 1) & 1, abort, lim)) { ok = false; break; }
             tmem_fence_after();
-            const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
+            const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)((t & 1) * kS1Off + k0);
 #pragma unroll
             for (int c = 0; c < kPart / 32; ++c) tmem_ld32(sc + 32 * c, p + 32 * c);
             float qn = 0.f;
@@ -903,7 +909,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_ld();
             tmem_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->sfree);
+            if (lane == 0) mbar_arrive(&bars->sfree[t & 1]);
             float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             logits(qn, mx);
             const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
@@ -911,9 +917,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             float sm4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int k = 0; k < kPart; ++k) sm4[k & 3] += ex2_approx(p[k] - mref);
-            parts[((t % 3) * kSplit + qc) * 128 + row] = make_float2(m, (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]));
+            parts[((t & 3) * kSplit + qc) * 128 + row] = make_float2(m, (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]));
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->hx[t % 3]);
+            if (lane == 0) mbar_arrive(&bars->hx[t & 3]);
           }
           if (qc == 0 && t >= 2) {  // C(t - 2)
             const int u = t - 2, su = u & 1;
@@ -933,8 +939,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (gu < a.N && rank == 0) a.rowstat[gu] = make_float2(M, S);  // log2 units
           }
           if (qc == 0 && t >= 1 && t <= T) {  // B(t - 1)
-            const int u = t - 1, hu = u % 3, su = u & 1;
-            if (!mbar_wait_warp(&bars->hx[hu], (u / 3) & 1, abort, lim)) { ok = false; break; }
+            const int u = t - 1, hu = u & 3, su = u & 1;
+            if (!mbar_wait_warp(&bars->hx[hu], (u >> 2) & 1, abort, lim)) { ok = false; break; }
             float2 o[kSplit];
 #pragma unroll
             for (int q = 0; q < kSplit; ++q) o[q] = parts[(hu * kSplit + q) * 128 + row];
@@ -958,7 +964,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = t & 1;
         const int64_t grow = (cid + (int64_t)t * ncl) * kBM + row;
         const bool valid = grow < a.N;
-        if (!mbar_wait_warp(&bars->sfull, t & 1, abort, lim)) { ok = false; break; }
+        if (!mbar_wait_warp(&bars->sfull[0], t & 1, abort, lim)) { ok = false; break; }
         tmem_fence_after();
         const uint32_t sc = tmem + lane_addr + kSCol + (uint32_t)k0;
 #pragma unroll
@@ -970,7 +976,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         tmem_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->sfree);
+        if (lane == 0) mbar_arrive(&bars->sfree[0]);
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         logits(qn, mx);
         float2* hxs = halfx + s * kSplit * 128;
