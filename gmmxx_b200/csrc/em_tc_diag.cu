@@ -84,7 +84,10 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kHalfLog2e = 0.5f * kLog2e;  // logit scale of a unit distance (diag: s = 1)
 constexpr int kMaxCluster = kMaxClusterDiag;
 
-enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpSoftmax0 = 6 };
+// EM modes issue the E-steps from warp kWarpMma and the M-steps from warp
+// kWarpMmaM, on another SM sub-partition (warp % 4): one thread issuing every
+// MMA of a tile shares its sub-partition with four busy softmax warps
+enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpSoftmax0 = 6, kWarpMmaM = 22 };
 // EM statistics, or inference without the M-step (TcLaunch::infer); the
 // spherical large-K passes: each row's (max, scaled sum) over the cluster's
 // components (kModeRowStat), then the M-step with r = 2^(l - lse) from the
@@ -94,7 +97,7 @@ enum Warp { kWarpPrep0 = 0, kWarpTma = 4, kWarpMma = 5, kWarpSoftmax0 = 6 };
 enum Mode {
   kModeEm = 0, kModeLse = 1, kModeArgmax = 2, kModeProba = 3, kModeRowStat = 4, kModeExtLse = 5, kModeProbaExt = 6
 };
-constexpr int kThreads = (kWarpSoftmax0 + kSoftWarps) * 32;  // 22 warps, <= 88 registers each
+constexpr int kThreads = (kWarpMmaM + 1) * 32;  // 23 warps, <= 80 registers each
 
 // Shared memory carve-up (byte offsets from the 1024-aligned dynamic block)
 // and tensor memory columns of each covariance type's layout: diag (bf16 X,
@@ -271,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->mfree, 1);
     mbar_init(&bars->rfull, kSoftWarps);
     mbar_init(&bars->rfree, 1);
-    mbar_init(&bars->mdone, 1);
+    mbar_init(&bars->mdone, 2);  // both issuing threads commit
     mbar_init(&bars->pfull, kSoftWarps);
     mbar_init(&bars->pfree, kSoftWarps);
     mbar_init(&bars->qfull[0], 4);
@@ -516,8 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&bars->xfull[u % kNStage], (u / kNStage) & 1, nullptr, lim);
       if (missued > 0) mbar_wait(&bars->mxfull, (missued - 1) & 1, nullptr, lim);
     }
-  } else if (warp == kWarpMma) {
-    // ---------------- MMA issuer (one thread) ----------------
+  } else if (warp == kWarpMma || warp == kWarpMmaM) {
+    // ---------------- MMA issuers (one thread each) ----------------
     if (lane == 0) {
       // A (TMEM) x W^T (K-major); tied: N also covers this rank's y columns
       const uint32_t id_e = idesc_bf16(128, kKC + 16 * ny, 0, 0);
@@ -618,29 +621,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       using Hi = std::integral_constant<int, 0>;
       using Lo = std::integral_constant<int, 1>;
-      // Issue order: E(0), E(1), then per tile M_hi(t), M_lo(t), E(t+2).
-      // M_lo(t) waits for the residual R(t), written by the softmax after the
-      // logits of t+1 (whose S(t+1) is already queued); E(t+2) then still ends
-      // before the softmax finishes tile t+1.  Keeping M_lo(t) ahead of E(t+2)
-      // matters: its completion frees the M-step stage for X(t+1) (TMA, then
-      // the prep's s_hi / s_lo), which M_hi(t+1) needs.  Queued behind E(t+2)
-      // it would put an E-step, a TMA round trip and the stage refill into the
-      // critical path of every tile.
-      if constexpr (kEm) {
-        if (ok && T > 0) ok = issue_e(0);
-        if (ok && T > 1) ok = issue_e(1);
+      // Two issuing threads: the E-steps in tile order, each once the
+      // softmax loaded S(t-1) and the prep wrote the operand of t; the M-steps
+      // M_hi(t), M_lo(t) as the softmax writes the two R parts (M_lo(t) after
+      // the logits of t+1).  The tensor pipe takes them in arrival order.
+      if (warp == kWarpMma) {  // E-steps, each as soon as S is free and the operand written
+        for (int t = 0; ok && t < T; ++t) ok = issue_e(t);
+      } else if constexpr (kEm) {  // M-steps
         for (int t = 0; ok && t < T; ++t) {
           if (!issue_m(t, Hi{})) { ok = false; break; }
           if (!issue_m(t, Lo{})) { ok = false; break; }
-          if (t + 2 < T && !issue_e(t + 2)) { ok = false; break; }
         }
-      } else {  // inference: E-steps only, each as soon as S is free
-        for (int t = 0; ok && t < T; ++t) ok = issue_e(t);
       }
       if (!ok) set_abort(bars, a.status);
       mma_commit(&bars->mdone);
     }
-  } else if (warp >= kWarpSoftmax0) {
+  } else if (warp >= kWarpSoftmax0 && warp < kWarpSoftmax0 + kSoftWarps) {
     // ---------------- softmax: 16 warps, kSplit per TMEM lane quarter ----------------
     // warp w reads lanes 32 (w % 4) .. +31 (the tensor-memory access rule);
     // part qc of the row owns components [qc kPart, qc kPart + kPart)
