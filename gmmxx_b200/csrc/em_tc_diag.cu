@@ -1281,17 +1281,20 @@ static int sph128_infer(const TcLaunch& L, const CUtensorMap& tmap, bool one_pas
       default: return launch_mode<kModeProba, GMMXX_SPHERICAL>(L, tmap, st, &ncl);
     }
   }
-  const int nch = L.nchunks, gc = kGroupChunks, groups = (nch + gc - 1) / gc;
-  for (int g = 0; g < groups; ++g) {
-    const int csize = std::min(gc, nch - g * gc);
+  // per-row passes in groups of kRowStatChunks chunks (clusters of 2), the
+  // responsibilities in groups of kGroupChunks (no clusters)
+  const int nch = L.nchunks, g1 = kRowStatChunks, groups1 = (nch + g1 - 1) / g1;
+  for (int g = 0; g < groups1; ++g) {
+    const int csize = std::min(g1, nch - g * g1);
     float2* rs = L.rowstat + (int64_t)g * L.N;
     const int rc = L.infer == kModeArgmax
-                       ? launch_mode<kModeArgmax, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, nullptr, rs)
-                       : launch_mode<kModeRowStat, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, nullptr, rs);
+                       ? launch_mode<kModeArgmax, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * g1, csize, nullptr, rs)
+                       : launch_mode<kModeRowStat, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * g1, csize, nullptr, rs);
     if (rc) return rc;
   }
-  if (int rc = launch_infer_combine(L, groups, L.infer, st)) return rc;
+  if (int rc = launch_infer_combine(L, groups1, L.infer, st)) return rc;
   if (L.infer != kModeProba) return GMMXX_OK;
+  const int gc = kGroupChunks, groups = (nch + gc - 1) / gc;
   for (int g = 0; g < groups; ++g) {
     const int csize = std::min(gc, nch - g * gc);
     if (int rc = launch_mode<kModeProbaExt, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, L.lse, nullptr))
@@ -1301,11 +1304,11 @@ static int sph128_infer(const TcLaunch& L, const CUtensorMap& tmap, bool one_pas
 }
 
 // Spherical, bf16 X, D = 128, EM statistics: K <= 512 in one pass over a
-// cluster of ceil(K / 128) CTAs; K > 1024 in groups of 4 chunks (512
-// components) in two passes -- row statistics per group, their combination
-// into each row's log-sum-exp and the log-likelihood, then per group the
-// responsibilities from it and the M-step (no cluster exchange).  Inference
-// (TcLaunch::infer 1-3) runs on the same layouts.
+// cluster of ceil(K / 128) CTAs; K > 1024 in two passes -- row statistics
+// per group of 2 chunks (256 components, clusters of 2), their combination
+// into each row's log-sum-exp and the log-likelihood, then per group of 4
+// chunks the responsibilities from it and the M-step (no cluster exchange).
+// Inference (TcLaunch::infer 1-3) runs on the same layouts.
 int launch_em_tc_sph128(const TcLaunch& L, cudaStream_t st) {
   if (L.D != 128 || L.infer < 0 || L.infer > 3)
     return set_error(GMMXX_ERR_UNSUPPORTED, "spherical kernel: D = 128, mode %d", L.infer);
@@ -1328,14 +1331,17 @@ int launch_em_tc_sph128(const TcLaunch& L, cudaStream_t st) {
     if (int rc = launch_mode<kModeEm, GMMXX_SPHERICAL>(L, tmap, st, &ncl)) return rc;
     return launch_tc_reduce(L, ncl, st);
   }
-  const int gc = kGroupChunks, groups = (nch + gc - 1) / gc;
-  for (int g = 0; g < groups; ++g) {
-    const int csize = std::min(gc, nch - g * gc);
-    if (int rc = launch_mode<kModeRowStat, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * gc, csize, nullptr,
+  // first pass in groups of kRowStatChunks chunks (clusters of 2), the
+  // second in groups of kGroupChunks (no clusters)
+  const int g1 = kRowStatChunks, groups1 = (nch + g1 - 1) / g1;
+  for (int g = 0; g < groups1; ++g) {
+    const int csize = std::min(g1, nch - g * g1);
+    if (int rc = launch_mode<kModeRowStat, GMMXX_SPHERICAL>(L, tmap, st, &ncl, g * g1, csize, nullptr,
                                                             L.rowstat + (int64_t)g * L.N))
       return rc;
   }
-  if (int rc = launch_rowstat_combine(L, groups, st)) return rc;
+  if (int rc = launch_rowstat_combine(L, groups1, st)) return rc;
+  const int gc = kGroupChunks, groups = (nch + gc - 1) / gc;
   for (int g = 0; g < groups; ++g) {
     const int csize = std::min(gc, nch - g * gc);
     const int rc = sph_ext_enabled()

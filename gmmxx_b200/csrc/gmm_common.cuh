@@ -77,6 +77,11 @@ constexpr int kMaxComponentsSph = 16384;
 // co-reside 33 at a time (132 SMs) against 15 of 8 (120 SMs), for the same
 // work per CTA; the price is twice the passes over X, which HBM absorbs.
 constexpr int kGroupChunks = 4;
+// The row-statistics (first) pass of the diag-layout spherical kernel runs
+// in groups of 2 chunks: 74 co-resident clusters of 2 use all 148 SMs, and
+// the cluster exchange has one peer; its row partials take 8 B per row per
+// group (32 groups at K = 8192).
+constexpr int kRowStatChunks = 2;
 __host__ __device__ inline bool tc_eligible(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   if (B != 1 || N < 65536) return false;
   if (cov == GMMXX_DIAG) return D == 64 && K <= 128 * kMaxClusterDiag;
@@ -97,6 +102,13 @@ __host__ __device__ inline int tc_group_chunks(int64_t K) {
 __host__ __device__ inline int tc_groups(int64_t K) {
   const int nch = (int)((K + 127) / 128), gc = tc_group_chunks(K);
   return (nch + gc - 1) / gc;
+}
+// row-partial groups of the grouped spherical path: the larger of
+// em_tc_kernel's groups (kGroupChunks) and the first pass's (kRowStatChunks)
+__host__ __device__ inline int tc_rowstat_groups(int64_t K) {
+  const int nch = (int)((K + 127) / 128);
+  if (nch <= kMaxClusterSph) return 1;
+  return (nch + kRowStatChunks - 1) / kRowStatChunks;
 }
 // three bf16 terms per weight: a_j (and v_j for diag), 16 KB blocks of
 // [128 components][64 features]; tied: three blocks of [192 rows][64] (the
@@ -185,7 +197,7 @@ inline Layout make_layout(int cov, int64_t B, int64_t N, int64_t D, int64_t K) {
   L.tc_params = L.tc_consts = L.tc_part = L.tc_part_ll = L.tc_rowstat = L.tc_lse = 0;
   if (tc_eligible(cov, B, N, D, K)) {
     const int nch = (int)((K + 127) / 128);
-    const int G = tc_groups(K);
+    const int G = tc_rowstat_groups(K) > tc_groups(K) ? tc_rowstat_groups(K) : tc_groups(K);
     const int C = tc_group_chunks(K);
     L.tc_cluster = C;
     L.tc_chunks = nch;

@@ -101,14 +101,15 @@ def test_accumulate_path_selection(lib, monkeypatch):
 
 
 def test_large_k_spherical_workspace_has_per_group_row_partials(lib):
-    """Spherical K > 1024 runs in groups of 512 components (4 chunks): the
-    workspace grows by 8 B per row per group (the (max, sum) row partials),
-    plus the per-row log-sum-exp buffers, over the fixed-size tables."""
+    """Spherical K > 1024: the first pass writes (max, sum) row partials per
+    group of 256 components (2 chunks), so the workspace grows by 8 B per
+    row per such group, plus the per-row log-sum-exp buffers, over the
+    fixed-size tables."""
     k, d = 8192, 128
     n1, n2 = 1 << 20, 1 << 21
     slope = (_native.workspace_bytes(_native.SPHERICAL, 1, n2, d, k) -
              _native.workspace_bytes(_native.SPHERICAL, 1, n1, d, k)) / (n2 - n1)
-    groups = k // 512
+    groups = k // 256
     per_row = 8 * groups + 4 + 4 + 8 / 64  # row partials, tc log-sum-exp, CUDA-core lse, LL partials
     assert abs(slope - per_row) < 0.01
     # one-pass window (K <= 1024): no per-group partials
