@@ -64,13 +64,19 @@ def launches_per_iteration(cfg, tc_path: bool, approx: bool = False) -> int:
     finalize (per component, then per problem).  Statistics: 3 (pack,
     tensor-core kernel, reduce; or rows, mstep, reduce; or the two approximate
     top-k passes and reduce); 2 for the one-pass K <= 64 kernel and its
-    reduce; for spherical K > 1024 the grouped passes: pack, G row-partial
-    launches, combine, log-likelihood sum, G x (M-step launch + reduce)."""
+    reduce; for spherical K > 1024 the grouped passes: pack, G1 row-partial
+    launches, combine, log-likelihood sum, G2 x (M-step launch + reduce) --
+    G1 = G2 = the groups of 4 chunks on em_tc_kernel (D = 64, or the legacy
+    layout); on the diag-kernel layout (D = 128) G1 counts groups of 2
+    chunks (the row-statistics pass) and G2 groups of 4."""
     prep = 2 + (2 if cfg.cov_type in ("tied", "full") else 0)
     stats = 2 if (not tc_path and not approx and cfg.K <= 64) else 3  # K <= 64: one-pass kernel + reduce
     if tc_path and cfg.cov_type == "spherical" and cfg.K > 1024:
-        groups = (((cfg.K + 127) // 128) + 3) // 4  # groups of 4 chunks (512 components)
-        stats = 3 + 3 * groups
+        nch = (cfg.K + 127) // 128
+        g2 = (nch + 3) // 4  # groups of 4 chunks (512 components)
+        new_layout = cfg.D == 128 and os.environ.get("GMMXX_B200_SPH_KERNEL") != "legacy"
+        g1 = (nch + 1) // 2 if new_layout else g2
+        stats = 3 + g1 + 2 * g2
     return prep + stats + 2
 
 

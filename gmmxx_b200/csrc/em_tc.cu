@@ -720,11 +720,29 @@ __global__ void tc_lse_combine_kernel(const float2* rowstat, int groups, int64_t
                                       float scale = 1.f) {
   double acc = 0.0;
   for (int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; n < N; n += (int64_t)gridDim.x * blockDim.x) {
+    // the groups' partials in blocks of 8 independent loads (the second
+    // sweep re-reads them from cache), summed in group order
     float M = -INFINITY;
-    for (int g = 0; g < groups; ++g) M = fmaxf(M, rowstat[(int64_t)g * N + n].x);
+    int g = 0;
+    for (; g + 8 <= groups; g += 8) {
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = __ldg(&rowstat[(int64_t)(g + i) * N + n].x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) M = fmaxf(M, x[i]);
+    }
+    for (; g < groups; ++g) M = fmaxf(M, __ldg(&rowstat[(int64_t)g * N + n].x));
     float S = 0.f;
-    for (int g = 0; g < groups; ++g) {
-      const float2 e = rowstat[(int64_t)g * N + n];
+    g = 0;
+    for (; g + 8 <= groups; g += 8) {
+      float2 e[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) e[i] = __ldg(&rowstat[(int64_t)(g + i) * N + n]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) S += e[i].y * exp2f(e[i].x - M);
+    }
+    for (; g < groups; ++g) {
+      const float2 e = __ldg(&rowstat[(int64_t)g * N + n]);
       S += e.y * exp2f(e.x - M);
     }
     const float l2 = M + log2f(S);
@@ -742,6 +760,11 @@ __global__ void tc_lse_combine_kernel(const float2* rowstat, int groups, int64_t
     ll_part[blockIdx.x] = s;
   }
 }
+
+// blocks of the per-row combine kernels: four per SM (their log-likelihood
+// partials, one per block, fit the kTcMaxClusters * kMaxClusterSph slots)
+constexpr int kCombineBlocks = 4 * 148;
+static_assert(kCombineBlocks <= kTcMaxClusters * kMaxClusterSph, "log-likelihood partial slots");
 
 // Grouped inference: each row's label from the per-group (max logit, first
 // component), groups in increasing component order, strictly larger wins.
@@ -977,7 +1000,7 @@ static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
   if (L.infer == 3 && L.lse == nullptr) return set_error(GMMXX_ERR_WORKSPACE, "per-row log-sum-exp buffer missing");
   if (int rc = launch_tc_pack(GMMXX_SPHERICAL, DB, L, st)) return rc;
   auto csz = [&](int g) { return std::min(gc, L.nchunks - g * gc); };
-  const int nb = std::min<int>(kMaxClusters, 148);
+  const int nb = kCombineBlocks;
   int ncl = 0;
   if (L.infer == 2) {  // labels
     if (groups == 1) return launch_mode<GMMXX_SPHERICAL, DB, kModeArgmax>(L, 0, csz(0), nullptr, nullptr, &ncl, st, 3);
@@ -1014,7 +1037,7 @@ static int launch_sph_infer(const TcLaunch& L, cudaStream_t st) {
 }
 
 int launch_infer_combine(const TcLaunch& L, int groups, int infer, cudaStream_t st) {
-  const int nb = std::min<int>(kMaxClusters, 148);
+  const int nb = kCombineBlocks;
   if (infer == 2) {
     tc_argmax_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.out_i);
     return check_launch("tc_argmax_combine_kernel");
@@ -1025,7 +1048,7 @@ int launch_infer_combine(const TcLaunch& L, int groups, int infer, cudaStream_t 
 }
 
 int launch_rowstat_combine(const TcLaunch& L, int groups, cudaStream_t st) {
-  const int nb = std::min<int>(kMaxClusters, 148);
+  const int nb = kCombineBlocks;
   tc_lse_combine_kernel<<<nb, 256, 0, st>>>(L.rowstat, groups, L.N, L.lse, L.part_ll);
   if (int rc = check_launch("tc_lse_combine_kernel")) return rc;
   tc_ll_sum_kernel<<<1, 32, 0, st>>>(L.part_ll, nb, L.ll);
