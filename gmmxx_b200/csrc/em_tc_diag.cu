@@ -52,9 +52,24 @@
 // (x^T P x - 2 x.P mu + mu^T P mu).clamp_min(0): the unclamped value is a
 // positive definite quadratic form and differs from zero by rounding only.
 //
+// Spherical covariance, bf16 X, D = 128 (kSph): the E-step operand is x
+// (two 64-feature boxes), |x|^2 comes from the prep warps in fp32, the
+// logit is c2 - h_k max(S + |x|^2 + |mu_k|^2, 0), and the M-step stage is
+// [x[0:64] | x[64:128] | aux] with |x|^2 in three bf16 terms next to the
+// constant 1 in the aux group.  K <= 512 runs in one pass (kModeEm).  For
+// K > 1024 the first pass (kModeRowStat) writes each row's (max, scaled sum)
+// over a group of 2 chunks: it has no M-step, so X gets a three-slot staging
+// ring in the M-step stage and R buffer and the E-step reads X from its slot
+// (A from shared memory), S has two slots in the M-step accumulator columns,
+// and the softmax is pipelined over three tiles (part table in the R
+// buffer).  The second pass runs in em_tc_sph_ext.cu (or, for comparison,
+// here as kModeExtLse).  Inference: labels, log-sum-exp and responsibilities
+// in one pass for K <= 512, else per group with the combine kernels and, for
+// the responsibilities, kModeProbaExt from the combined log-sum-exp.
+//
 // Reference semantics: gmmxx/torch_fallback.py:2508-2651 (diag E/M chunk
 // loop), expanded-distance logits 357-397; tied 435-465 (logits), 2912-3139
-// (matrix E/M loop).
+// (matrix E/M loop); spherical 2097-2291 (E/M chunk loop), logits 337-354.
 #include "gmm_common.cuh"
 #include "tc_ptx.cuh"
 #include "tc_api.cuh"
