@@ -26,6 +26,8 @@
 #include "rows_api.cuh"
 
 #include <float.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 
@@ -532,6 +534,202 @@ __global__ void __launch_bounds__(kThreads) em_small_kernel(RowArgs a) {
   }
 }
 
+// Full covariance, K <= 32: the one-pass kernel on a 128-row x 32-component
+// tile.  The 64 x 64 tile above pads K = 32 to 64 components, so half of its
+// E-step and M-step products are spent on padding; here each one counts.
+// E-step thread: rows 4 ty.., components 4 tx.. (8 x 32 threads), the same
+// feature order as tile_dots; the row's log-sum-exp over its 8 threads,
+// merged in the order the 64-wide tile merges its non-empty lanes.  M-step
+// thread: components 4 kg.., features 4 fg.. of a 64-feature chunk, over one
+// half (rh) of the tile's rows; the halves are added (half 0 + half 1) at
+// the flush, so the statistics are deterministic.
+constexpr int kNR = 128;  // rows per tile
+constexpr int kNK = 32;   // components
+
+__host__ __device__ inline int64_t smem_bytes_narrow(int D) {
+  return (int64_t)(kFC * kNR + kFC * kNK + kNR * kNK + kNR * 64 + kNR * (D + 1)) * 4 +
+         round_up((int64_t)D * (D + 1) / 2 * 2, 16);
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(kThreads) em_small_narrow_kernel(RowArgs a) {
+  static_assert(kThreads == 256 && NCH <= 3, "thread maps and the flush buffer");
+  extern __shared__ __align__(16) char smem_raw[];
+  const int D = a.D, xst = D + 1, FE = a.FE;
+  float* phic = reinterpret_cast<float*>(smem_raw);  // [kFC][kNR]
+  float* wc = phic + kFC * kNR;                        // [kFC][kNK]
+  float* R = wc + kFC * kNK;                           // [kNR][kNK]
+  float* phim = R + kNR * kNK;                         // [kNR][64]
+  float* xs = phim + kNR * 64;                         // [kNR][D + 1]
+  uint16_t* pairs = reinterpret_cast<uint16_t*>(xs + kNR * xst);
+  const int b = blockIdx.z;
+  const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;                                // E-step 8 x 32
+  const int kg = threadIdx.x & 7, fg = (threadIdx.x >> 3) & 15, rh = threadIdx.x >> 7;  // M-step 8 x 16 x 2
+  for (int i = threadIdx.x; i < D; i += kThreads) {
+    int p = i * D - i * (i - 1) / 2;
+    for (int j = i; j < D; ++j) pairs[p++] = (uint16_t)(i | (j << 8));
+  }
+  float macc[NCH][4][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) macc[c][i][j] = 0.f;
+  float nk[4] = {0.f, 0.f, 0.f, 0.f};
+  double ll = 0.0;
+  const float* wtb = a.wt + (int64_t)b * FE * a.Kp;
+
+  const int64_t rstart = (int64_t)blockIdx.x * a.rows_per_cta;
+  const int64_t rend = min(rstart + a.rows_per_cta, a.N);
+  float acc[4][4];
+  for (int64_t row0 = rstart; row0 < rend; row0 += kNR) {
+    __syncthreads();  // the previous tile's reads of xs, R and phim are done
+    {
+      const int64_t base = ((int64_t)b * a.N + row0) * D;
+      const int64_t nrows = min((int64_t)kNR, a.N - row0);
+      for (int e = threadIdx.x; e < kNR * D; e += kThreads) {
+        const int r = e / D, d = e - r * D;
+        xs[r * xst + d] = (r < nrows) ? load_x(a.x, base + e, a.dt) : 0.f;
+      }
+    }
+    // E-step: the tile's features against the 32 components, kFC at a time
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int f0 = 0; f0 < FE; f0 += kFC) {
+      __syncthreads();
+      for (int e = threadIdx.x; e < kFC * kNR; e += kThreads) {
+        const int r = e & (kNR - 1), f = e / kNR;
+        phic[e] = (f0 + f < FE) ? feat_e<GMMXX_FULL>(xs + r * xst, f0 + f, D, pairs) : 0.f;
+      }
+      for (int e = threadIdx.x; e < kFC * kNK; e += kThreads) {
+        const int k = e & (kNK - 1), f = e / kNK;
+        wc[e] = (f0 + f < FE) ? __ldg(wtb + (int64_t)(f0 + f) * a.Kp + k) : 0.f;
+      }
+      __syncthreads();
+#pragma unroll 8
+      for (int f = 0; f < kFC; ++f) {
+        const float4 xv = *reinterpret_cast<const float4*>(phic + f * kNR + ty * 4);
+        const float4 wv = *reinterpret_cast<const float4*>(wc + f * kNK + tx * 4);
+        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+        const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
+      }
+    }
+    // logits (full covariance: no per-row term), invalid components -> -inf
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = tx * 4 + j;
+      if (k < a.K) {
+        const CompConst c = a.cc[(int64_t)b * a.K + k];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float dist = acc[i][j] + c.mpm;
+          dist = fmaxf(dist, 0.f);
+          acc[i][j] = c.lw - 0.5f * (c.s * dist + c.ln);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i][j] = -INFINITY;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float m = fmaxf(fmaxf(acc[i][0], acc[i][1]), fmaxf(acc[i][2], acc[i][3]));
+      float sm = 0.f;
+      if (m != -INFINITY) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sm += expf(acc[i][j] - m);
+      }
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, sm, o);
+        lse_merge(m, sm, m2, s2);
+      }
+      float run_m = -INFINITY, run_s = 0.f;
+      lse_merge(run_m, run_s, m, sm);
+      const float l = run_m + logf(run_s);
+      const int64_t row = row0 + ty * 4 + i;
+      const bool ok = row < rend;
+      if (ok && tx == 0) ll += (double)l;
+      float r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = ok ? expf(acc[i][j] - l) : 0.f;  // -inf -> 0
+      *reinterpret_cast<float4*>(R + (ty * 4 + i) * kNK + tx * 4) = make_float4(r[0], r[1], r[2], r[3]);
+    }
+    // M-step: sum over this half's rows of r_nk psi(x_n), 64 features at a time
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      __syncthreads();  // R written; the previous chunk's reads of phim are done
+      for (int e = threadIdx.x; e < kNR * 64; e += kThreads) {
+        const int r = e >> 6, f = e & 63;
+        phim[e] = feat_m<GMMXX_FULL>(xs + r * xst, 0.f, 1 + c * 64 + f, D, a.FM, pairs);
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int rr = 0; rr < kNR / 2; ++rr) {
+        const int r = rh * (kNR / 2) + rr;
+        const float4 rv = *reinterpret_cast<const float4*>(R + r * kNK + kg * 4);
+        const float4 pv = *reinterpret_cast<const float4*>(phim + r * 64 + fg * 4);
+        const float ra[4] = {rv.x, rv.y, rv.z, rv.w};
+        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+        if (c == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) nk[i] += ra[i];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) macc[c][i][j] = fmaf(ra[i], pa[j], macc[c][i][j]);
+      }
+    }
+  }
+  // flush: half 1 hands its sums to half 0 through shared memory (phim, idle
+  // now), half 0 adds them and writes this CTA's partial slot
+  constexpr int kW = NCH * 16 + 4;
+  static_assert(128 * kW <= kNR * 64, "flush buffer inside phim");
+  __syncthreads();
+  float* red = phim + (threadIdx.x & 127) * kW;
+  if (rh == 1) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) red[c * 16 + i * 4 + j] = macc[c][i][j];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[NCH * 16 + i] = nk[i];
+  }
+  __syncthreads();
+  if (rh == 0) {
+    float* st = a.part + ((int64_t)b * a.part_blocks + blockIdx.x) * a.Kp * a.FM;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = kg * 4 + i;
+      if (k >= a.K) continue;
+      if (fg == 0) st[(int64_t)k * a.FM] = nk[i] + red[NCH * 16 + i];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int f = 1 + c * 64 + fg * 4 + j;
+          if (f < a.FM) st[(int64_t)k * a.FM + f] = macc[c][i][j] + red[c * 16 + i * 4 + j];
+        }
+    }
+  }
+  if (a.ll_part != nullptr) {
+    __shared__ double red_ll[kThreads / 32];
+    const double tot = block_sum<double>(ll, red_ll);
+    if (threadIdx.x == 0) a.ll_part[(int64_t)b * gridDim.x + blockIdx.x] = tot;
+  }
+}
+
 // Approximate top-k EM (torch_fallback.py:667-767 _topk_logits_for_chunk /
 // _accumulate_topk_stats; _cuda.py:783-889): a row's responsibilities are
 // the softmax of its top_k logits, zero for every other component.
@@ -890,9 +1088,43 @@ static int launch_small_c(const RowArgs& a, int B, cudaStream_t st) {
   return set_error(GMMXX_ERR_UNSUPPORTED, "statistics width %d exceeds the SIMT window", a.FM);
 }
 
+template <int NCH>
+static int launch_small_narrow_t(RowArgs a, int B, cudaStream_t st) {
+  const int64_t sm = smem_bytes_narrow(a.D);
+  auto k = em_small_narrow_kernel<NCH>;
+  if (int rc = prep_smem(k, sm)) return rc;
+  const int64_t tiles = ceil_div(a.N, kNR);
+  const int64_t nblk_max = mstep_blocks(B, a.N, a.Kp);
+  a.rows_per_cta = ceil_div(tiles, wave_blocks(k, sm, 1, B, nblk_max, tiles)) * kNR;
+  const int64_t nblk = ceil_div(a.N, a.rows_per_cta);
+  a.part_blocks = nblk_max;
+  dim3 grid((unsigned)nblk, 1u, (unsigned)B);
+  k<<<grid, kThreads, sm, st>>>(a);
+  if (int rc = check_launch("em_small_narrow_kernel")) return rc;
+  const int64_t n = (int64_t)B * a.K * a.FM;
+  stats_reduce_kernel<<<(unsigned)ceil_div(std::max<int64_t>(n, 1), 256), 256, 0, st>>>(
+      a.part, nblk, nblk_max, a.Kp, a.K, a.FM, B, a.stats, a.ll_part, nblk, a.ll);
+  return check_launch("stats_reduce_kernel");
+}
+
+// GMMXX_B200_SMALL_TILE=wide keeps full covariance with K <= 32 on the 64 x 64
+// tile (the A/B switch of the two tilings)
+static bool narrow_enabled() {
+  const char* e = getenv("GMMXX_B200_SMALL_TILE");
+  return !(e != nullptr && strcmp(e, "wide") == 0);
+}
+
 int launch_em_small(int cov, const RowArgs& a, int B, cudaStream_t st) {
   if (a.N == 0) return GMMXX_OK;
   if (a.Kp != kBK) return set_error(GMMXX_ERR_UNSUPPORTED, "one-pass statistics need K <= %d", kBK);
+  if (cov == GMMXX_FULL && a.K <= kNK && narrow_enabled()) {
+    switch ((int)ceil_div(a.FM - 1, 64)) {
+      case 1: return launch_small_narrow_t<1>(a, B, st);
+      case 2: return launch_small_narrow_t<2>(a, B, st);
+      case 3: return launch_small_narrow_t<3>(a, B, st);
+      default: break;  // wider statistics: the 64 x 64 tile
+    }
+  }
   switch (cov) {
     case GMMXX_SPHERICAL: return launch_small_c<GMMXX_SPHERICAL>(a, B, st);
     case GMMXX_DIAG: return launch_small_c<GMMXX_DIAG>(a, B, st);
