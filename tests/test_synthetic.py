@@ -71,3 +71,23 @@ def test_initial_parameters_are_shared_and_seeded():
     assert np.array_equal(m1, m2) and np.array_equal(c1, c2) and np.array_equal(w1, w2)
     assert c1.shape == (1, 512, 64) and (c1 == 1).all() and np.allclose(w1, 1 / 512)
     assert abs((m1 - mix.means).std() - 0.5) < 0.01  # the generating means perturbed by N(0, 0.5^2)
+
+
+def test_bench_launch_count_matches_the_kernel_sequence(monkeypatch):
+    """bench.py's gpu_launches claim per EM iteration: prep (2, +2 Cholesky
+    kernels for tied / full), the statistics kernels, finalize (2).  Config
+    4 (spherical D = 128, K = 8192) on the diag-kernel layout: pack, 32
+    row-statistics launches (groups of 2 chunks), combine, log-likelihood
+    sum, 16 x (second pass + reduce); on em_tc_kernel (the legacy layout)
+    the first pass has 16 groups of 4 chunks."""
+    import bench
+
+    monkeypatch.delenv("GMMXX_B200_SPH_KERNEL", raising=False)
+    cfg = synthetic.CONFIGS
+    assert bench.launches_per_iteration(cfg[4], True) == 2 + (1 + 32 + 2 + 2 * 16) + 2
+    assert bench.launches_per_iteration(cfg[1], True) == 2 + 3 + 2
+    assert bench.launches_per_iteration(cfg[2], True) == 4 + 3 + 2
+    assert bench.launches_per_iteration(cfg[3], False) == 4 + 2 + 2
+    assert bench.launches_per_iteration(cfg[0], False) == 2 + 2 + 2
+    monkeypatch.setenv("GMMXX_B200_SPH_KERNEL", "legacy")
+    assert bench.launches_per_iteration(cfg[4], True) == 2 + (1 + 16 + 2 + 2 * 16) + 2
